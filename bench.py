@@ -1,0 +1,413 @@
+#!/usr/bin/env python
+"""Benchmark of the paged-KV decode attention path on B200.
+
+Workload (one "step" = one decode token for every row through all 28 layers
+of the attention path): 256 rows with contexts U[2048, 8192] (seeded), a
+bf16 KV pool of ~150 GB whose blocks are handed out from a seeded random
+permutation, and per layer the fused RoPE + K/V append followed by paged
+decode attention over the blocks in place.  Q/K/V are synthetic N(0,1).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+value  : algorithmic HBM bytes of the path per step (K+V of every visible
+         token, q/k/v in, q/out, block tables) / device time, GB/s, summed
+         over ranks (replicas: each GPU owns its own pool and rows).
+e2e    : the same bytes over the time of the public API driven from pinned
+         host buffers (q/k/v H2D and O D2H every layer inside the timed region).
+--impl reference : the reference's CPU path (fp32 KVCache gather + SDPA,
+         restated in oracle/) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+PKG = REPO / "my-inference-engine_b200"
+for _p in (str(REPO), str(PKG)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+L, HQ, HKV, D = 28, 12, 2, 128
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seqs", type=int, default=256)
+    ap.add_argument("--ctx-min", type=int, default=2048)
+    ap.add_argument("--ctx-max", type=int, default=8192)
+    ap.add_argument("--pool-gb", type=float, default=150.0)
+    ap.add_argument("--layers", type=int, default=L)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seqs", type=int, default=4, help="rows in the CPU baseline sample")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def context_lengths(args):
+    g = torch.Generator().manual_seed(args.seed)
+    return torch.randint(args.ctx_min, args.ctx_max + 1, (args.seqs,), generator=g).tolist()
+
+
+def decode_bytes(lens):
+    """Algorithmic bytes of one paged decode launch (one layer)."""
+    B = len(lens)
+    kv = sum(lens) * HKV * D * 2 * 2
+    qo = 2 * B * HQ * D * 2
+    tables = sum(math.ceil(n / 16) for n in lens) * 4 + 2 * B * 4
+    return kv + qo + tables
+
+
+def append_bytes(B):
+    """Algorithmic bytes of one fused RoPE + append launch (one layer, T=1)."""
+    reads = B * (HQ + 2 * HKV) * D * 2 + 2 * B * D * 2 + 3 * B * 4 + B * 4
+    writes = B * HQ * D * 2 + B * 2 * HKV * D * 2
+    return reads + writes
+
+
+def measured_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except Exception:
+            pass
+    return {"hbm_gbs": FALLBACK_HBM_GBS}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.lines = []
+        self.proc = None
+        try:
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", uuid, "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx.append(float(f[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- our arm
+class DecodeWorkload:
+    def __init__(self, args, device):
+        import model
+        from kv_cache import KVCache
+
+        self.device = device
+        self.lens = context_lengths(args)
+        self.layers = args.layers
+        B = len(self.lens)
+        bytes_per_block = L * 2 * 16 * HKV * D * 2
+        num_blocks = int(args.pool_gb * 1e9 // bytes_per_block)
+        need = sum(math.ceil(n / 16) for n in self.lens)
+        assert num_blocks >= need, f"pool of {num_blocks} blocks cannot hold {need}"
+        pitch = math.ceil((args.ctx_max + 1) / 16)
+        self.cache = KVCache(num_blocks, 16, device, torch.bfloat16, max_seqs=B,
+                             max_blocks_per_seq=pitch)
+        g = torch.Generator().manual_seed(args.seed + 1)
+        self.cache._free_blocks = torch.randperm(num_blocks, generator=g).tolist()
+        self.seqs = [self.cache.alloc() for _ in self.lens]
+        for s, n in zip(self.seqs, self.lens):
+            self.cache.ensure_capacity(s, n)
+            self.cache._lengths[s] = n - 1  # history in the pool; this step appends token n-1
+        gd = torch.Generator(device=device).manual_seed(args.seed + 2)
+        for l in range(L):  # synthetic history, layer by layer to bound temporaries
+            self.cache.buf[l].normal_(generator=gd)
+        _, self.step, _ = self.cache.prepare(self.seqs, 1)
+        self.cos, self.sin = model.rope_table(pitch * 16, torch.bfloat16, device)
+        self.q = torch.randn(self.layers, B, HQ, 1, D, device=device, generator=gd).to(torch.bfloat16)
+        self.k = torch.randn(self.layers, B, HKV, 1, D, device=device, generator=gd).to(torch.bfloat16)
+        self.v = torch.randn(self.layers, B, HKV, 1, D, device=device, generator=gd).to(torch.bfloat16)
+        self.q_rot = torch.empty_like(self.q)
+        self.out = torch.empty(self.layers, B, HQ, 1, D, device=device, dtype=torch.bfloat16)
+        self.handles = [self.cache.read(l, self.step) for l in range(self.layers)]
+        self.bytes_decode = decode_bytes(self.lens)
+        self.bytes_append = append_bytes(B)
+        torch.cuda.synchronize()
+
+    def run_layer(self, l, ev=None):
+        from kernels.fa2 import flash_attention
+
+        self.cache.append(l, self.step, self.q[l], self.k[l], self.v[l], self.cos, self.sin,
+                          self.q_rot[l])
+        kh, vh = self.handles[l]
+        if ev is not None:
+            ev[0].record()
+        flash_attention(self.q_rot[l], kh, vh, False, self.step.kv_lens, out=self.out[l])
+        if ev is not None:
+            ev[1].record()
+
+    def run_step(self, evs=None):
+        for l in range(self.layers):
+            self.run_layer(l, evs[l] if evs is not None else None)
+
+    def step_bytes(self):
+        return self.layers * (self.bytes_decode + self.bytes_append)
+
+
+def e2e_run(w: DecodeWorkload, steps, warmup):
+    """Public API from pinned host buffers: per layer H2D q/k/v, append +
+    attention, D2H O, all inside the timed region."""
+    from kernels.fa2 import flash_attention
+
+    B = len(w.lens)
+    hq = torch.empty(B, HQ, 1, D, dtype=torch.bfloat16).pin_memory()
+    hk = torch.empty(B, HKV, 1, D, dtype=torch.bfloat16).pin_memory()
+    hv = torch.empty(B, HKV, 1, D, dtype=torch.bfloat16).pin_memory()
+    hq.copy_(w.q[0].cpu())
+    hk.copy_(w.k[0].cpu())
+    hv.copy_(w.v[0].cpu())
+    hout = [torch.empty(B, HQ, 1, D, dtype=torch.bfloat16).pin_memory() for _ in range(w.layers)]
+    dq, dk, dv = (torch.empty(t.shape, dtype=t.dtype, device=w.device) for t in (hq, hk, hv))
+    qr = torch.empty_like(dq)
+    do = torch.empty_like(dq)
+
+    def one():
+        for l in range(w.layers):
+            dq.copy_(hq, non_blocking=True)
+            dk.copy_(hk, non_blocking=True)
+            dv.copy_(hv, non_blocking=True)
+            w.cache.append(l, w.step, dq, dk, dv, w.cos, w.sin, qr)
+            kh, vh = w.handles[l]
+            flash_attention(qr, kh, vh, False, w.step.kv_lens, out=do)
+            hout[l].copy_(do, non_blocking=True)
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        one()
+    e.record()
+    e.synchronize()
+    ms = s.elapsed_time(e) / steps
+    h2d = w.layers * (hq.numel() + hk.numel() + hv.numel()) * 2
+    d2h = w.layers * hout[0].numel() * 2
+    return ms, h2d, d2h
+
+
+# ---------------------------------------------------------------- CPU path
+class CpuPath:
+    """Reference CPU path (oracle restatement) on a bounded sample: the first
+    --cpu-seqs rows of the same length distribution, all layers, fp32."""
+
+    def __init__(self, args):
+        from oracle.reference_path import CpuDecodePath
+
+        self.lens = context_lengths(args)[: args.cpu_seqs]
+        self.layers = args.layers
+        self.path = CpuDecodePath(self.lens, args.layers, seed=args.seed)
+        self.bytes = args.layers * (decode_bytes(self.lens) + append_bytes(len(self.lens)))
+
+    def sample(self):
+        return (f"{len(self.lens)} rows (ctx {self.lens}) x {self.layers} layers per step, "
+                f"fp32 torch CPU")
+
+    def time_steps(self, n=None, seconds=None):
+        """Run steps until n steps or `seconds` elapse; return seconds per step."""
+        k, t0 = 0, time.perf_counter()
+        while True:
+            self.path.step()
+            k += 1
+            el = time.perf_counter() - t0
+            if (n is not None and k >= n) or (seconds is not None and el >= seconds):
+                return el / k, k
+
+
+def cpu_info():
+    name = ""
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                name = ln.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return name
+
+
+# ---------------------------------------------------------------- main
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    metric = "paged decode-attn HBM GB/s"
+    config = {"workload": "config3: 256 rows, ctx U[2048,8192], ~150 GB bf16 pool, 28 layers "
+                          "of RoPE+append + paged decode per step",
+              "seqs": args.seqs, "ctx_range": [args.ctx_min, args.ctx_max],
+              "pool_gb": args.pool_gb, "layers": args.layers, "block_size": 16,
+              "heads": [HQ, HKV, D], "l2": "inputs larger than L2 (KV read per step >> 126 MB)",
+              "parallelism": f"replicas x{args.gpus} (request-sharded, no collective)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        torch.set_num_threads(os.cpu_count() or 1)
+        threads = torch.get_num_threads()
+        # each timed step is a bounded sample: one pass of the CPU path over
+        # --cpu-seqs rows and every layer
+        cp = CpuPath(args)
+        cp.time_steps(n=args.warmup)
+        per_step, _ = cp.time_steps(n=args.steps)
+        val = cp.bytes / per_step / 1e9
+        sample = cp.sample()
+        line = {"metric": metric, "value": round(val, 3), "unit": "GB/s", "impl": "reference",
+                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(per_step * 1e3, 3), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": config,
+                "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": threads,
+                                 "kind": "port", "sample": sample, "cpu": cpu_info()},
+                "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    if world > 1:
+        torch.cuda.set_device(local)
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    dev = torch.device("cuda", torch.cuda.current_device())
+
+    w = DecodeWorkload(args, dev)
+    for _ in range(args.warmup):
+        w.run_step()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for _ in range(w.layers)] for _ in range(args.steps)]
+    clocks = ClockSampler(dev)
+    barrier()
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for i in range(args.steps):
+        w.run_step(evs[i])
+    t_end.record()
+    barrier()
+    clk = clocks.stop()
+    ms = t_start.elapsed_time(t_end) / args.steps
+    kern_ms = statistics.mean(a.elapsed_time(b) for st in evs for a, b in st)
+    ms_all = torch.tensor([ms], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(ms_all, op=torch.distributed.ReduceOp.MAX)
+    ms_max = float(ms_all.item())
+    total_bytes = w.step_bytes() * world
+    value = total_bytes / (ms_max * 1e-3) / 1e9
+
+    e2e = None
+    if not args.no_e2e:
+        e_ms, h2d, d2h = e2e_run(w, max(2, args.steps // 2), 1)
+        e_all = torch.tensor([e_ms], device=dev)
+        if world > 1:
+            torch.distributed.all_reduce(e_all, op=torch.distributed.ReduceOp.MAX)
+        e2e = {"value": round(total_bytes / (float(e_all.item()) * 1e-3) / 1e9, 2), "unit": "GB/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "ms_per_step": round(float(e_all.item()), 3)}
+
+    peaks, src = measured_peaks()
+    peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
+    achieved = w.bytes_decode / (kern_ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_source": src,
+                "frac_of_nominal_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
+                "kernel": "paged_decode_kernel", "bytes_per_launch": w.bytes_decode,
+                "avg_launch_ms": round(kern_ms, 4),
+                "traffic": None}
+    prof = REPO / "profiles" / "decode_traffic.json"
+    if prof.exists():
+        try:
+            roofline["traffic"] = json.loads(prof.read_text()).get("traffic_bytes_per_launch")
+        except Exception:
+            pass
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        torch.set_num_threads(os.cpu_count() or 1)
+        cp = CpuPath(args)
+        cp.time_steps(n=1)
+        per_step, n = cp.time_steps(seconds=12.0)
+        cpu = {"value": round(cp.bytes / per_step / 1e9, 3), "unit": "GB/s",
+               "cores": torch.get_num_threads(), "kind": "port",
+               "sample": cp.sample() + f", {n} steps timed", "cpu": cpu_info()}
+
+    if rank == 0:
+        line = {"metric": metric, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic", "config": config, "roofline": roofline,
+                "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+                "gpu_launches": args.steps * w.layers * 2 * 1,
+                "kv_bytes_per_step": w.step_bytes()}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

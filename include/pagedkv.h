@@ -1,0 +1,167 @@
+/*
+ * pagedkv.h -- C ABI of the B200 (sm_100a) paged-KV attention path.
+ *
+ * The library libpagedkv.so replaces the GPU half of two Python modules of the
+ * reference engine (shubhav1/my-inference-engine):
+ *
+ *   kv_cache.py   KVCache.write()   (kv_cache.py:108-115, index_copy_ scatter)
+ *                 KVCache.read()    (kv_cache.py:117-121, dense gather copy)
+ *                 apply_rope()      (model.py:58-65, five bf16 elementwise ops)
+ *   kernels/fa2.py fa2_forward + FlashAttention2Function.forward
+ *                                   (kernels/fa2.py:23-214)
+ *
+ * Conventions shared by every entry point
+ * ---------------------------------------
+ *  - All tensor arguments are raw device pointers; strides are in ELEMENTS.
+ *    The innermost (head_dim) dimension is always contiguous.
+ *  - Element type is bf16 for activations and the pool, int32 for tables and
+ *    lengths, fp32 for scratch.  head_dim must be 128 and block_size 16
+ *    (the Qwen2.5-1.5B path).
+ *  - The KV pool keeps the reference's layout (kv_cache.py:20-22):
+ *      buf[layer][k=0|v=1][slot][kv_head][head_dim],  slot = block*16 + pos%16
+ *    Entry points take the base of one layer's K plane (buf[layer,0]) and V
+ *    plane (buf[layer,1]) plus num_slots = num_blocks*16.
+ *  - Block tables are device-resident int32 [rows][table_pitch]; batch row b
+ *    uses table row seq_rows[b] (seq_rows may be NULL: row b).  Logical
+ *    position p of row b lives at slot table[row][p/16]*16 + p%16.
+ *  - Every call is asynchronous on `stream` and returns a pkv_status.  A
+ *    nonzero status means nothing was launched.  Memory is owned by the
+ *    caller; the library never allocates or frees device memory.
+ *  - err_flag (nullable, device int32) receives PKV_DEVERR_* bits when a
+ *    kernel meets an out-of-range block id / position: the bad access is
+ *    skipped (block 0 is read instead) and the flag is OR-ed, never a fault.
+ */
+#ifndef PAGEDKV_H_
+#define PAGEDKV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  PKV_OK = 0,
+  PKV_ERR_INVALID = 1,      /* bad shape, null pointer, bad count        */
+  PKV_ERR_UNSUPPORTED = 2,  /* head_dim != 128, group too large, ...     */
+  PKV_ERR_ALIGN = 3,        /* pointer / stride not 16-byte aligned      */
+  PKV_ERR_DRIVER = 4,       /* driver entry point / tensor map encoding  */
+  PKV_ERR_LAUNCH = 5,       /* kernel launch failed                      */
+  PKV_ERR_WORKSPACE = 6     /* workspace too small                       */
+} pkv_status;
+
+/* Bits a kernel ORs into *err_flag. */
+#define PKV_DEVERR_BLOCK_ID 1  /* table entry outside [0, num_blocks)      */
+#define PKV_DEVERR_POSITION 2  /* position beyond table pitch / rope rows  */
+#define PKV_DEVERR_TIMEOUT 4   /* a bounded wait on an mbarrier ran out    */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int pkv_version(void);
+
+/* Static text for a status code. */
+const char* pkv_status_string(int status);
+
+/* Detail of the most recent failing call on this host thread ("" if none). */
+const char* pkv_last_error(void);
+
+/*
+ * Fused RoPE + K/V append for one layer and one forward step.
+ *
+ * Replaces apply_rope (model.py:62-65, with cos/sin from rope_cos_sin
+ * model.py:151-155) followed by KVCache.write (kv_cache.py:108-115).
+ * For batch row b and step token t the position is pos = starts[b] + t:
+ *   - if rope_cos/rope_sin are non-NULL, q and k are rotated with row `pos`
+ *     of the bf16 tables [rope_rows][128], rounding to bf16 after every op
+ *     exactly like the reference: bf16(bf16(x*cos) + bf16(rotate_half(x)*sin));
+ *   - roped q goes to q_out [B][Hq][T][128] (strides q_out_s*), may be NULL;
+ *   - roped k and plain v go to the pool slot of (row b, pos).
+ * With rope_cos == NULL the call is exactly KVCache.write (k/v copied as-is,
+ * q ignored).  q, k, v are [B][H][T][128] with strides (sb, sh, st).
+ */
+int pkv_append_rope(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
+                    const void* k, int64_t k_sb, int64_t k_sh, int64_t k_st,
+                    const void* v, int64_t v_sb, int64_t v_sh, int64_t v_st,
+                    const void* rope_cos, const void* rope_sin, int64_t rope_rows,
+                    void* q_out, int64_t qo_sb, int64_t qo_sh, int64_t qo_st,
+                    void* k_pool, void* v_pool, int64_t num_slots,
+                    const int32_t* block_tables, int64_t table_pitch,
+                    const int32_t* seq_rows, const int32_t* starts,
+                    int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                    int32_t seq_len_q, int32_t head_dim,
+                    int32_t* err_flag, void* stream);
+
+/*
+ * Bytes of fp32 scratch pkv_paged_decode needs for these sizes (split-K
+ * partials + per-(row, kv_head) counters).  0 when one pass suffices.
+ */
+size_t pkv_decode_workspace_size(int32_t batch, int32_t num_q_heads,
+                                 int32_t num_kv_heads, int32_t max_kv_len);
+
+/*
+ * Paged decode attention (one query token per row) reading K/V blocks in
+ * place through the block table: no dense gather copy.
+ *
+ * Replaces KVCache.read (kv_cache.py:117-121) + fa2_forward with T=1
+ * (kernels/fa2.py:23-162 as launched at :192-207; model.py:103).
+ * q  : [B][Hq][128] (strides q_sb, q_sh)      out: [B][Hq][128] (o_sb, o_sh)
+ * kv_lens[b] keys are visible to row b (is_causal is irrelevant at T=1,
+ * fa2.py:110-111).  max_kv_len >= max(kv_lens) sizes the grid; the host
+ * keeps it without a device read.  sm_scale is 1/sqrt(128) in the reference
+ * (fa2.py:173).  Rows with kv_len == 0 produce NaN, as 0/0 does in
+ * fa2.py:151.  workspace: >= pkv_decode_workspace_size() bytes, zeroed
+ * before first use; the kernel leaves its counters at zero on exit.
+ */
+int pkv_paged_decode(const void* q, int64_t q_sb, int64_t q_sh,
+                     const void* k_pool, const void* v_pool, int64_t num_slots,
+                     const int32_t* block_tables, int64_t table_pitch,
+                     const int32_t* seq_rows, const int32_t* kv_lens,
+                     int32_t max_kv_len, int32_t batch, int32_t num_q_heads,
+                     int32_t num_kv_heads, int32_t head_dim, float sm_scale,
+                     void* out, int64_t o_sb, int64_t o_sh,
+                     void* workspace, size_t workspace_bytes,
+                     int32_t* err_flag, void* stream);
+
+/*
+ * Paged (ragged) prefill / chunked-prefill attention, T >= 1 queries per row.
+ *
+ * Replaces KVCache.read + fa2_forward with is_causal = T > 1
+ * (kernels/fa2.py:23-162; model.py:185).  Query i of row b sits at key
+ * position i + kv_lens[b] - T (bottom-right causal, fa2.py:110-111); with
+ * causal == 0 every query sees all kv_lens[b] keys.
+ * q/out: [B][Hq][T][128] with strides (sb, sh, st).
+ */
+int pkv_paged_prefill(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
+                      const void* k_pool, const void* v_pool, int64_t num_slots,
+                      const int32_t* block_tables, int64_t table_pitch,
+                      const int32_t* seq_rows, const int32_t* kv_lens,
+                      int32_t max_kv_len, int32_t batch, int32_t seq_len_q,
+                      int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                      int32_t causal, float sm_scale,
+                      void* out, int64_t o_sb, int64_t o_sh, int64_t o_st,
+                      int32_t* err_flag, void* stream);
+
+/*
+ * Attention over dense, padded K/V -- the exact argument contract of
+ * FlashAttention2Function.forward (kernels/fa2.py:166-214): K/V are
+ * [B][Hkv][S][128] with strides (sb, sh, ss); each stride must be a
+ * multiple of 8 elements (16 bytes) and the bases 16-byte aligned.
+ * Rows are masked to kv_lens[b] (<= S) and bottom-right causal when
+ * causal != 0.  T == 1 uses the decode kernel (and the workspace, sized by
+ * pkv_decode_workspace_size with max_kv_len = S), T > 1 the prefill kernel.
+ */
+int pkv_dense_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
+                        const void* k, int64_t k_sb, int64_t k_sh, int64_t k_ss,
+                        const void* v, int64_t v_sb, int64_t v_sh, int64_t v_ss,
+                        const int32_t* kv_lens, int32_t batch, int32_t seq_len_q,
+                        int32_t seq_len_k, int32_t num_q_heads, int32_t num_kv_heads,
+                        int32_t head_dim, int32_t causal, float sm_scale,
+                        void* out, int64_t o_sb, int64_t o_sh, int64_t o_st,
+                        void* workspace, size_t workspace_bytes,
+                        int32_t* err_flag, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAGEDKV_H_ */

@@ -1,0 +1,123 @@
+// Fused RoPE + K/V append into the paged pool (sm_100a).
+//
+// Reference behaviour (bit-exact):
+//   model.py:151-155  cos/sin = cat(freqs, freqs).cos()/.sin() -> activation dtype
+//   model.py:58-65    rotate_half(x) = cat(-x2, x1);
+//                     x' = (x * cos) + (rotate_half(x) * sin)  -- each torch op on
+//                     bf16 tensors rounds its fp32 result to bf16 (RNE)
+//   kv_cache.py:108-115  index_copy_ of k, v into buf[layer, 0|1][slot]
+//   kv_cache.py:88-91    slot = table[p // 16] * 16 + p % 16
+// The cos/sin rows come from a table indexed by position, so the caller can
+// build it with exactly the reference's fp32 formula.
+//
+// One warp per (row, step token, head-of-{q, k, v}); lane l owns dims
+// {2l, 2l+1} and their rotation partners {64+2l, 64+2l+1}.
+#include "pkv_device.cuh"
+#include "pkv_kernels.h"
+
+namespace pkv {
+namespace {
+
+__device__ __forceinline__ float bf(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ __nv_bfloat16 rn(float x) { return __float2bfloat16_rn(x); }
+
+// bf16(bf16(x*c) + bf16(r*s)) with the multiplies and the add each rounded
+// separately (no FMA contraction), as three separate torch ops compute it.
+__device__ __forceinline__ __nv_bfloat16 rope1(__nv_bfloat16 x, __nv_bfloat16 c, __nv_bfloat16 r,
+                                               __nv_bfloat16 s) {
+  const __nv_bfloat16 xc = rn(__fmul_rn(bf(x), bf(c)));
+  const __nv_bfloat16 rs = rn(__fmul_rn(bf(r), bf(s)));
+  return rn(__fadd_rn(bf(xc), bf(rs)));
+}
+
+__global__ void __launch_bounds__(256) append_rope_kernel(const AppendLaunch a, int32_t num_blocks) {
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int64_t item = gid >> 5;
+  const int per_tok = (a.q_out ? a.num_q_heads : 0) + 2 * a.num_kv_heads;
+  const int64_t total = static_cast<int64_t>(a.batch) * a.seq_len_q * per_tok;
+  if (item >= total) return;
+  const int which = static_cast<int>(item % per_tok);
+  const int64_t bt = item / per_tok;
+  const int tt = static_cast<int>(bt % a.seq_len_q);
+  const int b = static_cast<int>(bt / a.seq_len_q);
+  const DevErr err{a.err};
+
+  const int pos = a.starts[b] + tt;
+  const bool rope = a.rope_cos != nullptr;
+  const int nq = a.q_out ? a.num_q_heads : 0;
+
+  // source row and destination row for this item
+  const __nv_bfloat16* src;
+  __nv_bfloat16* dst;
+  bool do_rope = rope;
+  if (which < nq) {
+    src = static_cast<const __nv_bfloat16*>(a.q) + b * a.q_sb + which * a.q_sh + tt * a.q_st;
+    dst = static_cast<__nv_bfloat16*>(a.q_out) + b * a.qo_sb + which * a.qo_sh + tt * a.qo_st;
+  } else {
+    const bool is_k = which < nq + a.num_kv_heads;
+    const int h = is_k ? which - nq : which - nq - a.num_kv_heads;
+    // destination slot through the block table
+    const int row = a.rows ? a.rows[b] : b;
+    const int64_t bi = pos >> 4;
+    if (pos < 0 || bi >= a.pitch) {
+      if (lane == 0) err.raise(PKV_DEVERR_POSITION);
+      return;
+    }
+    const int blk = a.tables[static_cast<int64_t>(row) * a.pitch + bi];
+    if (blk < 0 || blk >= num_blocks) {
+      if (lane == 0) err.raise(PKV_DEVERR_BLOCK_ID);
+      return;
+    }
+    const int64_t slot = static_cast<int64_t>(blk) * kBlockTokens + (pos & 15);
+    if (is_k) {
+      src = static_cast<const __nv_bfloat16*>(a.k) + b * a.k_sb + h * a.k_sh + tt * a.k_st;
+      dst = static_cast<__nv_bfloat16*>(a.k_pool) + (slot * a.num_kv_heads + h) * kHeadDim;
+    } else {
+      src = static_cast<const __nv_bfloat16*>(a.v) + b * a.v_sb + h * a.v_sh + tt * a.v_st;
+      dst = static_cast<__nv_bfloat16*>(a.v_pool) + (slot * a.num_kv_heads + h) * kHeadDim;
+      do_rope = false;
+    }
+  }
+
+  const int d = 2 * lane;
+  const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(src + d);
+  const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(src + 64 + d);
+  if (!do_rope) {
+    *reinterpret_cast<__nv_bfloat162*>(dst + d) = lo;
+    *reinterpret_cast<__nv_bfloat162*>(dst + 64 + d) = hi;
+    return;
+  }
+  if (pos < 0 || pos >= a.rope_rows) {
+    if (lane == 0) err.raise(PKV_DEVERR_POSITION);
+    return;
+  }
+  const __nv_bfloat16* cr = static_cast<const __nv_bfloat16*>(a.rope_cos) + static_cast<int64_t>(pos) * kHeadDim;
+  const __nv_bfloat16* sr = static_cast<const __nv_bfloat16*>(a.rope_sin) + static_cast<int64_t>(pos) * kHeadDim;
+  const __nv_bfloat162 clo = *reinterpret_cast<const __nv_bfloat162*>(cr + d);
+  const __nv_bfloat162 chi = *reinterpret_cast<const __nv_bfloat162*>(cr + 64 + d);
+  const __nv_bfloat162 slo = *reinterpret_cast<const __nv_bfloat162*>(sr + d);
+  const __nv_bfloat162 shi = *reinterpret_cast<const __nv_bfloat162*>(sr + 64 + d);
+  // first half: x*cos + (-x2)*sin ; second half: x*cos + x1*sin
+  __nv_bfloat162 olo, ohi;
+  olo.x = rope1(lo.x, clo.x, __hneg(hi.x), slo.x);
+  olo.y = rope1(lo.y, clo.y, __hneg(hi.y), slo.y);
+  ohi.x = rope1(hi.x, chi.x, lo.x, shi.x);
+  ohi.y = rope1(hi.y, chi.y, lo.y, shi.y);
+  *reinterpret_cast<__nv_bfloat162*>(dst + d) = olo;
+  *reinterpret_cast<__nv_bfloat162*>(dst + 64 + d) = ohi;
+}
+
+}  // namespace
+
+cudaError_t launch_append(const AppendLaunch& a, cudaStream_t stream) {
+  const int per_tok = (a.q_out ? a.num_q_heads : 0) + 2 * a.num_kv_heads;
+  const int64_t warps = static_cast<int64_t>(a.batch) * a.seq_len_q * per_tok;
+  if (warps == 0) return cudaSuccess;
+  const int64_t blocks = (warps * 32 + 255) / 256;
+  const int32_t num_blocks = static_cast<int32_t>(a.num_slots / kBlockTokens);
+  append_rope_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a, num_blocks);
+  return cudaGetLastError();
+}
+
+}  // namespace pkv

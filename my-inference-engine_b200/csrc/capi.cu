@@ -1,0 +1,308 @@
+// extern "C" entry points of libpagedkv.so (declared in include/pagedkv.h):
+// argument validation, TMA tensor-map encoding, dispatch to the kernels.
+// Nothing here allocates device memory.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <mutex>
+#include <string>
+
+#include "../../include/pagedkv.h"
+#include "pkv_kernels.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+int ok() {
+  g_last_error.clear();
+  return PKV_OK;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point, so the
+// library does not link libcuda directly (it loads on machines without one).
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                              const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                              const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  });
+  return fn;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Pool plane [num_slots][Hkv][128] bf16 -> 3-D map, box {64, 1, 16}, 128B swizzle.
+int encode_pool(CUtensorMap* m, const void* base, int64_t num_slots, int32_t hkv) {
+  EncodeFn fn = encode_fn();
+  if (!fn) return fail(PKV_ERR_DRIVER, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(hkv), static_cast<cuuint64_t>(num_slots)};
+  cuuint64_t strides[2] = {128 * 2, static_cast<cuuint64_t>(hkv) * 128 * 2};
+  cuuint32_t box[3] = {64, 1, 16};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PKV_ERR_DRIVER, "pool tensor map encode failed (%d)", (int)r);
+  return PKV_OK;
+}
+
+// Dense [B][Hkv][S][128] bf16 with element strides -> 4-D map, box {64,16,1,1}.
+int encode_dense(CUtensorMap* m, const void* base, int32_t B, int32_t hkv, int32_t S, int64_t sb,
+                 int64_t sh, int64_t ss) {
+  EncodeFn fn = encode_fn();
+  if (!fn) return fail(PKV_ERR_DRIVER, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(hkv),
+                        static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(ss) * 2, static_cast<cuuint64_t>(sh) * 2,
+                           static_cast<cuuint64_t>(sb) * 2};
+  cuuint32_t box[4] = {64, 16, 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides,
+                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PKV_ERR_DRIVER, "dense tensor map encode failed (%d)", (int)r);
+  return PKV_OK;
+}
+
+int check_heads(int32_t hq, int32_t hkv, int32_t d) {
+  if (d != 128) return fail(PKV_ERR_UNSUPPORTED, "head_dim must be 128, got %d", d);
+  if (hq <= 0 || hkv <= 0 || hq % hkv != 0)
+    return fail(PKV_ERR_INVALID, "num_q_heads (%d) must be a positive multiple of num_kv_heads (%d)",
+                hq, hkv);
+  return PKV_OK;
+}
+
+bool mult8(int64_t s) { return (s % 8) == 0; }
+
+int check_pool(const void* kp, const void* vp, int64_t num_slots, const int32_t* tables,
+               int64_t pitch) {
+  if (!kp || !vp || !tables) return fail(PKV_ERR_INVALID, "null pool or block-table pointer");
+  if (num_slots <= 0 || num_slots % 16 != 0)
+    return fail(PKV_ERR_INVALID, "num_slots (%lld) must be a positive multiple of 16",
+                (long long)num_slots);
+  if (num_slots / 16 > INT32_MAX || num_slots > (int64_t(1) << 31))
+    return fail(PKV_ERR_UNSUPPORTED, "pool too large for 32-bit slot coordinates");
+  if (pitch <= 0) return fail(PKV_ERR_INVALID, "table_pitch must be positive");
+  if (!aligned16(kp) || !aligned16(vp)) return fail(PKV_ERR_ALIGN, "pool planes not 16-byte aligned");
+  return PKV_OK;
+}
+
+int launch_status(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return fail(PKV_ERR_LAUNCH, "%s launch failed: %s", what, cudaGetErrorString(e));
+  return ok();
+}
+
+}  // namespace
+
+extern "C" {
+
+int pkv_version(void) { return 100; }
+
+const char* pkv_status_string(int status) {
+  switch (status) {
+    case PKV_OK: return "ok";
+    case PKV_ERR_INVALID: return "invalid argument";
+    case PKV_ERR_UNSUPPORTED: return "unsupported configuration";
+    case PKV_ERR_ALIGN: return "misaligned pointer or stride";
+    case PKV_ERR_DRIVER: return "CUDA driver / tensor map error";
+    case PKV_ERR_LAUNCH: return "kernel launch failed";
+    case PKV_ERR_WORKSPACE: return "workspace too small";
+    default: return "unknown status";
+  }
+}
+
+const char* pkv_last_error(void) { return g_last_error.c_str(); }
+
+int pkv_append_rope(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, const void* k,
+                    int64_t k_sb, int64_t k_sh, int64_t k_st, const void* v, int64_t v_sb,
+                    int64_t v_sh, int64_t v_st, const void* rope_cos, const void* rope_sin,
+                    int64_t rope_rows, void* q_out, int64_t qo_sb, int64_t qo_sh, int64_t qo_st,
+                    void* k_pool, void* v_pool, int64_t num_slots, const int32_t* block_tables,
+                    int64_t table_pitch, const int32_t* seq_rows, const int32_t* starts,
+                    int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t seq_len_q,
+                    int32_t head_dim, int32_t* err_flag, void* stream) {
+  int st = check_heads(num_q_heads, num_kv_heads, head_dim);
+  if (st) return st;
+  if ((st = check_pool(k_pool, v_pool, num_slots, block_tables, table_pitch))) return st;
+  if (batch < 0 || seq_len_q < 0) return fail(PKV_ERR_INVALID, "negative batch / seq_len_q");
+  if (!k || !v || !starts) return fail(PKV_ERR_INVALID, "null k, v or starts");
+  if ((rope_cos == nullptr) != (rope_sin == nullptr))
+    return fail(PKV_ERR_INVALID, "rope_cos and rope_sin must both be set or both NULL");
+  if (rope_cos && rope_rows <= 0) return fail(PKV_ERR_INVALID, "rope_rows must be positive");
+  if (q_out && (!q || !rope_cos)) return fail(PKV_ERR_INVALID, "q_out needs q and rope tables");
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 3u ||
+      (q && (reinterpret_cast<uintptr_t>(q) & 3u)) ||
+      (q_out && (reinterpret_cast<uintptr_t>(q_out) & 3u)) ||
+      (rope_cos && ((reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin)) & 3u)))
+    return fail(PKV_ERR_ALIGN, "append pointers must be 4-byte aligned");
+  if ((k_sb | k_sh | k_st | v_sb | v_sh | v_st) & 1 ||
+      (q_out && ((q_sb | q_sh | q_st | qo_sb | qo_sh | qo_st) & 1)))
+    return fail(PKV_ERR_ALIGN, "append strides must be even (4-byte rows pairs)");
+  if (batch == 0 || seq_len_q == 0) return ok();
+  pkv::AppendLaunch a{};
+  a.q = q; a.q_sb = q_sb; a.q_sh = q_sh; a.q_st = q_st;
+  a.k = k; a.k_sb = k_sb; a.k_sh = k_sh; a.k_st = k_st;
+  a.v = v; a.v_sb = v_sb; a.v_sh = v_sh; a.v_st = v_st;
+  a.rope_cos = rope_cos; a.rope_sin = rope_sin; a.rope_rows = rope_rows;
+  a.q_out = q_out; a.qo_sb = qo_sb; a.qo_sh = qo_sh; a.qo_st = qo_st;
+  a.k_pool = k_pool; a.v_pool = v_pool; a.num_slots = num_slots;
+  a.tables = block_tables; a.pitch = table_pitch; a.rows = seq_rows; a.starts = starts;
+  a.batch = batch; a.num_q_heads = num_q_heads; a.num_kv_heads = num_kv_heads;
+  a.seq_len_q = seq_len_q; a.err = err_flag;
+  return launch_status(pkv::launch_append(a, static_cast<cudaStream_t>(stream)), "append_rope");
+}
+
+size_t pkv_decode_workspace_size(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                 int32_t max_kv_len) {
+  if (batch <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0) return 0;
+  return pkv::plan_decode(batch, num_q_heads, num_kv_heads, max_kv_len).workspace_bytes;
+}
+
+static int decode_common(const pkv::DecodeLaunch& a, const pkv::KVSource& src, cudaStream_t stream) {
+  const pkv::DecodePlan plan = pkv::plan_decode(a.batch, a.num_q_heads, a.num_kv_heads, a.max_kv_len);
+  if (plan.workspace_bytes > 0) {
+    if (!a.workspace || a.workspace_bytes < plan.workspace_bytes)
+      return fail(PKV_ERR_WORKSPACE, "decode needs %zu workspace bytes, got %zu",
+                  plan.workspace_bytes, a.workspace ? a.workspace_bytes : (size_t)0);
+    if (!aligned16(a.workspace)) return fail(PKV_ERR_ALIGN, "workspace not 16-byte aligned");
+  }
+  return launch_status(pkv::launch_decode(a, src, plan, stream), "paged_decode");
+}
+
+static int check_qo(const void* q, const void* out, int64_t s0, int64_t s1, int64_t s2, int64_t o0,
+                    int64_t o1, int64_t o2) {
+  if (!q || !out) return fail(PKV_ERR_INVALID, "null q or out");
+  if (!aligned16(q) || !aligned16(out)) return fail(PKV_ERR_ALIGN, "q/out not 16-byte aligned");
+  if (!mult8(s0) || !mult8(s1) || !mult8(s2) || !mult8(o0) || !mult8(o1) || !mult8(o2))
+    return fail(PKV_ERR_ALIGN, "q/out strides must be multiples of 8 elements");
+  return PKV_OK;
+}
+
+int pkv_paged_decode(const void* q, int64_t q_sb, int64_t q_sh, const void* k_pool,
+                     const void* v_pool, int64_t num_slots, const int32_t* block_tables,
+                     int64_t table_pitch, const int32_t* seq_rows, const int32_t* kv_lens,
+                     int32_t max_kv_len, int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                     int32_t head_dim, float sm_scale, void* out, int64_t o_sb, int64_t o_sh,
+                     void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream) {
+  int st = check_heads(num_q_heads, num_kv_heads, head_dim);
+  if (st) return st;
+  if ((st = check_pool(k_pool, v_pool, num_slots, block_tables, table_pitch))) return st;
+  if ((st = check_qo(q, out, q_sb, q_sh, 0, o_sb, o_sh, 0))) return st;
+  if (!kv_lens) return fail(PKV_ERR_INVALID, "null kv_lens");
+  if (batch < 0 || max_kv_len < 0) return fail(PKV_ERR_INVALID, "negative batch / max_kv_len");
+  if (batch == 0) return ok();
+  pkv::KVSource src{};
+  src.paged = true;
+  if ((st = encode_pool(&src.kmap, k_pool, num_slots, num_kv_heads))) return st;
+  if ((st = encode_pool(&src.vmap, v_pool, num_slots, num_kv_heads))) return st;
+  src.tables = block_tables;
+  src.pitch = table_pitch;
+  src.rows = seq_rows;
+  src.num_blocks = static_cast<int32_t>(num_slots / 16);
+  pkv::DecodeLaunch a{};
+  a.q = q; a.q_sb = q_sb; a.q_sh = q_sh;
+  a.out = out; a.o_sb = o_sb; a.o_sh = o_sh;
+  a.kv_lens = kv_lens; a.batch = batch; a.num_q_heads = num_q_heads; a.num_kv_heads = num_kv_heads;
+  a.max_kv_len = max_kv_len; a.sm_scale = sm_scale;
+  a.workspace = workspace; a.workspace_bytes = workspace_bytes; a.err = err_flag;
+  return decode_common(a, src, static_cast<cudaStream_t>(stream));
+}
+
+int pkv_paged_prefill(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, const void* k_pool,
+                      const void* v_pool, int64_t num_slots, const int32_t* block_tables,
+                      int64_t table_pitch, const int32_t* seq_rows, const int32_t* kv_lens,
+                      int32_t max_kv_len, int32_t batch, int32_t seq_len_q, int32_t num_q_heads,
+                      int32_t num_kv_heads, int32_t head_dim, int32_t causal, float sm_scale,
+                      void* out, int64_t o_sb, int64_t o_sh, int64_t o_st, int32_t* err_flag,
+                      void* stream) {
+  (void)max_kv_len;
+  int st = check_heads(num_q_heads, num_kv_heads, head_dim);
+  if (st) return st;
+  if ((st = check_pool(k_pool, v_pool, num_slots, block_tables, table_pitch))) return st;
+  if ((st = check_qo(q, out, q_sb, q_sh, q_st, o_sb, o_sh, o_st))) return st;
+  if (!kv_lens) return fail(PKV_ERR_INVALID, "null kv_lens");
+  if (batch < 0 || seq_len_q < 0) return fail(PKV_ERR_INVALID, "negative batch / seq_len_q");
+  if (batch == 0 || seq_len_q == 0) return ok();
+  pkv::KVSource src{};
+  src.paged = true;
+  if ((st = encode_pool(&src.kmap, k_pool, num_slots, num_kv_heads))) return st;
+  if ((st = encode_pool(&src.vmap, v_pool, num_slots, num_kv_heads))) return st;
+  src.tables = block_tables;
+  src.pitch = table_pitch;
+  src.rows = seq_rows;
+  src.num_blocks = static_cast<int32_t>(num_slots / 16);
+  pkv::PrefillLaunch a{};
+  a.q = q; a.q_sb = q_sb; a.q_sh = q_sh; a.q_st = q_st;
+  a.out = out; a.o_sb = o_sb; a.o_sh = o_sh; a.o_st = o_st;
+  a.kv_lens = kv_lens; a.batch = batch; a.seq_len_q = seq_len_q;
+  a.num_q_heads = num_q_heads; a.num_kv_heads = num_kv_heads; a.causal = causal ? 1 : 0;
+  a.sm_scale = sm_scale; a.err = err_flag;
+  return launch_status(pkv::launch_prefill(a, src, static_cast<cudaStream_t>(stream)),
+                       "paged_prefill");
+}
+
+int pkv_dense_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, const void* k,
+                        int64_t k_sb, int64_t k_sh, int64_t k_ss, const void* v, int64_t v_sb,
+                        int64_t v_sh, int64_t v_ss, const int32_t* kv_lens, int32_t batch,
+                        int32_t seq_len_q, int32_t seq_len_k, int32_t num_q_heads,
+                        int32_t num_kv_heads, int32_t head_dim, int32_t causal, float sm_scale,
+                        void* out, int64_t o_sb, int64_t o_sh, int64_t o_st, void* workspace,
+                        size_t workspace_bytes, int32_t* err_flag, void* stream) {
+  int st = check_heads(num_q_heads, num_kv_heads, head_dim);
+  if (st) return st;
+  if ((st = check_qo(q, out, q_sb, q_sh, q_st, o_sb, o_sh, o_st))) return st;
+  if (!k || !v || !kv_lens) return fail(PKV_ERR_INVALID, "null k, v or kv_lens");
+  if (!aligned16(k) || !aligned16(v)) return fail(PKV_ERR_ALIGN, "k/v not 16-byte aligned");
+  if (!mult8(k_sb) || !mult8(k_sh) || !mult8(k_ss) || !mult8(v_sb) || !mult8(v_sh) || !mult8(v_ss))
+    return fail(PKV_ERR_ALIGN, "k/v strides must be multiples of 8 elements");
+  if (batch < 0 || seq_len_q < 0 || seq_len_k < 0)
+    return fail(PKV_ERR_INVALID, "negative batch / seq lens");
+  if (batch == 0 || seq_len_q == 0) return ok();
+  if (seq_len_k == 0) return fail(PKV_ERR_INVALID, "seq_len_k must be positive");
+  pkv::KVSource src{};
+  src.paged = false;
+  if ((st = encode_dense(&src.kmap, k, batch, num_kv_heads, seq_len_k, k_sb, k_sh, k_ss))) return st;
+  if ((st = encode_dense(&src.vmap, v, batch, num_kv_heads, seq_len_k, v_sb, v_sh, v_ss))) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (seq_len_q == 1) {
+    pkv::DecodeLaunch a{};
+    a.q = q; a.q_sb = q_sb; a.q_sh = q_sh;
+    a.out = out; a.o_sb = o_sb; a.o_sh = o_sh;
+    a.kv_lens = kv_lens; a.batch = batch; a.num_q_heads = num_q_heads;
+    a.num_kv_heads = num_kv_heads; a.max_kv_len = seq_len_k; a.sm_scale = sm_scale;
+    a.workspace = workspace; a.workspace_bytes = workspace_bytes; a.err = err_flag;
+    return decode_common(a, src, s);
+  }
+  pkv::PrefillLaunch a{};
+  a.q = q; a.q_sb = q_sb; a.q_sh = q_sh; a.q_st = q_st;
+  a.out = out; a.o_sb = o_sb; a.o_sh = o_sh; a.o_st = o_st;
+  a.kv_lens = kv_lens; a.batch = batch; a.seq_len_q = seq_len_q;
+  a.num_q_heads = num_q_heads; a.num_kv_heads = num_kv_heads; a.causal = causal ? 1 : 0;
+  a.sm_scale = sm_scale; a.err = err_flag;
+  return launch_status(pkv::launch_prefill(a, src, s), "dense_prefill");
+}
+
+}  // extern "C"

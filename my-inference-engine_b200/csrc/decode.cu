@@ -1,0 +1,448 @@
+// Paged decode attention (one query token per row) for sm_100a.
+//
+// Reference behaviour: kernels/fa2.py:23-162 launched with SEQLEN_Q = 1 and
+// is_causal = False (model.py:103, model.py:185), over K/V that
+// kv_cache.py:117-121 gathered densely.  Here K/V blocks are read in place:
+//
+//   grid  = (partitions, kv_heads * sub_groups, batch)
+//   block = 4 warps; warp w takes blocks w, w+4, w+8 ... of its partition and
+//           streams them through its own NST-deep ring of TMA stages
+//           (K and V of one KV head for one 16-token block = 8 KiB / stage).
+//
+// Math per 16-token block, one warp, all query heads of the KV group at once
+// (mma.sync m16n8k16, tokens in M, query heads in N):
+//   S^T[16 tok x 8 heads] = K[16 x 128] . Q^T[128 x 8]          (8 MMAs)
+//   online softmax per head over tokens (shuffles across the 8 row lanes)
+//   O^T[128 x 8]        += V^T[128 x 16] . P^T[16 x 8]          (8 MMAs)
+// P^T reaches the B-operand layout with movmatrix.trans, V^T the A layout with
+// ldmatrix.trans, so nothing round-trips through shared memory.  The four
+// warps merge (m, l, O) in shared memory; with several partitions each CTA
+// stores a normalised partial plus its log2-sum-exp and the last CTA of a
+// (row, kv head) to finish merges them (flash-decoding), ordered by partition
+// index so the result does not depend on which CTA finished last.
+#include <math.h>
+
+#include "pkv_device.cuh"
+#include "pkv_kernels.h"
+
+namespace pkv {
+namespace {
+
+constexpr int kDecodeWarps = 4;
+constexpr int kDecodeStages = 3;  // per warp
+constexpr int kStageBytes = 2 * kHeadBlockBytes;  // K + V, one head, one block
+constexpr int kMaxHeadsPerCta = 8;
+
+struct DecodeParams {
+  const __nv_bfloat16* q;
+  int64_t q_sb, q_sh;
+  __nv_bfloat16* out;
+  int64_t o_sb, o_sh;
+  const int32_t* kv_lens;
+  const int32_t* tables;
+  int64_t pitch;
+  const int32_t* rows;
+  int32_t num_blocks;
+  int32_t group;       // query heads per KV head
+  int32_t sub_groups;  // CTAs per KV head (group > 8)
+  int32_t blocks_per_part;
+  int32_t max_parts;
+  float scale_log2;
+  float* part_o;
+  float* part_lse;
+  int32_t* counters;
+  int32_t* err;
+};
+
+template <int NST>
+constexpr int decode_smem_bytes() {
+  return kDecodeWarps * NST * kStageBytes + kDecodeWarps * NST * 8 + 1024;
+}
+
+template <bool kPaged, int NST>
+__global__ void __launch_bounds__(kDecodeWarps * 32, 2)
+    paged_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap kmap,
+                        const __grid_constant__ CUtensorMap vmap) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kDecodeWarps * NST * kStageBytes);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int b = blockIdx.z;
+  const int y = blockIdx.y;
+  const int kvh = y / p.sub_groups;
+  const int sub = y - kvh * p.sub_groups;
+  const int head0 = kvh * p.group + sub * kMaxHeadsPerCta;
+  const int nheads = min(kMaxHeadsPerCta, p.group - sub * kMaxHeadsPerCta);
+  const int part = blockIdx.x;
+  const DevErr err{p.err};
+
+  int kv_len = max(p.kv_lens[b], 0);
+  int nblk = (kv_len + kBlockTokens - 1) / kBlockTokens;
+  const int32_t* trow = nullptr;
+  if constexpr (kPaged) {
+    const int row = p.rows ? p.rows[b] : b;
+    trow = p.tables + static_cast<int64_t>(row) * p.pitch;
+    if (nblk > p.pitch) {
+      if (part == 0 && tid == 0) err.raise(PKV_DEVERR_POSITION);
+      nblk = static_cast<int>(p.pitch);
+      kv_len = nblk * kBlockTokens;
+    }
+  }
+  if (kv_len == 0) {
+    // fa2.py:151 divides by a zero row sum: the reference yields NaN.
+    if (part == 0) {
+      for (int i = tid; i < nheads * kHeadDim; i += blockDim.x) {
+        const int h = i / kHeadDim, d = i % kHeadDim;
+        p.out[b * p.o_sb + (head0 + h) * p.o_sh + d] = __float2bfloat16(__int_as_float(0x7fc00000));
+      }
+    }
+    return;
+  }
+  const int nparts = (nblk + p.blocks_per_part - 1) / p.blocks_per_part;
+  if (part >= nparts) return;
+  const int blk_begin = part * p.blocks_per_part;
+  const int blk_end = min(nblk, blk_begin + p.blocks_per_part);
+  const int span = blk_end - blk_begin;
+  const int my_n = span > warp ? (span - warp + kDecodeWarps - 1) / kDecodeWarps : 0;
+
+  uint8_t* wstage = smem + warp * NST * kStageBytes;
+  uint64_t* wbar = bars + warp * NST;
+  if (lane == 0) {
+    for (int s = 0; s < NST; ++s) mbar_init(&wbar[s], 1);
+    fence_mbar_init();
+    if (warp == 0) {
+      prefetch_tmap(&kmap);
+      prefetch_tmap(&vmap);
+    }
+  }
+  __syncwarp();
+
+  const uint64_t policy = policy_evict_first();
+  auto issue = [&](int i) {
+    const int j = blk_begin + warp + kDecodeWarps * i;
+    const int st = i % NST;
+    uint8_t* kst = wstage + st * kStageBytes;
+    uint8_t* vst = kst + kHeadBlockBytes;
+    mbar_arrive_expect_tx(&wbar[st], kStageBytes);
+    if constexpr (kPaged) {
+      int blk = trow[j];
+      if (blk < 0 || blk >= p.num_blocks) {
+        err.raise(PKV_DEVERR_BLOCK_ID);
+        blk = 0;
+      }
+      const int slot = blk * kBlockTokens;
+      tma_load_3d(kst, &kmap, &wbar[st], 0, kvh, slot, policy);
+      tma_load_3d(kst + kBoxBytes, &kmap, &wbar[st], 64, kvh, slot, policy);
+      tma_load_3d(vst, &vmap, &wbar[st], 0, kvh, slot, policy);
+      tma_load_3d(vst + kBoxBytes, &vmap, &wbar[st], 64, kvh, slot, policy);
+    } else {
+      const int tok = j * kBlockTokens;
+      tma_load_4d(kst, &kmap, &wbar[st], 0, tok, kvh, b, policy);
+      tma_load_4d(kst + kBoxBytes, &kmap, &wbar[st], 64, tok, kvh, b, policy);
+      tma_load_4d(vst, &vmap, &wbar[st], 0, tok, kvh, b, policy);
+      tma_load_4d(vst + kBoxBytes, &vmap, &wbar[st], 64, tok, kvh, b, policy);
+    }
+  };
+  if (lane == 0) {
+    for (int i = 0; i < min(NST, my_n); ++i) issue(i);
+  }
+
+  // Q^T as the B operand: lane (g, t) holds query head g, dims 2t..2t+1 and
+  // 2t+8..2t+9 of every 16-dim k-step.  Heads >= nheads are zero columns.
+  uint32_t qb[8][2];
+  {
+    const bool live = g < nheads;
+    const __nv_bfloat16* qp = p.q + b * p.q_sb + (head0 + (live ? g : 0)) * p.q_sh;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      qb[kk][0] = live ? *reinterpret_cast<const uint32_t*>(qp + kk * 16 + 2 * t) : 0u;
+      qb[kk][1] = live ? *reinterpret_cast<const uint32_t*>(qp + kk * 16 + 8 + 2 * t) : 0u;
+    }
+  }
+
+  float m0 = -INFINITY, m1 = -INFINITY;  // running max, heads 2t and 2t+1
+  float l0 = 0.f, l1 = 0.f;              // per-lane partial row sums
+  float o[8][4];
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+
+  // ldmatrix lane roles (constant across blocks)
+  const int a_row = (lane & 7) + ((lane >> 3) & 1) * 8;  // K rows for S^T
+  const int a_chk = lane >> 4;
+  const int v_tok = (lane & 7) + ((lane >> 4) & 1) * 8;  // V rows for O^T
+  const int v_chk = (lane >> 3) & 1;
+
+  int i = 0;
+  bool ok = true;
+  for (; i < my_n; ++i) {
+    const int st = i % NST;
+    ok = mbar_wait(&wbar[st], (i / NST) & 1, err);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) break;
+    const uint32_t kst = smem_u32(wstage + st * kStageBytes);
+    const uint32_t vst = kst + kHeadBlockBytes;
+    const int j = blk_begin + warp + kDecodeWarps * i;
+
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    float s2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(kst + (kk >> 2) * kBoxBytes + swz128(a_row, (kk & 3) * 2 + a_chk), a0, a1, a2, a3);
+      if (kk & 1)
+        mma_bf16(s2, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+      else
+        mma_bf16(s, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+    }
+    const int tok0 = j * kBlockTokens + g;
+    float x0 = (s[0] + s2[0]) * p.scale_log2;
+    float x1 = (s[1] + s2[1]) * p.scale_log2;
+    float x2 = (s[2] + s2[2]) * p.scale_log2;
+    float x3 = (s[3] + s2[3]) * p.scale_log2;
+    if (tok0 >= kv_len) x0 = x1 = -INFINITY;
+    if (tok0 + 8 >= kv_len) x2 = x3 = -INFINITY;
+
+    float mb0 = fmaxf(x0, x2), mb1 = fmaxf(x1, x3);
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      mb0 = fmaxf(mb0, __shfl_xor_sync(0xffffffffu, mb0, off));
+      mb1 = fmaxf(mb1, __shfl_xor_sync(0xffffffffu, mb1, off));
+    }
+    const float mn0 = fmaxf(m0, mb0), mn1 = fmaxf(m1, mb1);
+    const float base0 = mn0 == -INFINITY ? 0.f : mn0;
+    const float base1 = mn1 == -INFINITY ? 0.f : mn1;
+    const float al0 = ex2(m0 - base0), al1 = ex2(m1 - base1);
+    const float p0 = ex2(x0 - base0), p2 = ex2(x2 - base0);
+    const float p1 = ex2(x1 - base1), p3 = ex2(x3 - base1);
+    l0 = l0 * al0 + p0 + p2;
+    l1 = l1 * al1 + p1 + p3;
+    m0 = mn0;
+    m1 = mn1;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      o[mt][0] *= al0;
+      o[mt][1] *= al1;
+      o[mt][2] *= al0;
+      o[mt][3] *= al1;
+    }
+    const uint32_t pb0 = movm_t(pack_bf16(p0, p1));
+    const uint32_t pb1 = movm_t(pack_bf16(p2, p3));
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4_t(vst + (mt >> 2) * kBoxBytes + swz128(v_tok, (mt & 3) * 2 + v_chk), a0, a1, a2, a3);
+      mma_bf16(o[mt], a0, a1, a2, a3, pb0, pb1);
+    }
+    __syncwarp();
+    if (lane == 0 && i + NST < my_n) issue(i + NST);
+  }
+  if (!ok) {
+    // Give loads still in flight a bounded chance to land before the shared
+    // memory is reused, and contribute nothing from this warp.
+    for (int k = i; k < min(my_n, i + NST); ++k) mbar_wait(&wbar[k % NST], (k / NST) & 1, err);
+    m0 = m1 = -INFINITY;
+    l0 = l1 = 0.f;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+  }
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+
+  // ---- merge the four warps (reuses the stage ring) ----
+  __syncthreads();
+  float* cm = reinterpret_cast<float*>(smem);                   // [4][8]
+  float* cl = cm + kDecodeWarps * 8;                             // [4][8]
+  float* co = reinterpret_cast<float*>(smem + 1024);             // [4][8][128]
+  if (g == 0) {
+    cm[warp * 8 + 2 * t] = m0;
+    cm[warp * 8 + 2 * t + 1] = m1;
+    cl[warp * 8 + 2 * t] = l0;
+    cl[warp * 8 + 2 * t + 1] = l1;
+  }
+  {
+    float* cw = co + warp * 8 * kHeadDim;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      const int d = mt * 16 + g;
+      cw[(2 * t) * kHeadDim + d] = o[mt][0];
+      cw[(2 * t + 1) * kHeadDim + d] = o[mt][1];
+      cw[(2 * t) * kHeadDim + d + 8] = o[mt][2];
+      cw[(2 * t + 1) * kHeadDim + d + 8] = o[mt][3];
+    }
+  }
+  __syncthreads();
+
+  const int h = tid >> 4;         // 0..7
+  const int d0 = (tid & 15) * 8;  // 8 dims per thread
+  float acc[8];
+  float L = 0.f, M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kDecodeWarps; ++w) M = fmaxf(M, cm[w * 8 + h]);
+  const float mbase = M == -INFINITY ? 0.f : M;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll
+  for (int w = 0; w < kDecodeWarps; ++w) {
+    const float f = ex2(cm[w * 8 + h] - mbase);
+    L += f * cl[w * 8 + h];
+    const float* src = co + (w * 8 + h) * kHeadDim + d0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] += f * src[e];
+  }
+
+  if (nparts == 1) {
+    if (h < nheads) {
+      const float inv = 1.f / L;
+      uint4 pk;
+      pk.x = pack_bf16(acc[0] * inv, acc[1] * inv);
+      pk.y = pack_bf16(acc[2] * inv, acc[3] * inv);
+      pk.z = pack_bf16(acc[4] * inv, acc[5] * inv);
+      pk.w = pack_bf16(acc[6] * inv, acc[7] * inv);
+      *reinterpret_cast<uint4*>(p.out + b * p.o_sb + (head0 + h) * p.o_sh + d0) = pk;
+    }
+    return;
+  }
+
+  // ---- split-K: store this partition, last CTA merges ----
+  const int64_t unit = static_cast<int64_t>(b) * gridDim.y + y;
+  {
+    const int64_t slot = unit * p.max_parts + part;
+    const float inv = 1.f / L;
+    float4* dst = reinterpret_cast<float4*>(p.part_o + (slot * 8 + h) * kHeadDim + d0);
+    dst[0] = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
+    dst[1] = make_float4(acc[4] * inv, acc[5] * inv, acc[6] * inv, acc[7] * inv);
+    if ((tid & 15) == 0) p.part_lse[slot * 8 + h] = mbase + log2f(L);
+  }
+  __threadfence();
+  __syncthreads();
+  __shared__ int s_last;
+  if (tid == 0) {
+    const int prev = atomicAdd(&p.counters[unit], 1);
+    s_last = (prev == nparts - 1);
+    if (s_last) p.counters[unit] = 0;  // every partition has arrived: rearm
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (h >= nheads) return;
+  const float* lse = p.part_lse + unit * p.max_parts * 8 + h;
+  float LM = -INFINITY;
+  for (int q = 0; q < nparts; ++q) LM = fmaxf(LM, __ldcg(lse + q * 8));
+  float W = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  for (int q = 0; q < nparts; ++q) {
+    const float w = ex2(__ldcg(lse + q * 8) - LM);
+    W += w;
+    const float4* src =
+        reinterpret_cast<const float4*>(p.part_o + ((unit * p.max_parts + q) * 8 + h) * kHeadDim + d0);
+    const float4 u = __ldcg(src), v = __ldcg(src + 1);
+    acc[0] += w * u.x;
+    acc[1] += w * u.y;
+    acc[2] += w * u.z;
+    acc[3] += w * u.w;
+    acc[4] += w * v.x;
+    acc[5] += w * v.y;
+    acc[6] += w * v.z;
+    acc[7] += w * v.w;
+  }
+  const float inv = 1.f / W;
+  uint4 pk;
+  pk.x = pack_bf16(acc[0] * inv, acc[1] * inv);
+  pk.y = pack_bf16(acc[2] * inv, acc[3] * inv);
+  pk.z = pack_bf16(acc[4] * inv, acc[5] * inv);
+  pk.w = pack_bf16(acc[6] * inv, acc[7] * inv);
+  *reinterpret_cast<uint4*>(p.out + b * p.o_sb + (head0 + h) * p.o_sh + d0) = pk;
+}
+
+// Enough CTAs to give every SM several waves of 2 resident CTAs, without
+// shrinking a partition below 16 blocks (256 tokens).
+constexpr int kTargetCtas = 148 * 2 * 6;
+constexpr int kMinBlocksPerPart = 16;
+
+template <bool kPaged>
+cudaError_t launch_decode_t(const DecodeParams& prm, const KVSource& src, dim3 grid,
+                            cudaStream_t stream) {
+  constexpr int NST = kDecodeStages;
+  auto kern = paged_decode_kernel<kPaged, NST>;
+  constexpr int smem = decode_smem_bytes<NST>();
+  static int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured_device = dev;
+  }
+  kern<<<grid, kDecodeWarps * 32, smem, stream>>>(prm, src.kmap, src.vmap);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+DecodePlan plan_decode(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                       int32_t max_kv_len) {
+  DecodePlan pl{};
+  const int group = num_q_heads / num_kv_heads;
+  pl.sub_groups = (group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta;
+  const int64_t units = static_cast<int64_t>(batch) * num_kv_heads * pl.sub_groups;
+  const int nblk = max(1, (max_kv_len + kBlockTokens - 1) / kBlockTokens);
+  const int64_t units1 = units > 0 ? units : 1;
+  int64_t parts = (kTargetCtas + units1 - 1) / units1;
+  int bpp = static_cast<int>((nblk + parts - 1) / parts);
+  bpp = max(bpp, kMinBlocksPerPart);
+  bpp = (bpp + kDecodeWarps - 1) / kDecodeWarps * kDecodeWarps;
+  pl.blocks_per_part = bpp;
+  pl.max_parts = (nblk + bpp - 1) / bpp;
+  if (pl.max_parts > 1) {
+    const int64_t slots = units * pl.max_parts;
+    pl.workspace_bytes = static_cast<size_t>(slots) * 8 * kHeadDim * sizeof(float) +
+                         static_cast<size_t>(slots) * 8 * sizeof(float) +
+                         static_cast<size_t>(units) * sizeof(int32_t);
+  } else {
+    pl.workspace_bytes = 0;
+  }
+  return pl;
+}
+
+cudaError_t launch_decode(const DecodeLaunch& a, const KVSource& src, const DecodePlan& plan,
+                          cudaStream_t stream) {
+  DecodeParams prm{};
+  prm.q = static_cast<const __nv_bfloat16*>(a.q);
+  prm.q_sb = a.q_sb;
+  prm.q_sh = a.q_sh;
+  prm.out = static_cast<__nv_bfloat16*>(a.out);
+  prm.o_sb = a.o_sb;
+  prm.o_sh = a.o_sh;
+  prm.kv_lens = a.kv_lens;
+  prm.tables = src.tables;
+  prm.pitch = src.pitch;
+  prm.rows = src.rows;
+  prm.num_blocks = src.num_blocks;
+  prm.group = a.num_q_heads / a.num_kv_heads;
+  prm.sub_groups = plan.sub_groups;
+  prm.blocks_per_part = plan.blocks_per_part;
+  prm.max_parts = plan.max_parts;
+  prm.scale_log2 = a.sm_scale * 1.4426950408889634f;
+  prm.err = a.err;
+  if (plan.max_parts > 1) {
+    const int64_t units = static_cast<int64_t>(a.batch) * a.num_kv_heads * plan.sub_groups;
+    const int64_t slots = units * plan.max_parts;
+    float* ws = static_cast<float*>(a.workspace);
+    prm.part_o = ws;
+    prm.part_lse = ws + slots * 8 * kHeadDim;
+    prm.counters = reinterpret_cast<int32_t*>(prm.part_lse + slots * 8);
+  }
+  dim3 grid(plan.max_parts, a.num_kv_heads * plan.sub_groups, a.batch);
+  return src.paged ? launch_decode_t<true>(prm, src, grid, stream)
+                   : launch_decode_t<false>(prm, src, grid, stream);
+}
+
+}  // namespace pkv

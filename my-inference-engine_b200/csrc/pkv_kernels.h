@@ -1,0 +1,86 @@
+// Host-side launch interface between the C ABI layer (capi.cu) and the
+// kernel translation units.  Not part of the public ABI.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace pkv {
+
+// Where K/V rows come from: the paged pool (3-D tensor map over
+// [slot][kv_head][128]) or a dense [B][Hkv][S][128] tensor (4-D map).
+struct KVSource {
+  bool paged;
+  CUtensorMap kmap;
+  CUtensorMap vmap;
+  const int32_t* tables;  // paged only
+  int64_t pitch;
+  const int32_t* rows;
+  int32_t num_blocks;
+};
+
+struct DecodeLaunch {
+  const void* q;
+  int64_t q_sb, q_sh;
+  void* out;
+  int64_t o_sb, o_sh;
+  const int32_t* kv_lens;
+  int32_t batch, num_q_heads, num_kv_heads;
+  int32_t max_kv_len;
+  float sm_scale;
+  void* workspace;
+  size_t workspace_bytes;
+  int32_t* err;
+};
+
+struct DecodePlan {
+  int32_t sub_groups;       // ceil(group / 8): CTAs sharing one KV head
+  int32_t blocks_per_part;  // 16-token blocks per split-K partition
+  int32_t max_parts;        // grid.x
+  size_t workspace_bytes;   // 0 when max_parts == 1
+};
+
+DecodePlan plan_decode(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                       int32_t max_kv_len);
+cudaError_t launch_decode(const DecodeLaunch& a, const KVSource& src, const DecodePlan& plan,
+                          cudaStream_t stream);
+
+struct PrefillLaunch {
+  const void* q;
+  int64_t q_sb, q_sh, q_st;
+  void* out;
+  int64_t o_sb, o_sh, o_st;
+  const int32_t* kv_lens;
+  int32_t batch, seq_len_q, num_q_heads, num_kv_heads;
+  int32_t causal;
+  float sm_scale;
+  int32_t* err;
+};
+cudaError_t launch_prefill(const PrefillLaunch& a, const KVSource& src, cudaStream_t stream);
+
+struct AppendLaunch {
+  const void* q;
+  int64_t q_sb, q_sh, q_st;
+  const void* k;
+  int64_t k_sb, k_sh, k_st;
+  const void* v;
+  int64_t v_sb, v_sh, v_st;
+  const void* rope_cos;
+  const void* rope_sin;
+  int64_t rope_rows;
+  void* q_out;
+  int64_t qo_sb, qo_sh, qo_st;
+  void* k_pool;
+  void* v_pool;
+  int64_t num_slots;
+  const int32_t* tables;
+  int64_t pitch;
+  const int32_t* rows;
+  const int32_t* starts;
+  int32_t batch, num_q_heads, num_kv_heads, seq_len_q;
+  int32_t* err;
+};
+cudaError_t launch_append(const AppendLaunch& a, cudaStream_t stream);
+
+}  // namespace pkv

@@ -1,0 +1,275 @@
+"""Paged KV cache with device-resident int32 block tables (drop-in for the
+reference's kv_cache.py:8-121).
+
+Host semantics are the reference's, decision for decision: a Python free list
+popped from its tail (kv_cache.py:26, :64), blocks returned by `free`/`trim`
+appended at the tail and therefore reused first (:47-50, :66-72), monotonic
+sequence ids (:31-45), `RuntimeError("KV cache exhausted ...")` when the pool
+runs dry (:58-61), lengths kept as plain ints so reading them never syncs.
+
+What moves to the device:
+  * `block_tables` -- int32 [max_seqs, table_pitch]; each live sequence owns a
+    row.  New block ids are queued on the host and uploaded in one copy at the
+    next `prepare`, so there is no per-token host loop and no [B, S] index
+    tensor (the reference builds both every step, kv_cache.py:88-100).
+  * `prepare(seqs, T)` uploads one int32 [3, B] array (table row, start,
+    kv_len per batch row) and returns a `PagedStep` in the two positions the
+    reference returns slot_mapping and gather_idx.
+  * `write()` scatters through the table on the GPU; `read()` returns
+    zero-copy `PagedKV` handles instead of a dense gathered copy;
+    `append()` fuses RoPE on q and k with the write.
+
+`buf` keeps the reference layout [NUM_LAYERS, 2, num_blocks*16, NUM_KV_HEADS,
+HEAD_DIM] (kv_cache.py:20-22), so code that inspects it (bytes per token in
+metrics/benchmark_concurrency.py:25-26) and the CPU oracle read it unchanged.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+import pagedkv
+from model import HEAD_DIM, NUM_KV_HEADS, NUM_LAYERS
+
+BLOCK_SIZE = 16  # the kernels' block geometry (chat.py:22 uses 16 too)
+
+
+@dataclass
+class PagedStep:
+    """Device description of one forward step over B rows (built by prepare)."""
+    cache: "KVCache"
+    T: int
+    starts_host: list
+    rows: torch.Tensor      # int32 [B] table row of each batch row
+    starts: torch.Tensor    # int32 [B] length before this step
+    kv_lens: torch.Tensor   # int32 [B] starts + T
+    max_kv_len: int         # host-side max(kv_lens), sizes decode grids
+
+    @property
+    def batch(self) -> int:
+        return len(self.starts_host)
+
+
+class PagedKV:
+    """Zero-copy stand-in for one of the dense K/V tensors `read()` returned in
+    the reference: a layer's K (which=0) or V (which=1) plane plus the step's
+    block tables.  `shape` mirrors the dense [B, Hkv, S, D] it replaces."""
+
+    def __init__(self, cache: "KVCache", layer_idx: int, which: int, step: PagedStep):
+        self.cache, self.layer_idx, self.which, self.step = cache, layer_idx, which, step
+
+    @property
+    def plane(self) -> torch.Tensor:
+        return self.cache.buf[self.layer_idx, self.which]
+
+    @property
+    def shape(self) -> torch.Size:
+        return torch.Size((self.step.batch, NUM_KV_HEADS, self.step.max_kv_len, HEAD_DIM))
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return self.cache.buf.dtype
+
+    @property
+    def device(self) -> torch.device:
+        return self.cache.buf.device
+
+    @property
+    def is_cuda(self) -> bool:
+        return self.cache.buf.is_cuda
+
+    def materialize(self) -> torch.Tensor:
+        """Dense [B, Hkv, S, D] copy (test/debug only; the kernels never use it).
+        Positions past a row's kv_len read block 0's slots, as the reference's
+        padded gather does (kv_cache.py:95)."""
+        c, st = self.cache, self.step
+        S = st.max_kv_len
+        nb = math.ceil(S / c.block_size)
+        tbl = c.block_tables[st.rows.long(), :nb].long()
+        lens_blocks = (st.kv_lens.long() + c.block_size - 1) // c.block_size
+        valid = torch.arange(nb, device=tbl.device)[None, :] < lens_blocks[:, None]
+        tbl = torch.where(valid, tbl, torch.zeros_like(tbl))
+        pos = torch.arange(S, device=tbl.device)
+        idx = tbl[:, pos // c.block_size] * c.block_size + pos % c.block_size
+        return self.plane[idx].transpose(1, 2)
+
+
+class BlockTables:
+    """Host half of the cache: free list, per-sequence block lists, lengths and
+    table rows (no device memory; unit-testable on the CPU).  Every decision
+    matches the reference KVCache (kv_cache.py:24-72)."""
+
+    def __init__(self, num_blocks, block_size, max_seqs=None, max_blocks_per_seq=None):
+        self.num_blocks = num_blocks
+        self.block_size = block_size
+        self._free_blocks = list(range(num_blocks))
+        self._block_tables = {}  # seq id -> list of block ids, in logical order
+        self._lengths = {}  # seq id -> tokens written so far
+        self._next_seq = 0
+        self.max_seqs = int(max_seqs or min(num_blocks, 4096))
+        self.table_pitch = int(max_blocks_per_seq or min(num_blocks, 8192))
+        self._row_of = {}  # seq id -> table row
+        self._free_rows = list(range(self.max_seqs - 1, -1, -1))
+        self._pending = {}  # (row, col) -> block id not yet on the device (last write wins)
+
+    def free_block_count(self):
+        return len(self._free_blocks)
+
+    def blocks_needed(self, seq, total_len):
+        """Extra blocks `seq` (None for a brand-new sequence) needs to hold total_len tokens."""
+        held = len(self._block_tables[seq]) if seq is not None else 0
+        return max(0, math.ceil(total_len / self.block_size) - held)
+
+    def alloc(self):
+        """Start a new, empty sequence (and give it a device table row)."""
+        if not self._free_rows:
+            raise RuntimeError(f"KV cache exhausted: all {self.max_seqs} sequence rows in use")
+        seq = self._next_seq
+        self._next_seq += 1
+        self._block_tables[seq] = []
+        self._lengths[seq] = 0
+        self._row_of[seq] = self._free_rows.pop()
+        return seq
+
+    def free(self, seq):
+        """Return every block (and the table row) this sequence holds."""
+        self._free_blocks.extend(self._block_tables.pop(seq))
+        del self._lengths[seq]
+        self._free_rows.append(self._row_of.pop(seq))
+
+    def length(self, seq):
+        return self._lengths[seq]
+
+    def ensure_capacity(self, seq, total_len):
+        """Grow seq's block table until it covers total_len tokens. Raises if the pool runs dry."""
+        need = self.blocks_needed(seq, total_len)
+        if need > len(self._free_blocks):
+            raise RuntimeError(
+                f"KV cache exhausted: seq {seq} needs {need} more blocks, only {len(self._free_blocks)} free"
+            )
+        table = self._block_tables[seq]
+        if len(table) + need > self.table_pitch:
+            raise RuntimeError(
+                f"KV cache exhausted: seq {seq} would hold {len(table) + need} blocks, "
+                f"the device table holds {self.table_pitch} per sequence")
+        row = self._row_of[seq]
+        for _ in range(need):
+            blk = self._free_blocks.pop()
+            self._pending[(row, len(table))] = blk
+            table.append(blk)
+
+    def trim(self, seq):
+        """Give back any blocks past the one holding seq's last written token."""
+        table = self._block_tables[seq]
+        keep = math.ceil(self._lengths[seq] / self.block_size)
+        self._free_blocks.extend(table[keep:])
+        del table[keep:]
+
+    def advance(self, seqs, T):
+        """Record that every seq in `seqs` now holds T more tokens (after all layers wrote)."""
+        for s in seqs:
+            self._lengths[s] += T
+
+    def table_row(self, seq):
+        return self._row_of[seq]
+
+    def host_table(self, seq):
+        return list(self._block_tables[seq])
+
+    def take_pending(self):
+        """(row, col, block) entries queued since the last call."""
+        pend = [(r, c, b) for (r, c), b in self._pending.items()]
+        self._pending = {}
+        return pend
+
+    def step_rows(self, seqs, T):
+        """Host part of prepare(): reserve blocks, return (starts, rows)."""
+        starts = [self._lengths[s] for s in seqs]
+        for s, start in zip(seqs, starts):
+            self.ensure_capacity(s, start + T)
+        return starts, [self._row_of[s] for s in seqs]
+
+
+class KVCache(BlockTables):
+    """Paged KV cache shared by every concurrently active sequence.
+
+    Same constructor and methods as the reference (kv_cache.py:19-121), plus
+    two optional sizing knobs for the device tables:
+      max_seqs            table rows, i.e. sequences alive at once
+      max_blocks_per_seq  table pitch, i.e. longest sequence in blocks
+    """
+
+    def __init__(self, num_blocks, block_size, device, dtype, max_seqs=None,
+                 max_blocks_per_seq=None):
+        device = torch.device(device)
+        assert device.type == "cuda", "KVCache needs a CUDA device (no CPU fallback)"
+        assert block_size == BLOCK_SIZE, f"block_size must be {BLOCK_SIZE}"
+        assert dtype == torch.bfloat16, "the paged kernels store bf16 K/V"
+        super().__init__(num_blocks, block_size, max_seqs, max_blocks_per_seq)
+        self.buf = torch.zeros(NUM_LAYERS, 2, num_blocks * block_size, NUM_KV_HEADS, HEAD_DIM,
+                               device=device, dtype=dtype)
+        self.device = device
+        self.block_tables = torch.zeros(self.max_seqs, self.table_pitch, dtype=torch.int32,
+                                        device=device)
+        self.err_flag = torch.zeros(1, dtype=torch.int32, device=device)
+
+    # ---- device side ----
+    def flush_tables(self):
+        """Upload queued (row, col, block) entries in one copy + one scatter."""
+        pend = self.take_pending()
+        if not pend:
+            return
+        d = torch.tensor(pend, dtype=torch.int64).pin_memory().to(self.device, non_blocking=True)
+        flat = d[:, 0] * self.table_pitch + d[:, 1]
+        self.block_tables.view(-1).index_copy_(0, flat, d[:, 2].to(torch.int32))
+
+    def prepare(self, seqs, T):
+        """Set up one forward step that appends T tokens to every seq in `seqs`.
+
+        Returns (starts, step, step): each row's length before this step as
+        plain ints (as the reference), and a PagedStep where the reference
+        returned slot_mapping and gather_idx (kv_cache.py:74-101).
+        """
+        starts, rows = self.step_rows(seqs, T)
+        self.flush_tables()
+        B = len(seqs)
+        host = torch.empty(3, B, dtype=torch.int32, pin_memory=True)
+        host[0] = torch.tensor(rows, dtype=torch.int32)
+        st = torch.tensor(starts, dtype=torch.int32)
+        host[1] = st
+        host[2] = st + T
+        dev = host.to(self.device, non_blocking=True)
+        step = PagedStep(self, T, starts, dev[0], dev[1], dev[2], max(starts) + T)
+        return starts, step, step
+
+    def write(self, layer_idx, slot_mapping, k, v):
+        """Scatter this step's new k/v for one layer into their physical slots
+        (reference kv_cache.py:108-115).  k, v: [B, NUM_KV_HEADS, T, HEAD_DIM];
+        slot_mapping is the PagedStep from prepare()."""
+        step = slot_mapping
+        pagedkv.append_rope(None, k, v, None, None, None, self.buf[layer_idx, 0],
+                            self.buf[layer_idx, 1], self.block_tables, step.rows, step.starts,
+                            self.err_flag)
+
+    def append(self, layer_idx, step, q, k, v, rope_cos, rope_sin, q_out):
+        """Fused apply_rope(q, k) + write (model.py:92-96): roped q goes to
+        q_out, roped k and v into the pool.  rope_cos/sin: bf16 [positions, 128]."""
+        pagedkv.append_rope(q, k, v, rope_cos, rope_sin, q_out, self.buf[layer_idx, 0],
+                            self.buf[layer_idx, 1], self.block_tables, step.rows, step.starts,
+                            self.err_flag)
+
+    def read(self, layer_idx, gather_idx):
+        """This layer's K and V as zero-copy PagedKV handles (the reference
+        returned dense gathered copies, kv_cache.py:117-121)."""
+        step = gather_idx
+        return PagedKV(self, layer_idx, 0, step), PagedKV(self, layer_idx, 1, step)
+
+    def check_errors(self):
+        """Read (and clear) the device error flag; raises RuntimeError if a kernel
+        met an out-of-range block id or position.  Synchronises."""
+        v = int(self.err_flag.item())
+        if v:
+            self.err_flag.zero_()
+            raise RuntimeError(f"paged KV kernel reported device error bits {v:#x}")

@@ -1,0 +1,71 @@
+"""libpagedkv.so loads without a GPU and exports every symbol of the header."""
+import ctypes
+import re
+
+from conftest import REPO
+
+
+def _header_symbols():
+    text = (REPO / "include" / "pagedkv.h").read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\**\s+\**(pkv_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_expected_entry_points():
+    syms = _header_symbols()
+    for s in ["pkv_append_rope", "pkv_paged_decode", "pkv_paged_prefill", "pkv_dense_attention",
+              "pkv_decode_workspace_size", "pkv_version", "pkv_status_string", "pkv_last_error"]:
+        assert s in syms
+
+
+def test_library_builds_loads_and_exports_all_symbols():
+    import pagedkv_build
+
+    path = pagedkv_build.build()
+    lib = ctypes.CDLL(str(path))
+    for s in _header_symbols():
+        assert hasattr(lib, s), f"{s} declared in pagedkv.h but not exported"
+    import pagedkv
+
+    L = pagedkv.lib()
+    assert set(pagedkv.exported_symbols()) == set(_header_symbols()), \
+        "the ctypes binding and the header disagree"
+    assert L.pkv_version() >= 100
+    assert L.pkv_status_string(0) == b"ok"
+    assert L.pkv_status_string(6) == b"workspace too small"
+
+
+def test_decode_workspace_plan_is_host_only_and_sane():
+    import pagedkv
+
+    L = pagedkv.lib()
+    # short contexts need no split-K scratch
+    assert L.pkv_decode_workspace_size(4, 12, 2, 37) == 0
+    # long contexts at small batch split; size grows with batch
+    a = L.pkv_decode_workspace_size(4, 12, 2, 8192)
+    b = L.pkv_decode_workspace_size(8, 12, 2, 8192)
+    assert a > 0 and b >= a
+    # invalid head counts report 0 instead of failing
+    assert L.pkv_decode_workspace_size(4, 12, 5, 8192) == 0
+
+
+def test_entry_points_reject_bad_arguments_without_a_gpu():
+    """Validation runs before any CUDA call, so it is testable on the CPU."""
+    import pagedkv
+
+    L = pagedkv.lib()
+    # head_dim 64 -> PKV_ERR_UNSUPPORTED
+    st = L.pkv_paged_decode(16, 0, 0, 16, 16, 16, 16, 1, None, 16, 1, 1, 12, 2, 64, 1.0,
+                            16, 0, 0, None, 0, None, None)
+    assert st == 2 and b"head_dim" in L.pkv_last_error()
+    # Hq not a multiple of Hkv -> PKV_ERR_INVALID
+    st = L.pkv_paged_prefill(16, 0, 0, 0, 16, 16, 16, 16, 1, None, 16, 1, 1, 1, 12, 5, 128, 1,
+                             1.0, 16, 0, 0, 0, None, None)
+    assert st == 1
+    # misaligned pool plane -> PKV_ERR_ALIGN
+    st = L.pkv_paged_decode(16, 0, 0, 18, 16, 16, 16, 1, None, 16, 1, 1, 12, 2, 128, 1.0,
+                            16, 0, 0, None, 0, None, None)
+    assert st == 3
+    # num_slots not a multiple of 16 -> PKV_ERR_INVALID
+    st = L.pkv_append_rope(None, 0, 0, 0, 16, 0, 0, 0, 16, 0, 0, 0, None, None, 0, None, 0, 0, 0,
+                           16, 16, 17, 16, 1, None, 16, 1, 12, 2, 1, 128, None, None)
+    assert st == 1

@@ -1,0 +1,144 @@
+"""Ragged causal prefill attention through the C ABI vs the oracle and the
+reference's golden outputs (bf16, max-abs 2e-2)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_helpers import TOL, build_cache, max_err, write_history
+from oracle import attention_ref, cases
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("ci", [0, 2, 4])  # "prefill", "chunked", "ragged prefill"
+def test_reference_fa2_prefill_cases_dense(cuda, golden, ci):
+    from kernels.fa2 import FlashAttention2Function
+
+    fx = np.load(golden / "attention_cases.npz")
+    name, q, k, v, lens, causal = cases.fa2_cases()[ci]
+    assert cases.sha(q, k, v) == str(fx[f"c{ci}_input_sha"])
+    kv_lens = torch.tensor(lens, dtype=torch.int32, device=cuda)
+    out = FlashAttention2Function.apply(q.to(cuda), k.to(cuda), v.to(cuda), causal, kv_lens)
+    torch.cuda.synchronize()
+    rows = fx[f"c{ci}_rows"]
+    assert max_err(out[:, :, rows], fx[f"c{ci}_out"]) < TOL, name
+
+
+def test_config1_paged_prefill_matches_reference(cuda, golden):
+    from kernels.fa2 import FlashAttention2Function
+
+    fx = np.load(golden / "prefill_config1.npz")
+    inp = cases.prefill_config1_inputs()
+    T = inp["T"]
+    cache = build_cache(inp["num_blocks"], inp["perm"], cuda)
+    seqs = [cache.alloc() for _ in inp["prior"]]
+    write_history(cache, seqs, inp["hist_k"], inp["hist_v"])
+    starts, step, gidx = cache.prepare(seqs, T)
+    cache.write(0, step, inp["k_new"].to(cuda), inp["v_new"].to(cuda))
+    k, v = cache.read(0, gidx)
+    out = FlashAttention2Function.apply(inp["q"].to(cuda), k, v, True, step.kv_lens)
+    torch.cuda.synchronize()
+    cache.check_errors()
+    assert cases.sha(cache.buf[0].cpu()) == str(fx["pool_sha"])
+    for i, s in enumerate(seqs):
+        t = [x for x in fx["tables"][i] if x >= 0]
+        assert cache.block_tables[cache.table_row(s), :len(t)].tolist() == t
+    assert max_err(out, fx["out"]) < TOL
+
+
+def test_config1_full_batch8_from_empty(cuda):
+    """BASELINE config 1 at full size: 8 rows, prompt lengths U[16,1024], empty
+    caches, shuffled pool.  Each row prefilled on its own (one prompt per
+    prepare, chat.py:_admit) and checked against the oracle."""
+    from kernels.fa2 import flash_attention
+
+    g = torch.Generator().manual_seed(42)
+    lens = torch.randint(16, 1025, (8,), generator=g).tolist()
+    N = sum(math.ceil(n / 16) for n in lens) + 16
+    cache = build_cache(N, torch.randperm(N, generator=g).tolist(), cuda)
+    cache.buf.fill_(cases.PAD_VALUE)
+    for n in lens:
+        s = cache.alloc()
+        q = torch.randn(1, 12, n, 128, generator=g).to(torch.bfloat16)
+        k = torch.randn(1, 2, n, 128, generator=g).to(torch.bfloat16)
+        v = torch.randn(1, 2, n, 128, generator=g).to(torch.bfloat16)
+        _, step, gidx = cache.prepare([s], n)
+        cache.write(0, step, k.to(cuda), v.to(cuda))
+        kh, vh = cache.read(0, gidx)
+        out = flash_attention(q.to(cuda), kh, vh, True, step.kv_lens)
+        torch.cuda.synchronize()
+        want = attention_ref.attention_np(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                          [n], True)
+        assert max_err(out, want) < TOL, n
+    cache.check_errors()
+
+
+@pytest.mark.parametrize("prior,T", [([0, 0], 33), ([5, 100, 16], 16), ([1000, 3], 64),
+                                     ([0], 1024), ([17], 2), ([300, 0, 45, 1], 129)])
+def test_paged_prefill_random_vs_oracle(cuda, prior, T):
+    """Chunked prefill onto existing history (bottom-right causal), poisoned pool."""
+    from kernels.fa2 import flash_attention
+
+    g = torch.Generator().manual_seed(sum(prior) + T)
+    B = len(prior)
+    N = sum(math.ceil((n + T) / 16) for n in prior) + 8
+    cache = build_cache(N, torch.randperm(N, generator=g).tolist(), cuda)
+    cache.buf.fill_(cases.PAD_VALUE)
+    seqs = [cache.alloc() for _ in prior]
+    hk = [torch.randn(1, 2, n, 128, generator=g).to(torch.bfloat16) for n in prior]
+    hv = [torch.randn(1, 2, n, 128, generator=g).to(torch.bfloat16) for n in prior]
+    write_history(cache, seqs, hk, hv)
+    q = torch.randn(B, 12, T, 128, generator=g).to(torch.bfloat16)
+    kn = torch.randn(B, 2, T, 128, generator=g).to(torch.bfloat16)
+    vn = torch.randn(B, 2, T, 128, generator=g).to(torch.bfloat16)
+    _, step, gidx = cache.prepare(seqs, T)
+    cache.write(0, step, kn.to(cuda), vn.to(cuda))
+    kh, vh = cache.read(0, gidx)
+    out = flash_attention(q.to(cuda), kh, vh, True, step.kv_lens)
+    torch.cuda.synchronize()
+    cache.check_errors()
+    for b in range(B):
+        kd = torch.cat([hk[b], kn[b:b + 1]], 2)
+        vd = torch.cat([hv[b], vn[b:b + 1]], 2)
+        want = attention_ref.attention_np(q[b:b + 1].float().numpy(), kd.float().numpy(),
+                                          vd.float().numpy(), [prior[b] + T], True)
+        assert max_err(out[b:b + 1], want) < TOL, (b, prior[b], T)
+
+
+def test_non_causal_multi_query(cuda):
+    """is_causal=False with T > 1: every query sees all kv_len keys."""
+    from kernels.fa2 import flash_attention
+
+    g = torch.Generator().manual_seed(9)
+    lens = [50, 300]
+    q = torch.randn(2, 12, 20, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(2, 2, 300, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(2, 2, 300, 128, generator=g).to(torch.bfloat16)
+    out = flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), False,
+                          torch.tensor(lens, dtype=torch.int32, device=cuda))
+    want = attention_ref.attention_np(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                      lens, False)
+    assert max_err(out, want) < TOL
+
+
+def test_left_padded_batched_prefill(cuda):
+    """Ragged prompts in ONE call: rows left-padded to T, bottom-right causal
+    aligns each row's real queries with its keys (fa2.py:110-111)."""
+    from kernels.fa2 import flash_attention
+
+    g = torch.Generator().manual_seed(77)
+    lens = [16, 500, 1024, 77]
+    T = max(lens)
+    B = len(lens)
+    q = torch.randn(B, 12, T, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, 2, T, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, 2, T, 128, generator=g).to(torch.bfloat16)
+    out = flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), True,
+                          torch.tensor(lens, dtype=torch.int32, device=cuda))
+    for b, n in enumerate(lens):
+        want = attention_ref.attention_np(q[b:b + 1, :, T - n:].float().numpy(),
+                                          k[b:b + 1, :, :n].float().numpy(),
+                                          v[b:b + 1, :, :n].float().numpy(), [n], True)
+        assert max_err(out[b:b + 1, :, T - n:], want) < TOL
