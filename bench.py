@@ -46,7 +46,7 @@ FALLBACK_HBM_GBS = 6650.0
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seqs", type=int, default=256)
@@ -106,7 +106,7 @@ class ClockSampler:
             uuid = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", uuid, "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                 "-i", uuid, "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
                 text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()

@@ -183,6 +183,9 @@ size_t pkv_decode_workspace_size(int32_t batch, int32_t num_q_heads, int32_t num
 
 static int decode_common(const pkv::DecodeLaunch& a, const pkv::KVSource& src, cudaStream_t stream) {
   const pkv::DecodePlan plan = pkv::plan_decode(a.batch, a.num_q_heads, a.num_kv_heads, a.max_kv_len);
+  if (static_cast<int64_t>(a.batch) * a.num_kv_heads * plan.sub_groups > pkv::decode_max_units())
+    return fail(PKV_ERR_UNSUPPORTED, "batch * kv_heads too large for one decode launch (max %lld)",
+                (long long)pkv::decode_max_units());
   if (plan.workspace_bytes > 0) {
     if (!a.workspace || a.workspace_bytes < plan.workspace_bytes)
       return fail(PKV_ERR_WORKSPACE, "decode needs %zu workspace bytes, got %zu",

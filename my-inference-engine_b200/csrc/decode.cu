@@ -32,6 +32,9 @@ constexpr int kDecodeWarps = 4;
 constexpr int kDecodeStages = 3;  // per warp
 constexpr int kStageBytes = 2 * kHeadBlockBytes;  // K + V, one head, one block
 constexpr int kMaxHeadsPerCta = 8;
+// split-K completion counters: one int32 per (row, kv head, head sub-group)
+constexpr int64_t kDecodeMaxUnits = 1 << 16;
+constexpr size_t kDecodeCounterBytes = kDecodeMaxUnits * sizeof(int32_t);
 
 struct DecodeParams {
   const __nv_bfloat16* q;
@@ -362,6 +365,13 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
   *reinterpret_cast<uint4*>(p.out + b * p.o_sb + (head0 + h) * p.o_sh + d0) = pk;
 }
 
+}  // namespace
+
+size_t decode_counter_bytes() { return kDecodeCounterBytes; }
+int64_t decode_max_units() { return kDecodeMaxUnits; }
+
+namespace {
+
 // Enough CTAs to give every SM several waves of 2 resident CTAs, without
 // shrinking a partition below 16 blocks (256 tokens).
 constexpr int kTargetCtas = 148 * 2 * 6;
@@ -403,9 +413,8 @@ DecodePlan plan_decode(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
   pl.max_parts = (nblk + bpp - 1) / bpp;
   if (pl.max_parts > 1) {
     const int64_t slots = units * pl.max_parts;
-    pl.workspace_bytes = static_cast<size_t>(slots) * 8 * kHeadDim * sizeof(float) +
-                         static_cast<size_t>(slots) * 8 * sizeof(float) +
-                         static_cast<size_t>(units) * sizeof(int32_t);
+    pl.workspace_bytes = kDecodeCounterBytes + static_cast<size_t>(slots) * 8 * sizeof(float) +
+                         static_cast<size_t>(slots) * 8 * kHeadDim * sizeof(float);
   } else {
     pl.workspace_bytes = 0;
   }
@@ -435,10 +444,13 @@ cudaError_t launch_decode(const DecodeLaunch& a, const KVSource& src, const Deco
   if (plan.max_parts > 1) {
     const int64_t units = static_cast<int64_t>(a.batch) * a.num_kv_heads * plan.sub_groups;
     const int64_t slots = units * plan.max_parts;
-    float* ws = static_cast<float*>(a.workspace);
-    prm.part_o = ws;
-    prm.part_lse = ws + slots * 8 * kHeadDim;
-    prm.counters = reinterpret_cast<int32_t*>(prm.part_lse + slots * 8);
+    // Counters always live in the first kDecodeCounterBytes, whatever the
+    // plan, so a workspace reused with another shape never reads partials
+    // as counters; every launch leaves the counters it used at zero.
+    uint8_t* ws = static_cast<uint8_t*>(a.workspace);
+    prm.counters = reinterpret_cast<int32_t*>(ws);
+    prm.part_lse = reinterpret_cast<float*>(ws + kDecodeCounterBytes);
+    prm.part_o = prm.part_lse + slots * 8;
   }
   dim3 grid(plan.max_parts, a.num_kv_heads * plan.sub_groups, a.batch);
   return src.paged ? launch_decode_t<true>(prm, src, grid, stream)

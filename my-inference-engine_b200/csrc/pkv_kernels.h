@@ -41,6 +41,10 @@ struct DecodePlan {
   size_t workspace_bytes;   // 0 when max_parts == 1
 };
 
+// Fixed head of every split-K workspace: the completion counters.
+size_t decode_counter_bytes();
+int64_t decode_max_units();  // rows * kv_heads * sub_groups per launch
+
 DecodePlan plan_decode(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
                        int32_t max_kv_len);
 cudaError_t launch_decode(const DecodeLaunch& a, const KVSource& src, const DecodePlan& plan,
