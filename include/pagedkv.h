@@ -160,6 +160,44 @@ int pkv_dense_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
                         void* workspace, size_t workspace_bytes,
                         int32_t* err_flag, void* stream);
 
+/*
+ * Size of the library-owned scratch used by pkv_paged_decode_static_scratch:
+ * one array of this many bytes per GPU that loads the library, held until
+ * the process exits.
+ */
+#define PKV_DECODE_STATIC_SCRATCH_BYTES (8u << 20)
+
+/*
+ * pkv_paged_decode without a caller-provided workspace.  No counterpart in
+ * the reference: it exists for callers that cannot call cudaMalloc -- code
+ * running where the CUDA allocator is not theirs to use (a host that owns
+ * all device memory through its own pool, a plugin whose host forbids
+ * allocation during a serving step, or code that must not touch the
+ * allocator at all).  Inputs, outputs, pool and tables are still passed in;
+ * only the split-K scratch comes from a static device array of
+ * PKV_DECODE_STATIC_SCRATCH_BYTES inside the library.
+ *
+ *  - Calls no cudaMalloc/cudaFree or any allocating routine.
+ *  - The first call on a device looks up that array's device address (with
+ *    the device current), so make the first call on each device before any
+ *    stream capture begins.
+ *  - Shapes whose split-K scratch (pkv_decode_workspace_size) exceeds
+ *    PKV_DECODE_STATIC_SCRATCH_BYTES are rejected with PKV_ERR_WORKSPACE and
+ *    nothing is launched.
+ *  - Every call on a device shares the one array, which keeps the previous
+ *    call's contents; the call clears the counters it needs itself.  Calls
+ *    whose kernels overlap on the GPU (different streams without ordering)
+ *    race on the array and produce wrong results: order them on one stream.
+ */
+int pkv_paged_decode_static_scratch(const void* q, int64_t q_sb, int64_t q_sh,
+                                    const void* k_pool, const void* v_pool, int64_t num_slots,
+                                    const int32_t* block_tables, int64_t table_pitch,
+                                    const int32_t* seq_rows, const int32_t* kv_lens,
+                                    int32_t max_kv_len, int32_t batch, int32_t num_q_heads,
+                                    int32_t num_kv_heads, int32_t head_dim, float sm_scale,
+                                    void* out, int64_t o_sb, int64_t o_sh,
+                                    int32_t* err_flag, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -308,4 +308,45 @@ int pkv_dense_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
   return launch_status(pkv::launch_prefill(a, src, s), "dense_prefill");
 }
 
+int pkv_paged_decode_static_scratch(const void* q, int64_t q_sb, int64_t q_sh, const void* k_pool,
+                                    const void* v_pool, int64_t num_slots,
+                                    const int32_t* block_tables, int64_t table_pitch,
+                                    const int32_t* seq_rows, const int32_t* kv_lens,
+                                    int32_t max_kv_len, int32_t batch, int32_t num_q_heads,
+                                    int32_t num_kv_heads, int32_t head_dim, float sm_scale,
+                                    void* out, int64_t o_sb, int64_t o_sh, int32_t* err_flag,
+                                    void* stream) {
+  int st = check_heads(num_q_heads, num_kv_heads, head_dim);
+  if (st) return st;
+  if ((st = check_pool(k_pool, v_pool, num_slots, block_tables, table_pitch))) return st;
+  if ((st = check_qo(q, out, q_sb, q_sh, 0, o_sb, o_sh, 0))) return st;
+  if (!kv_lens) return fail(PKV_ERR_INVALID, "null kv_lens");
+  if (batch < 0 || max_kv_len < 0) return fail(PKV_ERR_INVALID, "negative batch / max_kv_len");
+  if (batch == 0) return ok();
+  const pkv::DecodePlan plan = pkv::plan_decode(batch, num_q_heads, num_kv_heads, max_kv_len);
+  if (static_cast<int64_t>(batch) * num_kv_heads * plan.sub_groups > pkv::decode_max_units())
+    return fail(PKV_ERR_UNSUPPORTED, "batch * kv_heads too large for one decode launch (max %lld)",
+                (long long)pkv::decode_max_units());
+  if (plan.workspace_bytes > PKV_DECODE_STATIC_SCRATCH_BYTES)
+    return fail(PKV_ERR_WORKSPACE,
+                "this shape needs %zu bytes of split-K scratch, more than the %u-byte static "
+                "array; use pkv_paged_decode with a caller-provided workspace",
+                plan.workspace_bytes, (unsigned)PKV_DECODE_STATIC_SCRATCH_BYTES);
+  pkv::KVSource src{};
+  src.paged = true;
+  if ((st = encode_pool(&src.kmap, k_pool, num_slots, num_kv_heads))) return st;
+  if ((st = encode_pool(&src.vmap, v_pool, num_slots, num_kv_heads))) return st;
+  src.tables = block_tables;
+  src.pitch = table_pitch;
+  src.rows = seq_rows;
+  src.num_blocks = static_cast<int32_t>(num_slots / 16);
+  pkv::DecodeLaunch a{};
+  a.q = q; a.q_sb = q_sb; a.q_sh = q_sh;
+  a.out = out; a.o_sb = o_sb; a.o_sh = o_sh;
+  a.kv_lens = kv_lens; a.batch = batch; a.num_q_heads = num_q_heads; a.num_kv_heads = num_kv_heads;
+  a.max_kv_len = max_kv_len; a.sm_scale = sm_scale; a.err = err_flag;
+  return launch_status(pkv::launch_decode_static(a, src, plan, static_cast<cudaStream_t>(stream)),
+                       "paged_decode_static_scratch");
+}
+
 }  // extern "C"

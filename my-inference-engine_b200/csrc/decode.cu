@@ -22,6 +22,8 @@
 // index so the result does not depend on which CTA finished last.
 #include <math.h>
 
+#include <mutex>
+
 #include "pkv_device.cuh"
 #include "pkv_kernels.h"
 
@@ -455,6 +457,60 @@ cudaError_t launch_decode(const DecodeLaunch& a, const KVSource& src, const Deco
   dim3 grid(plan.max_parts, a.num_kv_heads * plan.sub_groups, a.batch);
   return src.paged ? launch_decode_t<true>(prm, src, grid, stream)
                    : launch_decode_t<false>(prm, src, grid, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Decode with library-owned scratch, for callers that cannot allocate device
+// memory (see pkv_paged_decode_static_scratch in pagedkv.h).
+//
+// The split-K scratch lives in this file-scope device array instead of a
+// caller-provided workspace.  Host code must not pass `g_decode_scratch`
+// itself to a kernel: on the host that name only stands in for the device
+// symbol.  The device address is looked up once per device, with that device
+// current, through cudaGetSymbolAddress, and that pointer is what the kernel
+// receives.  Every GPU that loads the library keeps these bytes until exit.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) uint8_t g_decode_scratch[PKV_DECODE_STATIC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxScratchDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_ptr[kMaxScratchDevices] = {};
+}  // namespace
+
+cudaError_t decode_static_scratch(void** ptr) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxScratchDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess) return e;
+    g_scratch_ptr[dev] = p;
+  }
+  *ptr = g_scratch_ptr[dev];
+  return cudaSuccess;
+}
+
+cudaError_t launch_decode_static(const DecodeLaunch& a, const KVSource& src,
+                                 const DecodePlan& plan, cudaStream_t stream) {
+  void* scratch = nullptr;
+  cudaError_t e = decode_static_scratch(&scratch);
+  if (e != cudaSuccess) return e;
+  if (plan.max_parts > 1) {
+    // The array keeps whatever the previous call left in it.  Only the
+    // split-K completion counters must start at zero; clear the ones this
+    // launch uses (partials are always written before they are read).
+    const int64_t units = static_cast<int64_t>(a.batch) * a.num_kv_heads * plan.sub_groups;
+    e = cudaMemsetAsync(scratch, 0, static_cast<size_t>(units) * sizeof(int32_t), stream);
+    if (e != cudaSuccess) return e;
+  }
+  DecodeLaunch b = a;
+  b.workspace = scratch;
+  b.workspace_bytes = PKV_DECODE_STATIC_SCRATCH_BYTES;
+  return launch_decode(b, src, plan, stream);
 }
 
 }  // namespace pkv

@@ -49,6 +49,10 @@ DecodePlan plan_decode(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
                        int32_t max_kv_len);
 cudaError_t launch_decode(const DecodeLaunch& a, const KVSource& src, const DecodePlan& plan,
                           cudaStream_t stream);
+// Same launch with the split-K scratch taken from the library's static device
+// array (per-device address set up on first use); see decode.cu.
+cudaError_t launch_decode_static(const DecodeLaunch& a, const KVSource& src,
+                                 const DecodePlan& plan, cudaStream_t stream);
 
 struct PrefillLaunch {
   const void* q;
