@@ -58,6 +58,12 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seqs", type=int, default=4, help="rows in the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-engine", action="store_true")
+    ap.add_argument("--engine-chats", type=int, default=16)
+    ap.add_argument("--engine-reply", type=int, default=64)
+    ap.add_argument("--engine-prompt", type=int, nargs=2, default=[32, 1000])
+    ap.add_argument("--engine-blocks", type=int, default=1024)
+    ap.add_argument("--no-engine-cpu", action="store_true")
     return ap.parse_args()
 
 
@@ -285,6 +291,163 @@ def cpu_info():
     return name
 
 
+# ---------------------------------------------------------------- engine
+WEIGHT_BYTES = None  # filled from the model's parameter count
+
+
+def random_init_(model, seed, std=0.02):
+    """Random-init weights: N(0, std) for weights and
+    biases, RMSNorm weights 1, generated on the model's device."""
+    g = torch.Generator(device=next(model.parameters()).device).manual_seed(seed)
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if name.endswith("layernorm.weight") or name == "norm.weight":
+                p.fill_(1.0)
+            else:
+                p.normal_(0.0, std, generator=g)
+
+
+class SyntheticTokenizer:
+    """Token ids stand in for text: message "p<i>" encodes to prompt i."""
+
+    encoder = {"<|endoftext|>": -1}  # never sampled: replies run their full length
+
+    def __init__(self, prompts):
+        self.prompts = prompts
+
+    def encode(self, text):
+        if text == "\n":
+            return [198]
+        i = int(text.split("User: p", 1)[1].split("\n", 1)[0])
+        return list(self.prompts[i])
+
+    def decode(self, ids):
+        return ""
+
+
+class _CountingModel:
+    """Forwards to the model and records (B, T, sum of kv lens) per call."""
+
+    def __init__(self, model, cache):
+        self.model, self.cache, self.calls = model, cache, []
+
+    @property
+    def _graphs(self):
+        return self.model._graphs
+
+    def __call__(self, input_ids, cache, seqs):
+        B, T = input_ids.shape
+        kv = sum(cache.length(s) for s in seqs) + B * T
+        self.calls.append((B, T, kv))
+        return self.model(input_ids, cache, seqs)
+
+
+def engine_run(args, device, seed=0):
+    """BASELINE config 2 through chat.py: N concurrent chats, uniform random
+    prompts, fixed-length replies (EOS and stop sequences off, as
+    metrics/benchmark_concurrency.py:122,143 does), temperature-1 sampling,
+    the reference's 1024-block (448 MB) pool.  Returns tok/s and a roofline."""
+    import chat
+    import model as M
+    from kv_cache import KVCache
+
+    torch.manual_seed(seed)
+    m = M.Qwen2ForCausalLM().to(device, torch.bfloat16).eval()
+    random_init_(m, seed + 11)
+    cache = KVCache(args.engine_blocks, 16, device, torch.bfloat16)
+    chat.init(kv_cache=cache, start_worker=False)
+    chat.STOP_SEQUENCES = []
+    chat.MAX_REPLY_TOKENS = args.engine_reply
+    runner = m.enable_decode_graphs(cache, max_batch=max(args.engine_chats, 1))
+    for b in runner.buckets:  # capture outside the timed region
+        runner._capture(b)
+    g = torch.Generator().manual_seed(seed + 5)
+    lo, hi = args.engine_prompt
+    n = args.engine_chats
+    prompts = [torch.randint(0, M.VOCAB_SIZE, (int(torch.randint(lo, hi + 1, (1,), generator=g)),),
+                             generator=g).tolist() for _ in range(n + 1)]
+    tok = SyntheticTokenizer(prompts)
+    cm = _CountingModel(m, cache)
+
+    def one_round(idx, reply):
+        chat.MAX_REPLY_TOKENS = reply
+        chats = []
+        for i in idx:
+            c = chat.Chat(tok)
+            c.eos_id = -1
+            c.submit(cm, f"p{i}")
+            chats.append(c)
+        t0 = time.perf_counter()
+        chat.run_until_idle()
+        torch.cuda.synchronize()
+        el = time.perf_counter() - t0
+        toks = sum(len(c.ids) - len(tok.prompts[i]) - 1 for c, i in zip(chats, idx))
+        for c in chats:
+            c.release()
+        return el, toks
+
+    one_round([n], 4)  # warm-up: eager prefill path, sampling, one graph bucket
+    cm.calls.clear()
+    el, toks = one_round(list(range(n)), args.engine_reply)
+    torch.cuda.synchronize()
+    nparams = sum(p.numel() for p in m.parameters())
+    wbytes = nparams * 2
+    peaks, _ = measured_peaks()
+    bw = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS)) * 1e9
+    flops_peak = float(peaks.get("bf16_tflops", 1590.0)) * 1e12
+    kv_tok = L * 2 * HKV * D * 2
+    t_roof = 0.0
+    decode_steps = prefills = 0
+    for B, T, kv in cm.calls:
+        if T == 1:
+            decode_steps += 1
+            t_roof += (wbytes + kv * kv_tok) / bw
+        else:
+            prefills += 1
+            t_roof += max(2 * nparams * B * T / flops_peak, (wbytes + kv * kv_tok) / bw)
+    chat._kv_cache = None
+    del runner, m, cache
+    torch.cuda.empty_cache()
+    return {"tok_s": round(toks / el, 1), "tokens": toks, "wall_s": round(el, 4),
+            "decode_steps": decode_steps, "prefills": prefills,
+            "roofline_tok_s": round(toks / t_roof, 1), "frac": round(t_roof / el, 4),
+            "roofline_basis": "per call: decode = (weights + KV read) / measured HBM; "
+                              "prefill = max(2*params*tokens / measured bf16 peak, bytes / HBM)",
+            "config": f"config2: {n} chats, prompts U[{lo},{hi}] random ids, "
+                      f"{args.engine_reply}-token replies, {args.engine_blocks}-block pool, "
+                      f"random-init bf16 Qwen2.5-1.5B (std 0.02), temperature-1 sampling, "
+                      f"one prefill per tick (chat.py), CUDA-graph decode"}
+
+
+def engine_cpu_sample(seconds_budget=60.0):
+    """The reference engine's own CPU path (restated model + gather/SDPA cache,
+    fp32, chat.py's CPU dtype) on a bounded sample: 2 chats, 32-token prompts,
+    4-token replies, batched decode."""
+    from oracle.kvcache_ref import RefKVCache
+    from oracle.model_ref import RefQwen2
+
+    torch.manual_seed(0)
+    m = RefQwen2().eval()
+    random_init_(m, 11)
+    cache = RefKVCache(16, 16, torch.float32)
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, 151936, (32,), generator=g).tolist() for _ in range(2)]
+    seqs = [cache.alloc(), cache.alloc()]
+    t0 = time.perf_counter()
+    nxt = []
+    for r in range(2):
+        lg = m(torch.tensor([prompts[r]]), cache, [seqs[r]])[:, -1]
+        nxt.append(int(torch.multinomial(torch.softmax(lg.float(), -1), 1)[0]))
+    toks = 2
+    for _ in range(3):
+        lg = m(torch.tensor([[x] for x in nxt]), cache, seqs)[:, -1]
+        nxt = torch.multinomial(torch.softmax(lg.float(), -1), 1)[:, 0].tolist()
+        toks += 2
+    el = time.perf_counter() - t0
+    return {"tok_s": round(toks / el, 3), "cores": torch.get_num_threads(), "kind": "port",
+            "sample": "2 chats, 32-token prompts, 4-token replies, fp32 torch CPU (prefill included)"}
+
+
 # ---------------------------------------------------------------- main
 def main():
     args = parse()
@@ -358,6 +521,7 @@ def main():
         torch.distributed.all_reduce(ms_all, op=torch.distributed.ReduceOp.MAX)
     ms_max = float(ms_all.item())
     total_bytes = w.step_bytes() * world
+    step_bytes, bytes_decode, layers = w.step_bytes(), w.bytes_decode, w.layers
     value = total_bytes / (ms_max * 1e-3) / 1e9
 
     e2e = None
@@ -370,13 +534,28 @@ def main():
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": round(float(e_all.item()), 3)}
 
+    engine = None
+    if not args.no_engine:
+        del w
+        torch.cuda.empty_cache()
+        engine = engine_run(args, dev, seed=args.seed + rank)
+        tok_all = torch.tensor([engine["tok_s"]], device=dev, dtype=torch.float64)
+        if world > 1:
+            torch.distributed.all_reduce(tok_all)
+        engine["tok_s_all_gpus"] = round(float(tok_all.item()), 1)
+        engine["n_gpus"] = world
+        engine["scaling"] = "weak (each GPU serves its own chats)"
+        if rank == 0 and world == 1 and not args.no_engine_cpu:
+            torch.set_num_threads(os.cpu_count() or 1)
+            engine["cpu_baseline"] = engine_cpu_sample()
+
     peaks, src = measured_peaks()
     peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
-    achieved = w.bytes_decode / (kern_ms * 1e-3) / 1e9
+    achieved = bytes_decode / (kern_ms * 1e-3) / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": src,
                 "frac_of_nominal_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
-                "kernel": "paged_decode_kernel", "bytes_per_launch": w.bytes_decode,
+                "kernel": "paged_decode_kernel", "bytes_per_launch": bytes_decode,
                 "avg_launch_ms": round(kern_ms, 4),
                 "traffic": None}
     prof = REPO / "profiles" / "decode_traffic.json"
@@ -402,8 +581,8 @@ def main():
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic", "config": config, "roofline": roofline,
                 "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
-                "gpu_launches": args.steps * w.layers * 2 * 1,
-                "kv_bytes_per_step": w.step_bytes()}
+                "gpu_launches": args.steps * layers * 2,
+                "kv_bytes_per_step": step_bytes, "engine": engine}
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()

@@ -78,6 +78,8 @@ const char* pkv_last_error(void);
  *   - roped k and plain v go to the pool slot of (row b, pos).
  * With rope_cos == NULL the call is exactly KVCache.write (k/v copied as-is,
  * q ignored).  q, k, v are [B][H][T][128] with strides (sb, sh, st).
+ * A row with starts[b] < 0 is an inactive padding row (e.g. a batch padded
+ * to a captured size): nothing is read, rotated or stored for it.
  */
 int pkv_append_rope(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
                     const void* k, int64_t k_sb, int64_t k_sh, int64_t k_st,

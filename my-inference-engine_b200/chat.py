@@ -1,0 +1,390 @@
+"""Continuous-batching scheduler on the device-table KV cache (drop-in for the
+reference's chat.py:1-377).
+
+Every scheduling decision is the reference's, in the same order and with the
+same module-level names (the reference's benchmark monkey-patches `_admit`,
+`_finish`, `STOP_SEQUENCES`, `MAX_REPLY_TOKENS` on this module):
+  * a message reserves history + prompt + MAX_REPLY_TOKENS + trailing "\\n"
+    blocks up front (chat.py:117-125) and is rejected if that can never fit
+    (chat.py:214-229);
+  * idle chats are evicted least-recently-used first under `_cache_lock`
+    until the new message fits, else it is deferred (chat.py:128-146);
+  * at most one prefill per worker tick (chat.py:232-254), then one batched
+    decode step for every active job with a single device sync for sampling
+    (chat.py:257-308, :103-107);
+  * `_finish` trims unused reserved blocks (chat.py:194-211); `Chat.release`
+    frees a chat's blocks from a request thread (chat.py:325-330).
+What changes is underneath: the cache's block tables live on the device, the
+decode step can replay a captured CUDA graph (model.DecodeGraphs), and
+nothing is allocated or started at import -- `KV_CACHE` is created on first
+use and the worker thread on the first message (`init()` sets both up
+explicitly).
+"""
+from __future__ import annotations
+
+import queue
+import threading
+import time
+
+import torch
+import torch.nn.functional as F
+
+from kv_cache import KVCache
+from model import Qwen2ForCausalLM
+
+MODEL_PATH = "./qwen2.5-1.5b"
+MAX_REPLY_TOKENS = 512  # safety net against a reply that never hits EOS
+TEMPERATURE = 1
+
+BLOCK_SIZE = 16
+KV_CACHE_TOKENS = 8 * 2048  # the reference's 448 MB budget (1024 blocks)
+MAX_SEQ_LEN = 2048
+
+DEVICE = torch.device("cuda")
+DTYPE = torch.bfloat16
+
+_kv_cache = None
+
+
+def _kv():
+    global _kv_cache
+    if _kv_cache is None:
+        _kv_cache = KVCache(KV_CACHE_TOKENS // BLOCK_SIZE, BLOCK_SIZE, DEVICE, dtype=DTYPE)
+    return _kv_cache
+
+
+def __getattr__(name):  # module attribute KV_CACHE, created on first access
+    if name == "KV_CACHE":
+        return _kv()
+    raise AttributeError(name)
+
+
+def init(kv_cache=None, start_worker=True):
+    """Install a cache (default: the reference's 1024-block budget) and start
+    the worker thread now instead of on the first message."""
+    global _kv_cache
+    if kv_cache is not None:
+        _kv_cache = kv_cache
+    _kv()
+    if start_worker:
+        _ensure_worker()
+    return _kv_cache
+
+
+def load_qwen(model_path):
+    from safetensors.torch import load_file
+
+    model = Qwen2ForCausalLM()
+    state_dict = load_file(f"{model_path}/model.safetensors")
+    state_dict = {k.removeprefix("model."): v for k, v in state_dict.items()}
+    model.load_state_dict(state_dict)
+    model.eval()
+    return model.to(DEVICE, dtype=DTYPE)
+
+
+STOP_SEQUENCES = ["\nUser:", "\nUser"]
+
+
+def _overlap_len(text, patterns):
+    """Length of the longest suffix of `text` that could still grow into any of `patterns`."""
+    best = 0
+    for pattern in patterns:
+        for k in range(min(len(text), len(pattern) - 1), 0, -1):
+            if text.endswith(pattern[:k]):
+                best = max(best, k)
+                break
+    return best
+
+
+def _find_stop(text, patterns):
+    """The earliest-starting stop pattern found in `text`, or None."""
+    best = None
+    for pattern in patterns:
+        i = text.find(pattern)
+        if i != -1 and (best is None or i < text.find(best)):
+            best = pattern
+    return best
+
+
+def generate(model, new_ids, eos_id, max_tokens=MAX_REPLY_TOKENS):
+    """Single-sequence generation loop with its own private cache (chat.py:72-88)."""
+    cache = KVCache(MAX_SEQ_LEN // BLOCK_SIZE, BLOCK_SIZE, DEVICE, dtype=next(model.parameters()).dtype)
+    seq = cache.alloc()
+    next_id = new_ids
+    is_first = True
+    for _ in range(max_tokens):
+        with torch.no_grad():
+            input_id = torch.tensor([next_id] if is_first else [[next_id]], device=DEVICE)
+            is_first = False
+            logits = model(input_id, cache, [seq])
+        next_id = _sample(logits[:, -1])[0]
+        yield next_id
+        if next_id == eos_id:
+            break
+
+
+class _Job:
+    def __init__(self, chat, model, text, out_queue):
+        self.chat = chat
+        self.model = model
+        self.text = text
+        self.out_queue = out_queue
+        self.buffer = ""
+        self.steps = 0
+        self.next_token = None
+        self.new_ids = chat.tokenizer.encode(f"User: {text}\nAssistant:")
+
+
+def _sample(logits):
+    """One token id per row of [B, vocab] logits, one device sync for the batch."""
+    probs = F.softmax(logits.float() / TEMPERATURE, dim=-1)
+    return torch.multinomial(probs, num_samples=1).squeeze(1).tolist()
+
+
+_job_queue = queue.Queue()
+active = []
+_deferred = []
+_resident = []
+_cache_lock = threading.Lock()
+_worker_thread = None
+_worker_lock = threading.Lock()
+
+
+def _reserve_len(job):
+    trailing = len(job.chat.tokenizer.encode("\n"))
+    return len(job.chat.ids) + len(job.new_ids) + MAX_REPLY_TOKENS + trailing
+
+
+def _blocks_needed(job):
+    return _kv().blocks_needed(job.chat.seq, _reserve_len(job))
+
+
+def _evict(chat):
+    _kv().free(chat.seq)
+    chat.seq = None
+    _resident.remove(chat)
+
+
+def _make_room(job):
+    busy = {j.chat for j in active} | {job.chat}
+    with _cache_lock:
+        while _blocks_needed(job) > _kv().free_block_count():
+            idle = [c for c in _resident if c not in busy]
+            if not idle:
+                return False
+            _evict(idle[0])
+    return True
+
+
+def _touch(chat):
+    with _cache_lock:
+        if chat in _resident:
+            _resident.remove(chat)
+        _resident.append(chat)
+
+
+def _admit(job):
+    """Prefill one job (chat.py:157-185)."""
+    chat, model, text = job.chat, job.model, job.text
+    cache = _kv()
+    reserve_len = _reserve_len(job)
+    chat.pending.remove(text)
+    chat.messages.append(("user", text))
+    chat.ids.extend(job.new_ids)
+    chat.listeners = [job.out_queue]
+    chat.in_progress = ""
+    if chat.seq is None:
+        chat.seq = cache.alloc()
+    prefill_ids = chat.ids[cache.length(chat.seq):]
+    cache.ensure_capacity(chat.seq, reserve_len)
+    _touch(chat)
+    input_ids = torch.tensor([prefill_ids], device=DEVICE)
+    with torch.no_grad():
+        logits = model(input_ids, cache, [chat.seq])
+    job.next_token = _sample(logits[:, -1])[0]
+    active.append(job)
+
+
+def _emit(job, piece):
+    job.chat.in_progress += piece
+    for q in job.chat.listeners:
+        q.put(piece)
+
+
+def _finish(job):
+    chat = job.chat
+    chat.ids.extend(chat.tokenizer.encode("\n"))
+    with _cache_lock:
+        _kv().trim(chat.seq)
+    _touch(chat)
+    chat.messages.append(("assistant", chat.in_progress))
+    chat.in_progress = None
+    for q in chat.listeners:
+        q.put(None)
+    chat.listeners = []
+    active.remove(job)
+
+
+def _reject(job, reason):
+    job.chat.pending.remove(job.text)
+    job.out_queue.put(f"[error: {reason}]")
+    job.out_queue.put(None)
+
+
+def _try_admit_or_defer(job):
+    cache = _kv()
+    if cache.blocks_needed(None, _reserve_len(job)) > cache.num_blocks:
+        _reject(job, "conversation is too long for the KV cache")
+    elif _make_room(job):
+        _admit(job)
+    else:
+        _deferred.append(job)
+
+
+def _tick(block=True):
+    """One pass of the worker loop (chat.py:232-254).  Returns False when there
+    was nothing to do and `block` is False."""
+    for job in list(_deferred):
+        if _make_room(job):
+            _deferred.remove(job)
+            _admit(job)
+    if not active and not _deferred:
+        if not block and _job_queue.empty():
+            return False
+        _try_admit_or_defer(_job_queue.get())
+    elif not active and _deferred:
+        time.sleep(0.05)
+    elif not _job_queue.empty():
+        _try_admit_or_defer(_job_queue.get())
+    _process(active)
+    return True
+
+
+def _worker():
+    while True:
+        _tick(block=True)
+
+
+def run_until_idle():
+    """Drive the worker loop on the calling thread until every queued,
+    deferred and active job is done (deterministic, for benchmarks/tests)."""
+    while _tick(block=False) or active or _deferred:
+        pass
+
+
+def _ensure_worker():
+    global _worker_thread
+    with _worker_lock:
+        if _worker_thread is None:
+            _worker_thread = threading.Thread(target=_worker, daemon=True)
+            _worker_thread.start()
+
+
+def _process(active):
+    """One decode step for every job currently active, in FIFO order."""
+    continuing = []
+    for job in list(active):
+        chat = job.chat
+        token_id = job.next_token
+        chat.ids.append(token_id)
+
+        if token_id == chat.eos_id:
+            _finish(job)
+            continue
+
+        job.buffer += chat.tokenizer.decode([token_id])
+        stop = _find_stop(job.buffer, STOP_SEQUENCES)
+        if stop is not None:
+            job.buffer = job.buffer.split(stop)[0]
+            if job.buffer:
+                _emit(job, job.buffer)
+            _finish(job)
+            continue
+
+        overlap = _overlap_len(job.buffer, STOP_SEQUENCES)
+        release, job.buffer = job.buffer[:len(job.buffer) - overlap], job.buffer[len(job.buffer) - overlap:]
+        if release:
+            _emit(job, release)
+
+        job.steps += 1
+        if job.steps >= MAX_REPLY_TOKENS:
+            if job.buffer:
+                _emit(job, job.buffer)
+            _finish(job)
+            continue
+
+        continuing.append(job)
+
+    if not continuing:
+        return
+
+    model = continuing[0].model
+    seqs = [job.chat.seq for job in continuing]
+    # host tensor: the decode graph copies ids with the step's other inputs
+    input_ids = torch.tensor([[job.next_token] for job in continuing])
+    if not getattr(model, "_graphs", None):
+        input_ids = input_ids.to(DEVICE)
+    with torch.no_grad():
+        logits = model(input_ids, _kv(), seqs)
+
+    for job, token_id in zip(continuing, _sample(logits[:, -1])):
+        job.next_token = token_id
+
+
+class Chat:
+    def __init__(self, tokenizer):
+        self.tokenizer = tokenizer
+        self.ids = []
+        self.seq = None
+        self.messages = []
+        self.pending = []
+        self.in_progress = None
+        self.listeners = []
+        self.eos_id = tokenizer.encoder["<|endoftext|>"]
+
+    def release(self):
+        """Free this chat's KV-cache blocks, if it holds any."""
+        with _cache_lock:
+            if self.seq is not None:
+                _evict(self)
+
+    def submit(self, model, text):
+        """Queue a message without starting the worker thread; returns the
+        queue its reply pieces (then None) arrive on."""
+        self.pending.append(text)
+        out_queue = queue.Queue()
+        _job_queue.put(_Job(self, model, text, out_queue))
+        return out_queue
+
+    def send_stream(self, model, text):
+        """Yield decoded reply pieces as they are generated (chat.py:332-348)."""
+        out_queue = self.submit(model, text)
+        _ensure_worker()
+        while True:
+            piece = out_queue.get()
+            if piece is None:
+                break
+            yield piece
+
+    def all_messages(self):
+        result = list(self.messages)
+        if self.in_progress is not None:
+            result.append(("assistant", self.in_progress))
+        result.extend(("user", text) for text in self.pending)
+        return result
+
+    def watch(self):
+        if self.in_progress is None:
+            return None, None
+        q = queue.Queue()
+        self.listeners.append(q)
+        return self.in_progress, q
+
+    def send(self, model, text):
+        for piece in self.send_stream(model, text):
+            print(piece, end="", flush=True)
+        print()
+        return self.messages[-1][1]
+
+    def transcript(self):
+        return self.tokenizer.decode(self.ids)

@@ -43,7 +43,9 @@ __global__ void __launch_bounds__(256) append_rope_kernel(const AppendLaunch a, 
   const int b = static_cast<int>(bt / a.seq_len_q);
   const DevErr err{a.err};
 
-  const int pos = a.starts[b] + tt;
+  const int start = a.starts[b];
+  if (start < 0) return;  // inactive (padding) row: nothing to rotate or store
+  const int pos = start + tt;
   const bool rope = a.rope_cos != nullptr;
   const int nq = a.q_out ? a.num_q_heads : 0;
 

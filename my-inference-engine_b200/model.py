@@ -148,11 +148,15 @@ class Qwen2ForCausalLM(torch.nn.Module):
         inv_freq = 1.0 / (ROPE_THETA ** (torch.arange(0, HEAD_DIM, 2).float() / HEAD_DIM))
         self.register_buffer("inv_freq", inv_freq, persistent=False)
         self._rope = {}  # (device, dtype) -> (cos, sin) tables
+        self._rope_retired = []  # outgrown tables stay alive: captured graphs may point at them
+        self._graphs = {}  # id(cache) -> DecodeGraphs
 
     def rope_tables(self, num_positions, dtype, device):
         key = (str(device), dtype)
         tab = self._rope.get(key)
         if tab is None or tab[0].shape[0] < num_positions:
+            if tab is not None:
+                self._rope_retired.append(tab)
             n = max(num_positions, 2 * (tab[0].shape[0] if tab is not None else 0), 4096)
             tab = rope_table(n, dtype, device)
             self._rope[key] = tab
@@ -160,20 +164,118 @@ class Qwen2ForCausalLM(torch.nn.Module):
 
     def forward(self, input_ids, cache, seqs):
         """input_ids: [B, T]. cache: a KVCache. seqs: that cache's sequence id for
-        each batch item.  Returns logits for each row's last position: [B, 1, vocab]."""
+        each batch item.  Returns logits for each row's last position: [B, 1, vocab].
+
+        A T == 1 step for which decode graphs were enabled (enable_decode_graphs)
+        replays a captured CUDA graph; everything else runs eagerly."""
         _, T = input_ids.shape
-        x = self.embed_tokens(input_ids)
-
+        runner = self._graphs.get(id(cache)) if T == 1 else None
+        if runner is not None and runner.covers(len(seqs)):
+            return runner.run(input_ids, seqs)[:, None]
         starts_list, slot_mapping, gather_idx = cache.prepare(seqs, T)
-        cos, sin = self.rope_tables(cache.table_pitch * cache.block_size, x.dtype, x.device)
-        kv_lens = gather_idx.kv_lens
-        is_causal = T > 1  # a single query row sees every key up to kv_lens anyway
-
-        for layer_idx, layer in enumerate(self.layers):
-            x = layer(x, cos, sin, None, is_causal, kv_lens, cache, layer_idx, slot_mapping, gather_idx)
-
+        logits = self.forward_step(input_ids, cache, gather_idx)
         cache.advance(seqs, T)
-
-        x = self.norm(x[:, -1:])
-        logits = x @ self.embed_tokens.weight.T
         return logits
+
+    def forward_step(self, input_ids, cache, step):
+        """Device-only part of forward(): embeddings, 28 layers over the step's
+        device tables, last-position logits.  No host synchronisation, so it can
+        be captured in a CUDA graph for a fixed batch."""
+        T = input_ids.shape[1]
+        x = self.embed_tokens(input_ids)
+        cos, sin = self.rope_tables(cache.table_pitch * cache.block_size, x.dtype, x.device)
+        kv_lens = step.kv_lens
+        is_causal = T > 1  # a single query row sees every key up to kv_lens anyway
+        for layer_idx, layer in enumerate(self.layers):
+            x = layer(x, cos, sin, None, is_causal, kv_lens, cache, layer_idx, step, step)
+        x = self.norm(x[:, -1:])
+        return x @ self.embed_tokens.weight.T
+
+    # ---- CUDA-graph decode ----
+    def enable_decode_graphs(self, cache, max_batch=256):
+        """Capture the T == 1 forward per batch bucket (lazily, on first use)."""
+        self._graphs[id(cache)] = DecodeGraphs(self, cache, max_batch)
+        return self._graphs[id(cache)]
+
+
+def _buckets(max_batch):
+    b, out = 1, []
+    while b < max_batch:
+        out.append(b)
+        b = b * 2 if b < 16 else b + 16
+    out.append(max_batch)
+    return out
+
+
+class DecodeGraphs:
+    """CUDA graphs of the batched one-token forward, one per batch bucket.
+
+    Graph inputs are four int32 device vectors per bucket (token id, table
+    row, start, kv_len); a step fills them with ONE host-to-device copy from
+    pinned memory and replays the graph, so a decode step costs one copy, one
+    replay and the sampling that follows (chat.py:_process) instead of ~600
+    eager launches.  Rows beyond the live batch are inactive padding (start
+    -1, kv_len 0): the append kernel skips them and attention writes NaN for
+    them, which the caller never reads.  The decode kernels are captured with
+    max_kv_len = the cache's per-sequence capacity; partitions past a row's
+    length exit at once.
+    """
+
+    def __init__(self, model, cache, max_batch):
+        self.model, self.cache = model, cache
+        self.max_batch = min(max_batch, cache.max_seqs)
+        self.buckets = _buckets(self.max_batch)
+        self.graphs = {}
+        self.pool = torch.cuda.graph_pool_handle()
+        self.capacity = cache.table_pitch * cache.block_size
+
+    def covers(self, B):
+        return 0 < B <= self.max_batch
+
+    def _bucket(self, B):
+        return next(b for b in self.buckets if b >= B)
+
+    def _capture(self, Bp):
+        from kv_cache import PagedStep
+
+        dev = self.cache.device
+        ins = torch.zeros(4, Bp, dtype=torch.int32, device=dev)
+        ins[2].fill_(-1)
+        step = PagedStep(self.cache, 1, [0] * Bp, ins[1], ins[2], ins[3], self.capacity)
+        host = torch.empty(4, Bp, dtype=torch.int32, pin_memory=True)
+        # warm up on a side stream (lazy library / workspace set-up happens here)
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self.model.forward_step(ins[0].view(Bp, 1).long(), self.cache, step)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=self.pool):
+            logits = self.model.forward_step(ins[0].view(Bp, 1).long(), self.cache, step)
+        self.graphs[Bp] = (g, ins, host, logits)
+        return self.graphs[Bp]
+
+    def run(self, input_ids, seqs):
+        B = len(seqs)
+        Bp = self._bucket(B)
+        g, ins, host, logits = self.graphs.get(Bp) or self._capture(Bp)
+        starts, rows = self.cache.step_rows(seqs, 1)
+        self.cache.flush_tables()
+        if not input_ids.is_cuda:
+            host[0, :B] = input_ids.view(-1).to(torch.int32)
+        st = torch.tensor(starts, dtype=torch.int32)
+        host[1, :B] = torch.tensor(rows, dtype=torch.int32)
+        host[2, :B] = st
+        host[3, :B] = st + 1
+        if Bp > B:
+            host[0, B:] = 0
+            host[1, B:] = 0
+            host[2, B:] = -1
+            host[3, B:] = 0
+        ins.copy_(host, non_blocking=True)
+        if input_ids.is_cuda:  # device ids: a device-side copy, no host sync
+            ins[0, :B].copy_(input_ids.view(-1))
+        g.replay()
+        self.cache.advance(seqs, 1)
+        return logits[:B, 0]

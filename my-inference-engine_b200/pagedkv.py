@@ -105,6 +105,7 @@ def _stream(device: torch.device) -> int:
 
 # ---------------------------------------------------------------- workspace
 _workspaces: dict[int, torch.Tensor] = {}
+_retired_workspaces: list[torch.Tensor] = []  # outgrown buffers stay alive (captured graphs)
 
 
 def decode_workspace(batch: int, num_q_heads: int, num_kv_heads: int, max_kv_len: int,
@@ -121,6 +122,8 @@ def decode_workspace(batch: int, num_q_heads: int, num_kv_heads: int, max_kv_len
     idx = device.index if device.index is not None else torch.cuda.current_device()
     ws = _workspaces.get(idx)
     if ws is None or ws.numel() < need:
+        if ws is not None:
+            _retired_workspaces.append(ws)
         size = max(need, 2 * (ws.numel() if ws is not None else 0))
         ws = torch.zeros(size, dtype=torch.uint8, device=torch.device("cuda", idx))
         _workspaces[idx] = ws

@@ -21,6 +21,8 @@ records the exact reference call sequence it came from:
                        model's SDPA branch in fp32 (model.py:104-107).
   prefill_config1.npz  BASELINE config 1 (reduced to 3 rows for size): ragged
                        causal prefill + append into a shuffled pool.
+  scheduler_trace.json chat.py's scheduler (chat.py:110-311) driven tick by tick
+                       with a fake model/tokenizer (oracle.scheduler_trace).
   model_greedy.json    Qwen2ForCausalLM (fp32, CPU, SDPA branch) with
                        oracle.weights.random_state_dict(seed) weights: greedy
                        ids of a 2-row batched prefill + decode through
@@ -305,6 +307,24 @@ def gen_model_greedy(model_mod, kv_cache_mod, seed=2024):
     return {"seed": seed, "prompts": prompts, "steps": steps, "ids": ids, "margins": margins}
 
 
+# ---------------------------------------------------------------- scheduler
+def gen_scheduler_trace(reference):
+    """The reference chat.py's own scheduling functions (admission, deferral,
+    LRU eviction, one prefill per tick, batched decode, trim, release) driven
+    deterministically by oracle.scheduler_trace."""
+    import chat as chat_mod  # the reference's chat.py (CPU: fp32 cache, worker idle)
+    import kv_cache as kv_cache_mod
+    from oracle.scheduler_trace import run_trace
+
+    assert Path(chat_mod.__file__).resolve().parent == Path(reference).resolve()
+
+    def install(num_blocks):
+        chat_mod.KV_CACHE = kv_cache_mod.KVCache(num_blocks, 16, "cpu", torch.float32)
+        return chat_mod.KV_CACHE
+
+    return run_trace(chat_mod, install)
+
+
 def main():
     sys.path.insert(0, str(REPO))
     ap = argparse.ArgumentParser()
@@ -318,7 +338,7 @@ def main():
     assert Path(model_mod.__file__).resolve().parent == Path(a.reference).resolve(), \
         "imported the wrong model module"
     torch.set_num_threads(8)
-    want = (a.only or "kvcache,rope,attn,dec0,pre1,model").split(",")
+    want = (a.only or "kvcache,rope,attn,dec0,pre1,model,sched").split(",")
     if "kvcache" in want:
         (HERE / "kvcache_ops.json").write_text(json.dumps(gen_kvcache_ops(kv_cache_mod)))
     if "rope" in want:
@@ -331,6 +351,8 @@ def main():
         np.savez_compressed(HERE / "prefill_config1.npz", **gen_prefill_config1(model_mod, kv_cache_mod))
     if "model" in want:
         (HERE / "model_greedy.json").write_text(json.dumps(gen_model_greedy(model_mod, kv_cache_mod)))
+    if "sched" in want:
+        (HERE / "scheduler_trace.json").write_text(json.dumps(gen_scheduler_trace(a.reference)))
     print("wrote", ", ".join(want))
 
 

@@ -1,0 +1,109 @@
+"""The engine on the GPU: CUDA-graph decode steps give the eager forward's
+logits, and chat.py's scheduler drives the real model through prefill,
+batched graph decode, deferral and eviction to completion."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def small_model(cuda):
+    import model as M
+
+    torch.manual_seed(0)
+    m = M.Qwen2ForCausalLM().to(cuda, torch.bfloat16).eval()
+    g = torch.Generator(device=cuda).manual_seed(3)
+    with torch.no_grad():
+        for name, p in m.named_parameters():
+            if name.endswith("layernorm.weight") or name == "norm.weight":
+                p.fill_(1.0)
+            else:
+                p.normal_(0.0, 0.02, generator=g)
+    return m
+
+
+def test_decode_graph_matches_eager(cuda, small_model):
+    from kv_cache import KVCache
+
+    m = small_model
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, 151936, (n,), generator=g).tolist() for n in (5, 40, 17)]
+    caches, logits = [], []
+    for use_graph in (False, True):
+        c = KVCache(64, 16, cuda, torch.bfloat16)
+        if use_graph:
+            m.enable_decode_graphs(c, max_batch=4)
+        seqs = [c.alloc() for _ in prompts]
+        with torch.no_grad():
+            for s, p in zip(seqs, prompts):
+                m(torch.tensor([p], device=cuda), c, [s])
+            out = []
+            ids = [[11], [12], [13]]
+            for step in range(5):
+                lg = m(torch.tensor(ids), c, seqs)[:, -1].float()
+                out.append(lg)
+                ids = [[int(x)] for x in lg.argmax(-1).tolist()]
+        torch.cuda.synchronize()
+        c.check_errors()
+        caches.append(c)
+        logits.append(out)
+    m._graphs.clear()
+    for a, b in zip(*logits):
+        assert float((a - b).abs().max()) < 0.05
+        assert torch.equal(a.argmax(-1), b.argmax(-1))
+    # the pools hold the same K/V up to split-K rounding, and the graph's
+    # padding rows wrote nothing: blocks no sequence owns are still zero
+    assert float((caches[0].buf.float() - caches[1].buf.float()).abs().max()) < 0.05
+    c = caches[1]
+    used = {b for t in c._block_tables.values() for b in t}
+    unused = [b for b in range(c.num_blocks) if b not in used]
+    view = c.buf.view(c.buf.shape[0], 2, c.num_blocks, 16, -1)
+    assert int(view[:, :, unused].count_nonzero()) == 0
+
+
+def test_engine_serves_chats_with_eviction(cuda, small_model):
+    import chat
+    from kv_cache import KVCache
+
+    class Tok:
+        encoder = {"<|endoftext|>": -1}
+
+        def encode(self, text):
+            if text == "\n":
+                return [198]
+            body = text.split("User: ", 1)[1].split("\n", 1)[0]
+            return [100 + (ord(ch) * 7 + i) % 5000 for i, ch in enumerate(body)]
+
+        def decode(self, ids):
+            return "."
+
+    m = small_model
+    cache = KVCache(40, 16, cuda, torch.bfloat16)
+    chat.init(kv_cache=cache, start_worker=False)
+    m.enable_decode_graphs(cache, max_batch=8)
+    saved = (chat.MAX_REPLY_TOKENS, chat.STOP_SEQUENCES)
+    chat.MAX_REPLY_TOKENS = 24
+    chat.STOP_SEQUENCES = []
+    try:
+        tok = Tok()
+        chats = [chat.Chat(tok) for _ in range(6)]
+        texts = ["a" * 30, "b" * 120, "c" * 60, "d" * 5, "e" * 200, "f" * 90]
+        qs = [c.submit(m, t) for c, t in zip(chats, texts)]
+        chat.run_until_idle()
+        # second turns: the pool (640 tokens) cannot hold everyone -> LRU eviction
+        qs2 = [c.submit(m, "second turn " + t[:20]) for c, t in zip(chats, texts)]
+        chat.run_until_idle()
+        torch.cuda.synchronize()
+        cache.check_errors()
+        for q in qs + qs2:
+            pieces = []
+            while not q.empty():
+                pieces.append(q.get())
+            assert pieces[-1] is None and len(pieces) == 24 + 1  # 24 tokens, then done
+        for c in chats:
+            assert len(c.messages) == 4
+    finally:
+        chat.MAX_REPLY_TOKENS, chat.STOP_SEQUENCES = saved
+        chat._kv_cache = None
+        m._graphs.clear()
