@@ -338,8 +338,12 @@ class _CountingModel:
     def __call__(self, input_ids, cache, seqs):
         B, T = input_ids.shape
         kv = sum(cache.length(s) for s in seqs) + B * T
-        self.calls.append((B, T, kv))
-        return self.model(input_ids, cache, seqs)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        out = self.model(input_ids, cache, seqs)
+        e1.record()
+        self.calls.append((B, T, kv, e0, e1))
+        return out
 
 
 def engine_run(args, device, seed=0):
@@ -398,18 +402,25 @@ def engine_run(args, device, seed=0):
     kv_tok = L * 2 * HKV * D * 2
     t_roof = 0.0
     decode_steps = prefills = 0
-    for B, T, kv in cm.calls:
+    gpu_decode = gpu_prefill = 0.0
+    for B, T, kv, e0, e1 in cm.calls:
+        ms = e0.elapsed_time(e1)
         if T == 1:
             decode_steps += 1
+            gpu_decode += ms
             t_roof += (wbytes + kv * kv_tok) / bw
         else:
             prefills += 1
+            gpu_prefill += ms
             t_roof += max(2 * nparams * B * T / flops_peak, (wbytes + kv * kv_tok) / bw)
     chat._kv_cache = None
     del runner, m, cache
     torch.cuda.empty_cache()
     return {"tok_s": round(toks / el, 1), "tokens": toks, "wall_s": round(el, 4),
             "decode_steps": decode_steps, "prefills": prefills,
+            "model_ms": {"decode_total": round(gpu_decode, 2), "prefill_total": round(gpu_prefill, 2),
+                         "decode_per_step": round(gpu_decode / max(decode_steps, 1), 3),
+                         "note": "CUDA events around each model call on the stream"},
             "roofline_tok_s": round(toks / t_roof, 1), "frac": round(t_roof / el, 4),
             "roofline_basis": "per call: decode = (weights + KV read) / measured HBM; "
                               "prefill = max(2*params*tokens / measured bf16 peak, bytes / HBM)",

@@ -163,6 +163,29 @@ int pkv_dense_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
                         int32_t* err_flag, void* stream);
 
 /*
+ * Residual add + RMSNorm of the Qwen2 block, one launch.
+ *
+ * Replaces `x = x + sublayer_out` (model.py:136-137) followed by RMSNorm
+ * (model.py:49-55) with the reference's rounding: h = bf16(resid + a);
+ * out = bf16(weight * bf16(h * rsqrt(mean(h*h) + eps))), the mean and rsqrt
+ * in fp32.  resid == NULL normalises `a` alone; resid_out (nullable, may
+ * equal resid) receives h.  Rows of `dim` bf16 (dim % 8 == 0, <= 4096)
+ * with element row strides; 16-byte aligned rows.
+ */
+int pkv_add_rmsnorm(const void* a, int64_t a_stride, const void* resid, int64_t r_stride,
+                    void* resid_out, int64_t ro_stride, const void* weight, void* out,
+                    int64_t o_stride, int32_t rows, int32_t dim, float eps, void* stream);
+
+/*
+ * SwiGLU activation: out = bf16(bf16(silu(gate)) * up) where each row of `gu`
+ * is [gate (inter) | up (inter)] -- the output of one merged gate/up GEMM.
+ * Replaces F.silu(gate_proj(x)) * up_proj(x) (model.py:120) around the GEMMs.
+ * inter % 8 == 0; 16-byte aligned rows.
+ */
+int pkv_silu_mul(const void* gu, int64_t gu_stride, void* out, int64_t o_stride, int32_t rows,
+                 int32_t inter, void* stream);
+
+/*
  * Size of the library-owned scratch used by pkv_paged_decode_static_scratch:
  * one array of this many bytes per GPU that loads the library, held until
  * the process exits.

@@ -308,6 +308,35 @@ int pkv_dense_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
   return launch_status(pkv::launch_prefill(a, src, s), "dense_prefill");
 }
 
+int pkv_add_rmsnorm(const void* a, int64_t a_stride, const void* resid, int64_t r_stride,
+                    void* resid_out, int64_t ro_stride, const void* weight, void* out,
+                    int64_t o_stride, int32_t rows, int32_t dim, float eps, void* stream) {
+  if (!a || !weight || !out) return fail(PKV_ERR_INVALID, "null a, weight or out");
+  if (rows < 0 || dim <= 0 || dim % 8 != 0 || dim > 4096)
+    return fail(PKV_ERR_UNSUPPORTED, "dim must be a positive multiple of 8 up to 4096 (got %d)", dim);
+  if (!aligned16(a) || !aligned16(weight) || !aligned16(out) || (resid && !aligned16(resid)) ||
+      (resid_out && !aligned16(resid_out)) || !mult8(a_stride) || !mult8(o_stride) ||
+      (resid && !mult8(r_stride)) || (resid_out && !mult8(ro_stride)))
+    return fail(PKV_ERR_ALIGN, "add_rmsnorm rows must be 16-byte aligned");
+  if (rows == 0) return ok();
+  pkv::NormLaunch p{a, a_stride, resid, r_stride, resid_out, ro_stride, weight, out, o_stride,
+                    rows, dim, eps};
+  return launch_status(pkv::launch_add_rmsnorm(p, static_cast<cudaStream_t>(stream)), "add_rmsnorm");
+}
+
+int pkv_silu_mul(const void* gu, int64_t gu_stride, void* out, int64_t o_stride, int32_t rows,
+                 int32_t inter, void* stream) {
+  if (!gu || !out) return fail(PKV_ERR_INVALID, "null gu or out");
+  if (rows < 0 || inter <= 0 || inter % 8 != 0)
+    return fail(PKV_ERR_UNSUPPORTED, "inter must be a positive multiple of 8 (got %d)", inter);
+  if (!aligned16(gu) || !aligned16(out) || !mult8(gu_stride) || !mult8(o_stride))
+    return fail(PKV_ERR_ALIGN, "silu_mul rows must be 16-byte aligned");
+  if (rows == 0) return ok();
+  return launch_status(pkv::launch_silu_mul(gu, gu_stride, out, o_stride, rows, inter,
+                                            static_cast<cudaStream_t>(stream)),
+                       "silu_mul");
+}
+
 int pkv_paged_decode_static_scratch(const void* q, int64_t q_sb, int64_t q_sh, const void* k_pool,
                                     const void* v_pool, int64_t num_slots,
                                     const int32_t* block_tables, int64_t table_pitch,

@@ -50,8 +50,7 @@ struct DecodeParams {
   int32_t num_blocks;
   int32_t group;       // query heads per KV head
   int32_t sub_groups;  // CTAs per KV head (group > 8)
-  int32_t blocks_per_part;
-  int32_t max_parts;
+  int32_t max_parts;   // grid.x: partitions available to every row
   float scale_log2;
   float* part_o;
   float* part_lse;
@@ -107,10 +106,16 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
     }
     return;
   }
-  const int nparts = (nblk + p.blocks_per_part - 1) / p.blocks_per_part;
+  // Every row spreads over up to gridDim.x partitions, sized from its own
+  // length (a multiple of the warp count, at least one block per warp): the
+  // grid is planned for the longest row (or a captured capacity), short rows
+  // still get enough CTAs to hide latency.
+  const int per = (nblk + p.max_parts - 1) / p.max_parts;
+  const int bpp = max(kDecodeWarps, (per + kDecodeWarps - 1) / kDecodeWarps * kDecodeWarps);
+  const int nparts = (nblk + bpp - 1) / bpp;
   if (part >= nparts) return;
-  const int blk_begin = part * p.blocks_per_part;
-  const int blk_end = min(nblk, blk_begin + p.blocks_per_part);
+  const int blk_begin = part * bpp;
+  const int blk_end = min(nblk, blk_begin + bpp);
   const int span = blk_end - blk_begin;
   const int my_n = span > warp ? (span - warp + kDecodeWarps - 1) / kDecodeWarps : 0;
 
@@ -374,10 +379,15 @@ int64_t decode_max_units() { return kDecodeMaxUnits; }
 
 namespace {
 
-// Enough CTAs to give every SM several waves of 2 resident CTAs, without
-// shrinking a partition below 16 blocks (256 tokens).
+// The grid's partition count: enough CTAs to give every SM several waves of
+// 2 resident CTAs for the longest row.  Partitions of >= 16 blocks (256
+// tokens) keep the per-CTA set-up and merge cost amortised whenever that
+// still yields kTargetCtas / 4 CTAs; smaller (latency-bound) launches go
+// down to one block per warp.  The kernel sizes each row's partitions from
+// the row's own length within this count.
 constexpr int kTargetCtas = 148 * 2 * 6;
 constexpr int kMinBlocksPerPart = 16;
+constexpr int kMinBlocksPerPartSmall = kDecodeWarps;
 
 template <bool kPaged>
 cudaError_t launch_decode_t(const DecodeParams& prm, const KVSource& src, dim3 grid,
@@ -409,7 +419,8 @@ DecodePlan plan_decode(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
   const int64_t units1 = units > 0 ? units : 1;
   int64_t parts = (kTargetCtas + units1 - 1) / units1;
   int bpp = static_cast<int>((nblk + parts - 1) / parts);
-  bpp = max(bpp, kMinBlocksPerPart);
+  const int64_t ctas_at_16 = units * ((nblk + kMinBlocksPerPart - 1) / kMinBlocksPerPart);
+  bpp = max(bpp, ctas_at_16 >= kTargetCtas / 4 ? kMinBlocksPerPart : kMinBlocksPerPartSmall);
   bpp = (bpp + kDecodeWarps - 1) / kDecodeWarps * kDecodeWarps;
   pl.blocks_per_part = bpp;
   pl.max_parts = (nblk + bpp - 1) / bpp;
@@ -439,7 +450,6 @@ cudaError_t launch_decode(const DecodeLaunch& a, const KVSource& src, const Deco
   prm.num_blocks = src.num_blocks;
   prm.group = a.num_q_heads / a.num_kv_heads;
   prm.sub_groups = plan.sub_groups;
-  prm.blocks_per_part = plan.blocks_per_part;
   prm.max_parts = plan.max_parts;
   prm.scale_log2 = a.sm_scale * 1.4426950408889634f;
   prm.err = a.err;

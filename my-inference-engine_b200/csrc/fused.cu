@@ -1,0 +1,129 @@
+// Fused elementwise kernels of the Qwen2 block around the attention path
+// (sm_100a): residual add + RMSNorm, and SiLU(gate) * up.
+//
+// Reference op sequences (all on bf16 tensors, every torch op rounding its
+// fp32 result to bf16):
+//   model.py:136-137  x = x + attention_output ; x = x + mlp(...)
+//   model.py:49-55    RMSNorm: h = x.float(); v = mean(h*h); h = h * rsqrt(v + eps);
+//                     out = weight * h.to(bf16)
+//   model.py:120      down_proj(silu(gate_proj(x)) * up_proj(x))
+// One CTA per row for the norm (warp + shared-memory reduction of the sum
+// of squares); the SiLU product is a flat 8-wide vectorised loop.
+#include "pkv_device.cuh"
+#include "pkv_kernels.h"
+
+namespace pkv {
+namespace {
+
+__device__ __forceinline__ float bf(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ __nv_bfloat16 rn(float x) { return __float2bfloat16_rn(x); }
+
+constexpr int kNormThreads = 256;
+constexpr int kNormMaxPerThread = 16;  // dim <= 256 threads * 16 = 4096
+
+// One CTA per row: thread i owns elements [8i, 8i+8) (+ 2048 for dim > 2048).
+// h = a (+ resid) in bf16; resid_out = h; out = weight * bf16(h * rsqrt(mean(h^2) + eps))
+__global__ void __launch_bounds__(kNormThreads)
+    add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ a, int64_t a_stride,
+                       const __nv_bfloat16* resid, int64_t r_stride, __nv_bfloat16* resid_out,
+                       int64_t ro_stride, const __nv_bfloat16* __restrict__ weight,
+                       __nv_bfloat16* __restrict__ out, int64_t o_stride, int rows, int dim,
+                       float eps) {
+  __shared__ float warp_ss[kNormThreads / 32];
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  float h[2][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const int col = (c * kNormThreads + tid) * 8;
+    if (col < dim) {
+      const uint4 av = *reinterpret_cast<const uint4*>(a + row * a_stride + col);
+      const __nv_bfloat16* ap = reinterpret_cast<const __nv_bfloat16*>(&av);
+      uint4 hv;
+      __nv_bfloat16* hp = reinterpret_cast<__nv_bfloat16*>(&hv);
+      if (resid) {
+        const uint4 rv = *reinterpret_cast<const uint4*>(resid + row * r_stride + col);
+        const __nv_bfloat16* rp = reinterpret_cast<const __nv_bfloat16*>(&rv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) hp[e] = rn(__fadd_rn(bf(rp[e]), bf(ap[e])));
+      } else {
+        hv = av;
+      }
+      if (resid_out) *reinterpret_cast<uint4*>(resid_out + row * ro_stride + col) = hv;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        h[c][e] = bf(hp[e]);
+        ss = __fadd_rn(ss, __fmul_rn(h[c][e], h[c][e]));
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if ((tid & 31) == 0) warp_ss[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kNormThreads / 32; ++w) tot += warp_ss[w];
+  const float r = rsqrtf(__fadd_rn(tot * (1.0f / static_cast<float>(dim)), eps));
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const int col = (c * kNormThreads + tid) * 8;
+    if (col < dim) {
+      const uint4 wv = *reinterpret_cast<const uint4*>(weight + col);
+      const __nv_bfloat16* wp = reinterpret_cast<const __nv_bfloat16*>(&wv);
+      uint4 ov;
+      __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(&ov);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) op[e] = rn(__fmul_rn(bf(wp[e]), bf(rn(__fmul_rn(h[c][e], r)))));
+      *reinterpret_cast<uint4*>(out + row * o_stride + col) = ov;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int64_t gu_stride,
+                    __nv_bfloat16* __restrict__ out, int64_t o_stride, int rows, int inter) {
+  const int per_row = inter / 8;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<int64_t>(rows) * per_row) return;
+  const int row = static_cast<int>(i / per_row);
+  const int col = static_cast<int>(i % per_row) * 8;
+  const uint4 gv = *reinterpret_cast<const uint4*>(gu + row * gu_stride + col);
+  const uint4 uv = *reinterpret_cast<const uint4*>(gu + row * gu_stride + inter + col);
+  const __nv_bfloat16* gp = reinterpret_cast<const __nv_bfloat16*>(&gv);
+  const __nv_bfloat16* up = reinterpret_cast<const __nv_bfloat16*>(&uv);
+  uint4 ov;
+  __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(&ov);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float g = bf(gp[e]);
+    const __nv_bfloat16 s = rn(g / (1.0f + expf(-g)));  // F.silu in fp32, then bf16
+    op[e] = rn(__fmul_rn(bf(s), bf(up[e])));
+  }
+  *reinterpret_cast<uint4*>(out + row * o_stride + col) = ov;
+}
+
+}  // namespace
+
+cudaError_t launch_add_rmsnorm(const NormLaunch& p, cudaStream_t stream) {
+  add_rmsnorm_kernel<<<p.rows, kNormThreads, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(p.a), p.a_stride,
+      static_cast<const __nv_bfloat16*>(p.resid), p.r_stride,
+      static_cast<__nv_bfloat16*>(p.resid_out), p.ro_stride,
+      static_cast<const __nv_bfloat16*>(p.weight), static_cast<__nv_bfloat16*>(p.out), p.o_stride,
+      p.rows, p.dim, p.eps);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_silu_mul(const void* gu, int64_t gu_stride, void* out, int64_t o_stride,
+                            int32_t rows, int32_t inter, cudaStream_t stream) {
+  const int64_t n = static_cast<int64_t>(rows) * (inter / 8);
+  if (n == 0) return cudaSuccess;
+  silu_mul_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(gu), gu_stride, static_cast<__nv_bfloat16*>(out), o_stride,
+      rows, inter);
+  return cudaGetLastError();
+}
+
+}  // namespace pkv

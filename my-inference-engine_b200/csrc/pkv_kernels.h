@@ -91,4 +91,21 @@ struct AppendLaunch {
 };
 cudaError_t launch_append(const AppendLaunch& a, cudaStream_t stream);
 
+struct NormLaunch {
+  const void* a;
+  int64_t a_stride;
+  const void* resid;  // nullable: no residual add
+  int64_t r_stride;
+  void* resid_out;    // nullable: sum not stored
+  int64_t ro_stride;
+  const void* weight;
+  void* out;
+  int64_t o_stride;
+  int32_t rows, dim;
+  float eps;
+};
+cudaError_t launch_add_rmsnorm(const NormLaunch& p, cudaStream_t stream);
+cudaError_t launch_silu_mul(const void* gu, int64_t gu_stride, void* out, int64_t o_stride,
+                            int32_t rows, int32_t inter, cudaStream_t stream);
+
 }  // namespace pkv

@@ -93,9 +93,15 @@ class QwenAttention(torch.nn.Module):
         from kernels.fa2 import flash_attention
 
         B, T, _ = x.shape
-        q = self.q_proj(x).view(B, T, NUM_HEADS, HEAD_DIM).transpose(1, 2)
-        k = self.k_proj(x).view(B, T, NUM_KV_HEADS, HEAD_DIM).transpose(1, 2)
-        v = self.v_proj(x).view(B, T, NUM_KV_HEADS, HEAD_DIM).transpose(1, 2)
+        if hasattr(self, "qkv_weight"):  # one GEMM over the merged q/k/v weights
+            qkv = F.linear(x, self.qkv_weight, self.qkv_bias).view(B, T, NUM_HEADS + 2 * NUM_KV_HEADS, HEAD_DIM)
+            q = qkv[:, :, :NUM_HEADS].transpose(1, 2)
+            k = qkv[:, :, NUM_HEADS:NUM_HEADS + NUM_KV_HEADS].transpose(1, 2)
+            v = qkv[:, :, NUM_HEADS + NUM_KV_HEADS:].transpose(1, 2)
+        else:
+            q = self.q_proj(x).view(B, T, NUM_HEADS, HEAD_DIM).transpose(1, 2)
+            k = self.k_proj(x).view(B, T, NUM_KV_HEADS, HEAD_DIM).transpose(1, 2)
+            v = self.v_proj(x).view(B, T, NUM_KV_HEADS, HEAD_DIM).transpose(1, 2)
 
         # RoPE on q and k + K/V into their pool blocks, one launch
         q_rot = torch.empty(B, T, NUM_HEADS, HEAD_DIM, device=x.device, dtype=x.dtype)
@@ -117,6 +123,12 @@ class QwenMLP(torch.nn.Module):
         self.down_proj = torch.nn.Linear(INTERMEDIATE_SIZE, HIDDEN_SIZE, bias=False)
 
     def forward(self, x):
+        if hasattr(self, "gate_up_weight"):  # one GEMM + the fused SwiGLU kernel
+            import pagedkv
+
+            shp = x.shape
+            gu = F.linear(x.reshape(-1, shp[-1]), self.gate_up_weight)
+            return self.down_proj(pagedkv.silu_mul(gu)).view(*shp[:-1], HIDDEN_SIZE)
         return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
 
 
@@ -172,6 +184,8 @@ class Qwen2ForCausalLM(torch.nn.Module):
         runner = self._graphs.get(id(cache)) if T == 1 else None
         if runner is not None and runner.covers(len(seqs)):
             return runner.run(input_ids, seqs)[:, None]
+        if input_ids.device != cache.device:
+            input_ids = input_ids.to(cache.device, non_blocking=True)
         starts_list, slot_mapping, gather_idx = cache.prepare(seqs, T)
         logits = self.forward_step(input_ids, cache, gather_idx)
         cache.advance(seqs, T)
@@ -181,19 +195,77 @@ class Qwen2ForCausalLM(torch.nn.Module):
         """Device-only part of forward(): embeddings, 28 layers over the step's
         device tables, last-position logits.  No host synchronisation, so it can
         be captured in a CUDA graph for a fixed batch."""
-        T = input_ids.shape[1]
+        B, T = input_ids.shape
         x = self.embed_tokens(input_ids)
         cos, sin = self.rope_tables(cache.table_pitch * cache.block_size, x.dtype, x.device)
         kv_lens = step.kv_lens
         is_causal = T > 1  # a single query row sees every key up to kv_lens anyway
+        if not self.fused:
+            for layer_idx, layer in enumerate(self.layers):
+                x = layer(x, cos, sin, None, is_causal, kv_lens, cache, layer_idx, step, step)
+            x = self.norm(x[:, -1:])
+            return x @ self.embed_tokens.weight.T
+        # fused: residual add + RMSNorm in one kernel, the residual stream x
+        # updated in place; same op order as QwenBlock.forward (model.py:131-138)
+        import pagedkv
+
+        N = B * T
+        xs = x.view(N, HIDDEN_SIZE)
+        h = pagedkv.add_rmsnorm(xs, None, self.layers[0].input_layernorm.weight, RMS_NORM_EPS)
         for layer_idx, layer in enumerate(self.layers):
-            x = layer(x, cos, sin, None, is_causal, kv_lens, cache, layer_idx, step, step)
-        x = self.norm(x[:, -1:])
-        return x @ self.embed_tokens.weight.T
+            a = layer.self_attn(h.view(B, T, HIDDEN_SIZE), cos, sin, None, is_causal, kv_lens,
+                                cache, layer_idx, step, step)
+            h = pagedkv.add_rmsnorm(a.view(N, HIDDEN_SIZE), xs, layer.post_attention_layernorm.weight,
+                                    RMS_NORM_EPS, resid_out=xs)
+            m = layer.mlp(h)
+            if layer_idx + 1 < len(self.layers):
+                h = pagedkv.add_rmsnorm(m, xs, self.layers[layer_idx + 1].input_layernorm.weight,
+                                        RMS_NORM_EPS, resid_out=xs)
+        # last position only (model.py:204-206): x + mlp, then the final norm
+        last = T - 1
+        m_last = m.view(B, T, HIDDEN_SIZE)[:, last]
+        x_last = x.view(B, T, HIDDEN_SIZE)[:, last]
+        h = pagedkv.add_rmsnorm(m_last, x_last, self.norm.weight, RMS_NORM_EPS)
+        return (h @ self.embed_tokens.weight.T)[:, None]
+
+    @property
+    def fused(self):
+        return getattr(self, "_fused", False)
+
+    def fuse_weights_(self):
+        """Merge q/k/v (weights + biases) and gate/up weights into single
+        tensors so each needs one GEMM; the original parameters become views
+        of the merged tensors (no extra memory, state_dict unchanged).  Also
+        switches forward to the fused residual-add + RMSNorm kernels."""
+        if self.fused:
+            return self
+        with torch.no_grad():
+            for layer in self.layers:
+                at, mlp = layer.self_attn, layer.mlp
+                w = torch.cat([at.q_proj.weight, at.k_proj.weight, at.v_proj.weight]).contiguous()
+                b = torch.cat([at.q_proj.bias, at.k_proj.bias, at.v_proj.bias]).contiguous()
+                nq, nk = at.q_proj.weight.shape[0], at.k_proj.weight.shape[0]
+                at.q_proj.weight = nn.Parameter(w[:nq], requires_grad=False)
+                at.k_proj.weight = nn.Parameter(w[nq:nq + nk], requires_grad=False)
+                at.v_proj.weight = nn.Parameter(w[nq + nk:], requires_grad=False)
+                at.q_proj.bias = nn.Parameter(b[:nq], requires_grad=False)
+                at.k_proj.bias = nn.Parameter(b[nq:nq + nk], requires_grad=False)
+                at.v_proj.bias = nn.Parameter(b[nq + nk:], requires_grad=False)
+                at.register_buffer("qkv_weight", w, persistent=False)
+                at.register_buffer("qkv_bias", b, persistent=False)
+                gu = torch.cat([mlp.gate_proj.weight, mlp.up_proj.weight]).contiguous()
+                ni = mlp.gate_proj.weight.shape[0]
+                mlp.gate_proj.weight = nn.Parameter(gu[:ni], requires_grad=False)
+                mlp.up_proj.weight = nn.Parameter(gu[ni:], requires_grad=False)
+                mlp.register_buffer("gate_up_weight", gu, persistent=False)
+        self._fused = True
+        return self
 
     # ---- CUDA-graph decode ----
     def enable_decode_graphs(self, cache, max_batch=256):
-        """Capture the T == 1 forward per batch bucket (lazily, on first use)."""
+        """Capture the T == 1 forward per batch bucket (lazily, on first use).
+        Merges the projection weights first (fuse_weights_)."""
+        self.fuse_weights_()
         self._graphs[id(cache)] = DecodeGraphs(self, cache, max_batch)
         return self._graphs[id(cache)]
 

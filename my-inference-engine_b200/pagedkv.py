@@ -47,6 +47,10 @@ _SIGNATURES = {
     "pkv_paged_prefill": (
         [_vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
          _i32, _i32, ctypes.c_float, _vp, _i64, _i64, _i64, _vp, _vp], ctypes.c_int),
+    "pkv_add_rmsnorm": (
+        [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, ctypes.c_float, _vp],
+        ctypes.c_int),
+    "pkv_silu_mul": ([_vp, _i64, _vp, _i64, _i32, _i32, _vp], ctypes.c_int),
     "pkv_paged_decode_static_scratch": (
         [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
          ctypes.c_float, _vp, _i64, _i64, _vp, _vp], ctypes.c_int),
@@ -195,6 +199,33 @@ def dense_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_lens: 
         out.stride(2), _ptr(ws), ws.numel() if ws is not None else 0, _ptr(err),
         _stream(q.device))
     _check(st, "pkv_dense_attention")
+
+
+def add_rmsnorm(a: torch.Tensor, resid: torch.Tensor | None, weight: torch.Tensor,
+                eps: float, resid_out: torch.Tensor | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """pkv_add_rmsnorm over the last dim of 2-D row views (any row stride)."""
+    rows, dim = a.shape
+    if out is None:
+        out = torch.empty(rows, dim, dtype=a.dtype, device=a.device)
+    st = lib().pkv_add_rmsnorm(
+        _ptr(a), a.stride(0), _ptr(resid), resid.stride(0) if resid is not None else 0,
+        _ptr(resid_out), resid_out.stride(0) if resid_out is not None else 0, _ptr(weight),
+        _ptr(out), out.stride(0), rows, dim, eps, _stream(a.device))
+    _check(st, "pkv_add_rmsnorm")
+    return out
+
+
+def silu_mul(gu: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """pkv_silu_mul: gu [rows, 2*inter] -> [rows, inter]."""
+    rows, two_inter = gu.shape
+    inter = two_inter // 2
+    if out is None:
+        out = torch.empty(rows, inter, dtype=gu.dtype, device=gu.device)
+    st = lib().pkv_silu_mul(_ptr(gu), gu.stride(0), _ptr(out), out.stride(0), rows, inter,
+                            _stream(gu.device))
+    _check(st, "pkv_silu_mul")
+    return out
 
 
 def default_scale(d: int = HEAD_DIM) -> float:

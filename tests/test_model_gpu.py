@@ -90,10 +90,17 @@ def _agreement(ref_logits, flat_ids, margin):
     return decisive, agree, worst
 
 
-def test_greedy_ids_match_oracle_and_reference(cuda, models):
+@pytest.mark.parametrize("fused", [False, True])
+def test_greedy_ids_match_oracle_and_reference(cuda, models, fused):
+    """fused=True: merged q/k/v and gate/up GEMMs + fused add/RMSNorm/SwiGLU
+    kernels (the engine's path); fused=False: the reference's op structure."""
+    import copy
+
     from kv_cache import KVCache
 
     ours, ref32, ref16, fx = models
+    if fused:
+        ours = copy.deepcopy(ours).fuse_weights_()
     prompts, steps = fx["prompts"], fx["steps"]
     c1 = KVCache(64, 16, cuda, torch.bfloat16)
     s1 = [c1.alloc(), c1.alloc()]
