@@ -42,9 +42,11 @@ def test_decode_workspace_plan_is_host_only_and_sane():
     assert L.pkv_decode_workspace_size(4, 12, 2, 37) == 0
     # long contexts split into partitions: scratch is needed, and bounded by
     # the planner's CTA target (~1776 partitions) plus the 256 KiB counter head
-    for B in (1, 4, 8, 64, 256, 1024):
+    for B in (1, 4, 8, 64, 256):
         n = L.pkv_decode_workspace_size(B, 12, 2, 8192)
         assert 0 < n < (256 << 10) + 4000 * 8 * 129 * 4, (B, n)
+    # a batch that alone fills the machine needs no split
+    assert L.pkv_decode_workspace_size(1024, 12, 2, 8192) == 0
     # invalid head counts report 0 instead of failing
     assert L.pkv_decode_workspace_size(4, 12, 5, 8192) == 0
 
