@@ -64,6 +64,8 @@ def parse():
     ap.add_argument("--engine-prompt", type=int, nargs=2, default=[32, 1000])
     ap.add_argument("--engine-blocks", type=int, default=1024)
     ap.add_argument("--no-engine-cpu", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--prefill-steps", type=int, default=20)
     return ap.parse_args()
 
 
@@ -289,6 +291,70 @@ def cpu_info():
     except OSError:
         pass
     return name
+
+
+# ---------------------------------------------------------------- prefill
+def prefill_run(args, device, seed=0):
+    """BASELINE config 1 on the tcgen05 prefill kernel: 8 rows with prompt
+    lengths U[16,1024] (seeded) appended to empty caches in a shuffled pool,
+    then per layer ONE causal attention launch over the paged K/V with the
+    queries left-padded to the longest prompt (bottom-right alignment puts each
+    row's real queries on its own keys; padded query rows see no key).
+    Useful FLOPs = sum_b 4*12*128*L_b(L_b+1)/2 per layer."""
+    from kernels.fa2 import flash_attention
+    from kv_cache import KVCache, PagedStep
+
+    g = torch.Generator().manual_seed(seed + 42)
+    lens = torch.randint(16, 1025, (8,), generator=g).tolist()
+    T = max(lens)
+    N = sum(math.ceil(n / 16) for n in lens) + 16
+    cache = KVCache(N, 16, device, torch.bfloat16)
+    cache._free_blocks = torch.randperm(N, generator=g).tolist()
+    seqs = [cache.alloc() for _ in lens]
+    gd = torch.Generator(device=device).manual_seed(seed + 43)
+    for s_, n in zip(seqs, lens):  # prompt K/V appended through the product path
+        k = torch.randn(1, HKV, n, D, device=device, generator=gd).to(torch.bfloat16)
+        v = torch.randn(1, HKV, n, D, device=device, generator=gd).to(torch.bfloat16)
+        _, st, _ = cache.prepare([s_], n)
+        for l in range(L):
+            cache.write(l, st, k, v)
+        cache.advance([s_], n)
+    rows = torch.tensor([cache.table_row(x) for x in seqs], dtype=torch.int32, device=device)
+    kvl = torch.tensor(lens, dtype=torch.int32, device=device)
+    step = PagedStep(cache, T, [0] * len(lens), rows, kvl - T, kvl, T)
+    q = torch.randn(L, len(lens), HQ, T, D, device=device, generator=gd).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    handles = [cache.read(l, step) for l in range(L)]
+
+    def one():
+        for l in range(L):
+            kh, vh = handles[l]
+            flash_attention(q[l], kh, vh, True, kvl, out=out[l])
+
+    for _ in range(3):
+        one()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.prefill_steps):
+        one()
+    e1.record()
+    e1.synchronize()
+    cache.check_errors()
+    ms = e0.elapsed_time(e1) / args.prefill_steps / L
+    flops = sum(4 * HQ * D * n * (n + 1) / 2 for n in lens)
+    peaks, src = measured_peaks()
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    tf = flops / (ms * 1e-3) / 1e12
+    del cache, q, out, handles
+    torch.cuda.empty_cache()
+    return {"metric": "paged causal prefill attention, useful TFLOP/s", "value": round(tf, 1),
+            "unit": "TFLOP/s", "kernel": "prefill_tc_kernel (tcgen05 + TMEM)",
+            "ms_per_launch": round(ms, 4), "flops_per_launch": flops,
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak,
+                         "unit": "TFLOP/s", "frac": round(tf / peak, 4), "peak_source": src},
+            "config": f"config1: 8 rows, prompt lengths {lens} from empty caches, shuffled "
+                      f"{N}-block pool, causal, queries left-padded to {T}, one launch per layer"}
 
 
 # ---------------------------------------------------------------- engine
@@ -545,10 +611,11 @@ def main():
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": round(float(e_all.item()), 3)}
 
+    del w
+    torch.cuda.empty_cache()
+    prefill = None if args.no_prefill else prefill_run(args, dev, seed=args.seed)
     engine = None
     if not args.no_engine:
-        del w
-        torch.cuda.empty_cache()
         engine = engine_run(args, dev, seed=args.seed + rank)
         tok_all = torch.tensor([engine["tok_s"]], device=dev, dtype=torch.float64)
         if world > 1:
@@ -593,7 +660,7 @@ def main():
                 "data": "synthetic", "config": config, "roofline": roofline,
                 "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
                 "gpu_launches": args.steps * layers * 2,
-                "kv_bytes_per_step": step_bytes, "engine": engine}
+                "kv_bytes_per_step": step_bytes, "prefill": prefill, "engine": engine}
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()

@@ -87,6 +87,24 @@ int encode_dense(CUtensorMap* m, const void* base, int32_t B, int32_t hkv, int32
   return PKV_OK;
 }
 
+// Q [B][Hq][T][128] bf16 -> 4-D map, box {64, 128, 1, 1} (128 query rows).
+int encode_q(CUtensorMap* m, const void* base, int32_t B, int32_t hq, int32_t T, int64_t sb,
+             int64_t sh, int64_t st) {
+  EncodeFn fn = encode_fn();
+  if (!fn) return fail(PKV_ERR_DRIVER, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(T), static_cast<cuuint64_t>(hq),
+                        static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(st) * 2, static_cast<cuuint64_t>(sh) * 2,
+                           static_cast<cuuint64_t>(sb) * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides,
+                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PKV_ERR_DRIVER, "q tensor map encode failed (%d)", (int)r);
+  return PKV_OK;
+}
+
 int check_heads(int32_t hq, int32_t hkv, int32_t d) {
   if (d != 128) return fail(PKV_ERR_UNSUPPORTED, "head_dim must be 128, got %d", d);
   if (hq <= 0 || hkv <= 0 || hq % hkv != 0)
@@ -113,6 +131,13 @@ int check_pool(const void* kp, const void* vp, int64_t num_slots, const int32_t*
 int launch_status(cudaError_t e, const char* what) {
   if (e != cudaSuccess) return fail(PKV_ERR_LAUNCH, "%s launch failed: %s", what, cudaGetErrorString(e));
   return ok();
+}
+
+int launch_prefill_any(const pkv::PrefillLaunch& a, const pkv::KVSource& src, cudaStream_t s) {
+  CUtensorMap qmap;
+  int st = encode_q(&qmap, a.q, a.batch, a.num_q_heads, a.seq_len_q, a.q_sb, a.q_sh, a.q_st);
+  if (st) return st;
+  return launch_status(pkv::launch_prefill_tc(a, qmap, src, s), "prefill_tc");
 }
 
 }  // namespace
@@ -263,8 +288,7 @@ int pkv_paged_prefill(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, c
   a.kv_lens = kv_lens; a.batch = batch; a.seq_len_q = seq_len_q;
   a.num_q_heads = num_q_heads; a.num_kv_heads = num_kv_heads; a.causal = causal ? 1 : 0;
   a.sm_scale = sm_scale; a.err = err_flag;
-  return launch_status(pkv::launch_prefill(a, src, static_cast<cudaStream_t>(stream)),
-                       "paged_prefill");
+  return launch_prefill_any(a, src, static_cast<cudaStream_t>(stream));
 }
 
 int pkv_dense_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, const void* k,
@@ -305,7 +329,7 @@ int pkv_dense_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
   a.kv_lens = kv_lens; a.batch = batch; a.seq_len_q = seq_len_q;
   a.num_q_heads = num_q_heads; a.num_kv_heads = num_kv_heads; a.causal = causal ? 1 : 0;
   a.sm_scale = sm_scale; a.err = err_flag;
-  return launch_status(pkv::launch_prefill(a, src, s), "dense_prefill");
+  return launch_prefill_any(a, src, s);
 }
 
 int pkv_add_rmsnorm(const void* a, int64_t a_stride, const void* resid, int64_t r_stride,

@@ -19,7 +19,6 @@ __device__ __forceinline__ float bf(__nv_bfloat16 x) { return __bfloat162float(x
 __device__ __forceinline__ __nv_bfloat16 rn(float x) { return __float2bfloat16_rn(x); }
 
 constexpr int kNormThreads = 256;
-constexpr int kNormMaxPerThread = 16;  // dim <= 256 threads * 16 = 4096
 
 // One CTA per row: thread i owns elements [8i, 8i+8) (+ 2048 for dim > 2048).
 // h = a (+ resid) in bf16; resid_out = h; out = weight * bf16(h * rsqrt(mean(h^2) + eps))

@@ -65,7 +65,9 @@ struct PrefillLaunch {
   float sm_scale;
   int32_t* err;
 };
-cudaError_t launch_prefill(const PrefillLaunch& a, const KVSource& src, cudaStream_t stream);
+// tcgen05/TMEM prefill; qmap: 4-D map over q [B][Hq][T][128], box {64,128,1,1}
+cudaError_t launch_prefill_tc(const PrefillLaunch& a, const CUtensorMap& qmap, const KVSource& src,
+                              cudaStream_t stream);
 
 struct AppendLaunch {
   const void* q;

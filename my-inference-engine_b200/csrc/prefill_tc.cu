@@ -1,0 +1,514 @@
+// Ragged causal prefill attention on the 5th-generation tensor cores
+// (tcgen05 + TMEM, sm_100a).
+//
+// Contract: kernels/fa2.py:23-162 with is_causal = T > 1 (model.py:185):
+// query i of row b sits at key i + kv_len - T (bottom-right, fa2.py:110-111),
+// keys >= kv_len are masked (fa2.py:132-136), online softmax in fp32, P
+// rounded to bf16 before the PV product (fa2.py:145), O / l at the end
+// (fa2.py:151).
+//
+//   grid  = (ceil(T/128), Hq, B): one CTA per 128 query rows of one head
+//   block = 6 warps
+//     warp 0    TMA producer (one thread): Q tile once, then 128-key K/V
+//               tiles (eight 16-token blocks each, through the block table)
+//               into a 2-deep ring; a tile's block ids are read one tile ahead
+//     warp 1    owns TMEM (512 columns: S0, S1, O) and issues tcgen05.mma:
+//               S[b] = Q.K^T (M=128, N=128, K=128 in 8 steps), then
+//               O += P.V (K = 16 keys per step, only the loaded blocks)
+//     warps 2-5 softmax: warp w owns TMEM lanes 32*(w%4).., i.e. one query
+//               row per thread, so row max / sum need no shuffles; writes P
+//               (bf16) to shared memory, rescales O in TMEM when a row's max
+//               moved, epilogue
+// Shared-memory operands use the canonical 128B-swizzled layouts: Q, K, P
+// K-major (rows of 64 elements, 8-row groups 1024 B apart, k-steps advance
+// the start address by 32 B), V MN-major (64-dim groups 16 KB apart, 8-key
+// groups 1024 B apart).  Every wait is bounded.
+#include <math.h>
+
+#include "pkv_device.cuh"
+#include "pkv_kernels.h"
+
+namespace pkv {
+namespace {
+
+constexpr int kRows = 128;                         // query rows per CTA (MMA M)
+constexpr int kKeys = 128;                         // keys per tile (N of Q.K^T, K of P.V)
+constexpr int kTileBlocks = kKeys / kBlockTokens;  // 8
+constexpr int kRegion = kRows * 128;               // 16 KiB: 128 rows x 64 bf16
+constexpr int kOperand = 2 * kRegion;              // 32 KiB: dims (or keys) 0-63 | 64-127
+constexpr int kStages = 2;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+// smem map (offsets from the 1024-aligned base)
+constexpr int kOffQ = 0;
+constexpr int kOffKV = kOffQ + kOperand;  // stage s: K at +s*64K, V at +32K
+constexpr int kOffP = kOffKV + kStages * 2 * kOperand;
+constexpr int kOffBar = kOffP + kOperand;
+constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 1 + 1 + 1;
+constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
+
+// instruction descriptors (kind::f16): fp32 accumulate, bf16 A/B, M=128, N=128
+constexpr uint32_t kIdescBase = (1u << 4) | (1u << 7) | (1u << 10) | ((kKeys >> 3) << 17) |
+                                ((kRows >> 4) << 24);
+constexpr uint32_t kIdescQK = kIdescBase;               // A K-major, B K-major
+constexpr uint32_t kIdescPV = kIdescBase | (1u << 16);  // B (V) MN-major
+
+struct TcParams {
+  __nv_bfloat16* out;
+  int64_t o_sb, o_sh, o_st;
+  const int32_t* kv_lens;
+  const int32_t* tables;
+  int64_t pitch;
+  const int32_t* rows;
+  int32_t num_blocks;
+  int32_t T;
+  int32_t group;
+  int32_t causal;
+  float scale_log2;
+  int32_t* err;
+};
+
+// ---------------------------------------------------------------- tcgen05
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) |
+         (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                     uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// K-major operand (Q, K or P): 128 rows, k-step kk covers elements
+// [16kk, 16kk+16) -> region kk/4, +32 B per step inside the 128 B row.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk) {
+  return sdesc(base + (kk >> 2) * kRegion + (kk & 3) * 32, 16, 1024);
+}
+
+template <bool kPaged>
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap qmap,
+                      const __grid_constant__ CUtensorMap kmap,
+                      const __grid_constant__ CUtensorMap vmap) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + kStages;
+  uint64_t* s_full = kv_empty + kStages;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_full = s_free + 2;
+  uint64_t* pv_done = p_full + 1;
+  uint64_t* mma_done = pv_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int b = blockIdx.z;
+  const int hq = blockIdx.y;
+  const int kvh = hq / p.group;
+  const int q0 = blockIdx.x * kRows;
+  const int T = p.T;
+  const DevErr err{p.err};
+
+  int kv_len = max(p.kv_lens[b], 0);
+  const int32_t* trow = nullptr;
+  if constexpr (kPaged) {
+    const int row = p.rows ? p.rows[b] : b;
+    trow = p.tables + static_cast<int64_t>(row) * p.pitch;
+    if (kv_len > p.pitch * kBlockTokens) {
+      if (tid == 0 && blockIdx.x == 0 && hq == 0) err.raise(PKV_DEVERR_POSITION);
+      kv_len = static_cast<int>(p.pitch) * kBlockTokens;
+    }
+  }
+  const int offset = kv_len - T;
+  int kv_end = kv_len;
+  if (p.causal) kv_end = min(kv_len, min(q0 + kRows, T) + offset);
+  kv_end = max(kv_end, 0);
+  const int nblk = (kv_end + kBlockTokens - 1) / kBlockTokens;
+  const int ntiles = (nblk + kTileBlocks - 1) / kTileBlocks;
+
+  if (ntiles == 0) {
+    // no visible key for any row of this tile (e.g. left padding): 0/0 rows,
+    // as the reference, without touching TMEM
+    const uint32_t nan2 = 0x7fc07fc0u;  // two bf16 quiet NaNs
+    const uint4 nv = make_uint4(nan2, nan2, nan2, nan2);
+    for (int i = tid; i < kRows * 16; i += kThreads) {
+      const int qi = q0 + i / 16;
+      if (qi < T)
+        *reinterpret_cast<uint4*>(p.out + b * p.o_sb + hq * p.o_sh +
+                                  static_cast<int64_t>(qi) * p.o_st + (i % 16) * 8) = nv;
+    }
+    return;
+  }
+
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&kv_full[s], 1);   // producer's arrive.expect_tx
+      mbar_init(&kv_empty[s], 1);  // tcgen05.commit after the tile's PV
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&s_full[s], 1);  // tcgen05.commit after Q.K^T
+      mbar_init(&s_free[s], 4);  // one arrival per softmax warp
+    }
+    mbar_init(p_full, 4);
+    mbar_init(pv_done, 1);
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sQ = smem_u32(smem + kOffQ);
+  const uint32_t sP = smem_u32(smem + kOffP);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    // One thread issues every TMA load.  A tile's eight block ids are loaded
+    // together one tile ahead, so table reads never serialise the issue.
+    if (lane == 0) {
+      auto fetch = [&](int j, int (&ids)[kTileBlocks]) {
+        if constexpr (kPaged) {
+#pragma unroll
+          for (int jb = 0; jb < kTileBlocks; ++jb) {
+            const int lb = j * kTileBlocks + jb;
+            // blocks past the row's end load the row's first block: finite
+            // data, masked out of S and never multiplied into O
+            ids[jb] = trow[lb < nblk ? lb : 0];
+          }
+#pragma unroll
+          for (int jb = 0; jb < kTileBlocks; ++jb) {
+            if (ids[jb] < 0 || ids[jb] >= p.num_blocks) {
+              err.raise(PKV_DEVERR_BLOCK_ID);
+              ids[jb] = 0;
+            }
+          }
+        }
+      };
+      prefetch_tmap(&qmap);
+      prefetch_tmap(&kmap);
+      prefetch_tmap(&vmap);
+      const uint64_t keep = policy_evict_last();
+      int cur[kTileBlocks] = {}, nxt[kTileBlocks] = {};
+      fetch(0, nxt);
+      mbar_arrive_expect_tx(q_full, kOperand);
+      tma_load_4d(smem + kOffQ, &qmap, q_full, 0, q0, hq, b, keep);
+      tma_load_4d(smem + kOffQ + kRegion, &qmap, q_full, 64, q0, hq, b, keep);
+      for (int j = 0; j < ntiles; ++j) {
+#pragma unroll
+        for (int jb = 0; jb < kTileBlocks; ++jb) cur[jb] = nxt[jb];
+        if (j + 1 < ntiles) fetch(j + 1, nxt);
+        const int st = j % kStages;
+        if (j >= kStages && !mbar_wait(&kv_empty[st], ((j / kStages) - 1) & 1, err)) break;
+        uint8_t* kt = smem + kOffKV + st * 2 * kOperand;
+        uint8_t* vt = kt + kOperand;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kOperand);
+#pragma unroll
+        for (int jb = 0; jb < kTileBlocks; ++jb) {
+          if constexpr (kPaged) {
+            const int slot = cur[jb] * kBlockTokens;
+            tma_load_3d(kt + jb * 2048, &kmap, &kv_full[st], 0, kvh, slot, keep);
+            tma_load_3d(kt + kRegion + jb * 2048, &kmap, &kv_full[st], 64, kvh, slot, keep);
+            tma_load_3d(vt + jb * 2048, &vmap, &kv_full[st], 0, kvh, slot, keep);
+            tma_load_3d(vt + kRegion + jb * 2048, &vmap, &kv_full[st], 64, kvh, slot, keep);
+          } else {
+            const int tok = (j * kTileBlocks + jb) * kBlockTokens;
+            tma_load_4d(kt + jb * 2048, &kmap, &kv_full[st], 0, tok, kvh, b, keep);
+            tma_load_4d(kt + kRegion + jb * 2048, &kmap, &kv_full[st], 64, tok, kvh, b, keep);
+            tma_load_4d(vt + jb * 2048, &vmap, &kv_full[st], 0, tok, kvh, b, keep);
+            tma_load_4d(vt + kRegion + jb * 2048, &vmap, &kv_full[st], 64, tok, kvh, b, keep);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool dead = !mbar_wait(q_full, 0, err);
+      auto issue_pv = [&](int i) -> bool {
+        if (!mbar_wait(p_full, i & 1, err)) return false;
+        tc_fence_after();
+        const int st = i % kStages;
+        const uint32_t sV = smem_u32(smem + kOffKV + st * 2 * kOperand + kOperand);
+        const int nb = min(kTileBlocks, nblk - i * kTileBlocks);
+        for (int kb = 0; kb < nb; ++kb) {
+          umma(tmem + kColO, kmajor_desc(sP, kb), sdesc(sV + kb * 2048, kRegion, 1024), kIdescPV,
+               (i > 0 || kb > 0) ? 1u : 0u);
+        }
+        umma_commit(pv_done);
+        umma_commit(&kv_empty[st]);
+        return true;
+      };
+      for (int j = 0; j < ntiles && !dead; ++j) {
+        const int st = j % kStages;
+        const int sb = j & 1;
+        if (!mbar_wait(&kv_full[st], (j / kStages) & 1, err)) {
+          dead = true;
+          break;
+        }
+        if (j >= 2 && !mbar_wait(&s_free[sb], ((j >> 1) - 1) & 1, err)) {
+          dead = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sK = smem_u32(smem + kOffKV + st * 2 * kOperand);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma(tmem + (sb ? kColS1 : kColS0), kmajor_desc(sQ, kk), kmajor_desc(sK, kk), kIdescQK,
+               kk > 0 ? 1u : 0u);
+        umma_commit(&s_full[sb]);
+        if (j >= 1 && !issue_pv(j - 1)) {
+          dead = true;
+          break;
+        }
+      }
+      if (!dead) issue_pv(ntiles - 1);
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, err);  // every MMA retired before TMEM is freed
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // query row within the tile == TMEM lane
+    const int qi = q0 + r;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const int lim = p.causal ? min(kv_len, qi + offset + 1) : kv_len;  // keys < lim visible
+    float m = -INFINITY, l = 0.f;
+    bool dead = false;
+    for (int j = 0; j < ntiles && !dead; ++j) {
+      const int sb = j & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[sb], (j >> 1) & 1, err))) {
+        dead = true;
+        break;
+      }
+      tc_fence_after();
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(lane_addr + (sb ? kColS1 : kColS0) + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = v[i];
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[sb]);
+
+      const int key0 = j * kKeys;
+      float mx = -INFINITY;
+      if (key0 + kKeys <= lim) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) {
+          s[i] *= p.scale_log2;
+          mx = fmaxf(mx, s[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) {
+          s[i] = (key0 + i < lim) ? s[i] * p.scale_log2 : -INFINITY;
+          mx = fmaxf(mx, s[i]);
+        }
+      }
+      // Lazy rescaling: keep the running max unless this tile raises it by
+      // more than 2^8 (P <= 256 then, exact in fp32 and bf16-representable);
+      // O is rescaled in TMEM only when some row of the warp moved its max.
+      float mn = m;
+      if (mx > m + kRescaleThreshold || m == -INFINITY) mn = mx;
+      const float base = mn == -INFINITY ? 0.f : mn;
+      const float alpha = (mn == m) ? 1.f : ex2(m - base);
+      float rs = 0.f;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        s[i] = ex2(s[i] - base);
+        rs += s[i];
+      }
+      l = l * alpha + rs;
+      m = mn;
+      const bool rescale = __any_sync(0xffffffffu, alpha != 1.f);
+      // P and O are free once the previous tile's PV product retired
+      if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, err))) {
+        dead = true;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int reg = 0; reg < 2; ++reg) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const int k = reg * 64 + c * 8;
+          uint4 pk;
+          pk.x = pack_bf16(s[k + 0], s[k + 1]);
+          pk.y = pack_bf16(s[k + 2], s[k + 3]);
+          pk.z = pack_bf16(s[k + 4], s[k + 5]);
+          pk.w = pack_bf16(s[k + 6], s[k + 7]);
+          *reinterpret_cast<uint4*>(smem + kOffP + reg * kRegion + swz128(r, c)) = pk;
+        }
+      }
+      fence_async_smem();
+      if (j >= 1 && rescale) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld32(lane_addr + kColO + c * 32, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= alpha;
+          tmem_st32(lane_addr + kColO + c * 32, v);
+        }
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    // ------------------------------------------------------------ epilogue
+    // tcgen05.ld is warp-collective: every lane loads, only rows < T store
+    bool have = !dead;
+    if (have) have = __all_sync(0xffffffffu, mbar_wait(pv_done, (ntiles - 1) & 1, err));
+    __nv_bfloat16* orow =
+        p.out + b * p.o_sb + hq * p.o_sh + static_cast<int64_t>(min(qi, T - 1)) * p.o_st;
+    if (have) {
+      tc_fence_after();
+      const float inv = 1.f / l;  // 0/0 -> NaN for a row with no visible key
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(lane_addr + kColO + c * 32, v);
+        tmem_wait_ld();
+        if (qi < T) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            uint4 pk;
+            pk.x = pack_bf16(v[e + 0] * inv, v[e + 1] * inv);
+            pk.y = pack_bf16(v[e + 2] * inv, v[e + 3] * inv);
+            pk.z = pack_bf16(v[e + 4] * inv, v[e + 5] * inv);
+            pk.w = pack_bf16(v[e + 6] * inv, v[e + 7] * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + e) = pk;
+          }
+        }
+      }
+    } else if (qi < T) {
+      // a timed-out wait: NaN rows rather than stale data
+      const uint32_t nan2 = 0x7fc07fc0u;
+      const uint4 nv = make_uint4(nan2, nan2, nan2, nan2);
+#pragma unroll
+      for (int e = 0; e < 128; e += 8) *reinterpret_cast<uint4*>(orow + e) = nv;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+template <bool kPaged>
+cudaError_t launch_tc_t(const TcParams& prm, const CUtensorMap& qmap, const KVSource& src,
+                        dim3 grid, cudaStream_t stream) {
+  auto kern = prefill_tc_kernel<kPaged>;
+  static int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    configured_device = dev;
+  }
+  kern<<<grid, kThreads, kSmemBytes, stream>>>(prm, qmap, src.kmap, src.vmap);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_prefill_tc(const PrefillLaunch& a, const CUtensorMap& qmap, const KVSource& src,
+                              cudaStream_t stream) {
+  TcParams prm{};
+  prm.out = static_cast<__nv_bfloat16*>(a.out);
+  prm.o_sb = a.o_sb;
+  prm.o_sh = a.o_sh;
+  prm.o_st = a.o_st;
+  prm.kv_lens = a.kv_lens;
+  prm.tables = src.tables;
+  prm.pitch = src.pitch;
+  prm.rows = src.rows;
+  prm.num_blocks = src.num_blocks;
+  prm.T = a.seq_len_q;
+  prm.group = a.num_q_heads / a.num_kv_heads;
+  prm.causal = a.causal;
+  prm.scale_log2 = a.sm_scale * 1.4426950408889634f;
+  prm.err = a.err;
+  dim3 grid((a.seq_len_q + kRows - 1) / kRows, a.num_q_heads, a.batch);
+  return src.paged ? launch_tc_t<true>(prm, qmap, src, grid, stream)
+                   : launch_tc_t<false>(prm, qmap, src, grid, stream);
+}
+
+}  // namespace pkv
