@@ -525,6 +525,25 @@ def engine_cpu_sample(seconds_budget=60.0):
             "sample": "2 chats, 32-token prompts, 4-token replies, fp32 torch CPU (prefill included)"}
 
 
+# ---------------------------------------------------------------- ranks
+def cross_rank(value, op, device, world):
+    """all_reduce of one float over the ranks (MAX or SUM); identity at N=1."""
+    if world == 1:
+        return float(value)
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=op)
+    return float(t.item())
+
+
+def replica_rate(units_per_rank, ms_local, device, world):
+    """Whole-job rate of N independent replicas: every rank processed
+    units_per_rank in its own time; the job took the slowest rank's time.
+    Returns (max ms over ranks, units of all ranks per second)."""
+    ms_max = cross_rank(ms_local, torch.distributed.ReduceOp.MAX if world > 1 else None, device,
+                        world)
+    return ms_max, units_per_rank * world / (ms_max * 1e-3)
+
+
 # ---------------------------------------------------------------- main
 def main():
     args = parse()
@@ -593,23 +612,18 @@ def main():
     clk = clocks.stop()
     ms = t_start.elapsed_time(t_end) / args.steps
     kern_ms = statistics.mean(a.elapsed_time(b) for st in evs for a, b in st)
-    ms_all = torch.tensor([ms], device=dev)
-    if world > 1:
-        torch.distributed.all_reduce(ms_all, op=torch.distributed.ReduceOp.MAX)
-    ms_max = float(ms_all.item())
-    total_bytes = w.step_bytes() * world
     step_bytes, bytes_decode, layers = w.step_bytes(), w.bytes_decode, w.layers
-    value = total_bytes / (ms_max * 1e-3) / 1e9
+    ms_max, rate = replica_rate(step_bytes, ms, dev, world)
+    total_bytes = step_bytes * world
+    value = rate / 1e9
 
     e2e = None
     if not args.no_e2e:
         e_ms, h2d, d2h = e2e_run(w, max(2, args.steps // 2), 1)
-        e_all = torch.tensor([e_ms], device=dev)
-        if world > 1:
-            torch.distributed.all_reduce(e_all, op=torch.distributed.ReduceOp.MAX)
-        e2e = {"value": round(total_bytes / (float(e_all.item()) * 1e-3) / 1e9, 2), "unit": "GB/s",
+        e_max, e_rate = replica_rate(step_bytes, e_ms, dev, world)
+        e2e = {"value": round(e_rate / 1e9, 2), "unit": "GB/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "ms_per_step": round(float(e_all.item()), 3)}
+               "ms_per_step": round(e_max, 3)}
 
     del w
     torch.cuda.empty_cache()
@@ -617,10 +631,9 @@ def main():
     engine = None
     if not args.no_engine:
         engine = engine_run(args, dev, seed=args.seed + rank)
-        tok_all = torch.tensor([engine["tok_s"]], device=dev, dtype=torch.float64)
-        if world > 1:
-            torch.distributed.all_reduce(tok_all)
-        engine["tok_s_all_gpus"] = round(float(tok_all.item()), 1)
+        wall_max, tok_rate = replica_rate(engine["tokens"], engine["wall_s"] * 1e3, dev, world)
+        engine["tok_s_all_gpus"] = round(tok_rate, 1)
+        engine["wall_s_max_over_gpus"] = round(wall_max / 1e3, 4)
         engine["n_gpus"] = world
         engine["scaling"] = "weak (each GPU serves its own chats)"
         if rank == 0 and world == 1 and not args.no_engine_cpu:
