@@ -1,7 +1,7 @@
 // Device-side building blocks shared by the paged-KV kernels (sm_100a).
 //
 // Inline PTX for: shared-memory mbarriers with bounded waits, TMA tile loads
-// (no cluster multicast anywhere: the library also runs in multi-process
+// (plain per-CTA TMA loads only: the library also runs in multi-process
 // replicas), ldmatrix / movmatrix, bf16 mma.sync, ex2.  Every wait is bounded:
 // after kSpinLimit polls it records PKV_DEVERR_TIMEOUT and gives up instead of
 // spinning forever.
