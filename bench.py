@@ -431,6 +431,9 @@ def engine_run(args, device, seed=0):
     runner = m.enable_decode_graphs(cache, max_batch=max(args.engine_chats, 1))
     for b in runner.buckets:  # capture outside the timed region
         runner._capture(b)
+    prunner = m.enable_prefill_graphs(cache, max_len=args.engine_prompt[1])
+    for b in prunner.buckets:
+        prunner._capture(b)
     g = torch.Generator().manual_seed(seed + 5)
     lo, hi = args.engine_prompt
     n = args.engine_chats
@@ -480,7 +483,7 @@ def engine_run(args, device, seed=0):
             gpu_prefill += ms
             t_roof += max(2 * nparams * B * T / flops_peak, (wbytes + kv * kv_tok) / bw)
     chat._kv_cache = None
-    del runner, m, cache
+    del runner, prunner, m, cache
     torch.cuda.empty_cache()
     return {"tok_s": round(toks / el, 1), "tokens": toks, "wall_s": round(el, 4),
             "decode_steps": decode_steps, "prefills": prefills,
@@ -493,7 +496,7 @@ def engine_run(args, device, seed=0):
             "config": f"config2: {n} chats, prompts U[{lo},{hi}] random ids, "
                       f"{args.engine_reply}-token replies, {args.engine_blocks}-block pool, "
                       f"random-init bf16 Qwen2.5-1.5B (std 0.02), temperature-1 sampling, "
-                      f"one prefill per tick (chat.py), CUDA-graph decode"}
+                      f"one prefill per tick (chat.py), CUDA-graph decode and prefill"}
 
 
 def engine_cpu_sample(seconds_budget=60.0):

@@ -80,6 +80,8 @@ const char* pkv_last_error(void);
  * q ignored).  q, k, v are [B][H][T][128] with strides (sb, sh, st).
  * A row with starts[b] < 0 is an inactive padding row (e.g. a batch padded
  * to a captured size): nothing is read, rotated or stored for it.
+ * q_lens (nullable, device int32 [B]): row b has only q_lens[b] <= T real
+ * tokens (right padding); tokens t >= q_lens[b] are skipped.
  */
 int pkv_append_rope(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
                     const void* k, int64_t k_sb, int64_t k_sh, int64_t k_st,
@@ -88,7 +90,7 @@ int pkv_append_rope(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
                     void* q_out, int64_t qo_sb, int64_t qo_sh, int64_t qo_st,
                     void* k_pool, void* v_pool, int64_t num_slots,
                     const int32_t* block_tables, int64_t table_pitch,
-                    const int32_t* seq_rows, const int32_t* starts,
+                    const int32_t* seq_rows, const int32_t* starts, const int32_t* q_lens,
                     int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
                     int32_t seq_len_q, int32_t head_dim,
                     int32_t* err_flag, void* stream);
@@ -132,11 +134,14 @@ int pkv_paged_decode(const void* q, int64_t q_sb, int64_t q_sh,
  * position i + kv_lens[b] - T (bottom-right causal, fa2.py:110-111); with
  * causal == 0 every query sees all kv_lens[b] keys.
  * q/out: [B][Hq][T][128] with strides (sb, sh, st).
+ * q_lens (nullable, device int32 [B]): row b has q_lens[b] <= T real queries
+ * at positions 0..q_lens[b]-1 (right padding); query i then sits at key
+ * i + kv_lens[b] - q_lens[b], and output rows i >= q_lens[b] are not written.
  */
 int pkv_paged_prefill(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
                       const void* k_pool, const void* v_pool, int64_t num_slots,
                       const int32_t* block_tables, int64_t table_pitch,
-                      const int32_t* seq_rows, const int32_t* kv_lens,
+                      const int32_t* seq_rows, const int32_t* kv_lens, const int32_t* q_lens,
                       int32_t max_kv_len, int32_t batch, int32_t seq_len_q,
                       int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
                       int32_t causal, float sm_scale,

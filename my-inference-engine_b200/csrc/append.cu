@@ -45,6 +45,7 @@ __global__ void __launch_bounds__(256) append_rope_kernel(const AppendLaunch a, 
 
   const int start = a.starts[b];
   if (start < 0) return;  // inactive (padding) row: nothing to rotate or store
+  if (a.q_lens && tt >= a.q_lens[b]) return;  // right padding of a shorter row
   const int pos = start + tt;
   const bool rope = a.rope_cos != nullptr;
   const int nq = a.q_out ? a.num_q_heads : 0;

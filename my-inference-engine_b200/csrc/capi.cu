@@ -167,7 +167,7 @@ int pkv_append_rope(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, con
                     int64_t rope_rows, void* q_out, int64_t qo_sb, int64_t qo_sh, int64_t qo_st,
                     void* k_pool, void* v_pool, int64_t num_slots, const int32_t* block_tables,
                     int64_t table_pitch, const int32_t* seq_rows, const int32_t* starts,
-                    int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t seq_len_q,
+                    const int32_t* q_lens, int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t seq_len_q,
                     int32_t head_dim, int32_t* err_flag, void* stream) {
   int st = check_heads(num_q_heads, num_kv_heads, head_dim);
   if (st) return st;
@@ -195,6 +195,7 @@ int pkv_append_rope(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, con
   a.q_out = q_out; a.qo_sb = qo_sb; a.qo_sh = qo_sh; a.qo_st = qo_st;
   a.k_pool = k_pool; a.v_pool = v_pool; a.num_slots = num_slots;
   a.tables = block_tables; a.pitch = table_pitch; a.rows = seq_rows; a.starts = starts;
+  a.q_lens = q_lens;
   a.batch = batch; a.num_q_heads = num_q_heads; a.num_kv_heads = num_kv_heads;
   a.seq_len_q = seq_len_q; a.err = err_flag;
   return launch_status(pkv::launch_append(a, static_cast<cudaStream_t>(stream)), "append_rope");
@@ -262,7 +263,8 @@ int pkv_paged_decode(const void* q, int64_t q_sb, int64_t q_sh, const void* k_po
 int pkv_paged_prefill(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, const void* k_pool,
                       const void* v_pool, int64_t num_slots, const int32_t* block_tables,
                       int64_t table_pitch, const int32_t* seq_rows, const int32_t* kv_lens,
-                      int32_t max_kv_len, int32_t batch, int32_t seq_len_q, int32_t num_q_heads,
+                      const int32_t* q_lens, int32_t max_kv_len, int32_t batch, int32_t seq_len_q,
+                      int32_t num_q_heads,
                       int32_t num_kv_heads, int32_t head_dim, int32_t causal, float sm_scale,
                       void* out, int64_t o_sb, int64_t o_sh, int64_t o_st, int32_t* err_flag,
                       void* stream) {
@@ -285,7 +287,7 @@ int pkv_paged_prefill(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, c
   pkv::PrefillLaunch a{};
   a.q = q; a.q_sb = q_sb; a.q_sh = q_sh; a.q_st = q_st;
   a.out = out; a.o_sb = o_sb; a.o_sh = o_sh; a.o_st = o_st;
-  a.kv_lens = kv_lens; a.batch = batch; a.seq_len_q = seq_len_q;
+  a.kv_lens = kv_lens; a.q_lens = q_lens; a.batch = batch; a.seq_len_q = seq_len_q;
   a.num_q_heads = num_q_heads; a.num_kv_heads = num_kv_heads; a.causal = causal ? 1 : 0;
   a.sm_scale = sm_scale; a.err = err_flag;
   return launch_prefill_any(a, src, static_cast<cudaStream_t>(stream));

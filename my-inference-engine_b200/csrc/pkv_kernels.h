@@ -60,6 +60,7 @@ struct PrefillLaunch {
   void* out;
   int64_t o_sb, o_sh, o_st;
   const int32_t* kv_lens;
+  const int32_t* q_lens;  // nullable: every row has seq_len_q queries
   int32_t batch, seq_len_q, num_q_heads, num_kv_heads;
   int32_t causal;
   float sm_scale;
@@ -88,6 +89,7 @@ struct AppendLaunch {
   int64_t pitch;
   const int32_t* rows;
   const int32_t* starts;
+  const int32_t* q_lens;  // nullable
   int32_t batch, num_q_heads, num_kv_heads, seq_len_q;
   int32_t* err;
 };

@@ -60,6 +60,7 @@ struct TcParams {
   __nv_bfloat16* out;
   int64_t o_sb, o_sh, o_st;
   const int32_t* kv_lens;
+  const int32_t* q_lens;  // nullable
   const int32_t* tables;
   int64_t pitch;
   const int32_t* rows;
@@ -167,7 +168,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int hq = blockIdx.y;
   const int kvh = hq / p.group;
   const int q0 = blockIdx.x * kRows;
-  const int T = p.T;
+  // this row's real query count (right padding beyond it is not written)
+  const int T = p.q_lens ? min(max(p.q_lens[blockIdx.z], 0), p.T) : p.T;
   const DevErr err{p.err};
 
   int kv_len = max(p.kv_lens[b], 0);
@@ -497,6 +499,7 @@ cudaError_t launch_prefill_tc(const PrefillLaunch& a, const CUtensorMap& qmap, c
   prm.o_sh = a.o_sh;
   prm.o_st = a.o_st;
   prm.kv_lens = a.kv_lens;
+  prm.q_lens = a.q_lens;
   prm.tables = src.tables;
   prm.pitch = src.pitch;
   prm.rows = src.rows;

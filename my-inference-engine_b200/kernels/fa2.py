@@ -66,7 +66,7 @@ def flash_attention(Q, K, V, is_causal=False, kv_lens=None, out=None):
         else:
             pagedkv.paged_prefill(Q, K.plane, V.plane, cache.block_tables, step.rows, kv_lens,
                                   step.max_kv_len, out, bool(is_causal), sm_scale, num_kv_heads,
-                                  cache.err_flag)
+                                  cache.err_flag, step.q_lens)
         return out
     # dense K/V: TMA needs 16-byte aligned rows
     def aligned(x):

@@ -46,6 +46,7 @@ class PagedStep:
     starts: torch.Tensor    # int32 [B] length before this step
     kv_lens: torch.Tensor   # int32 [B] starts + T
     max_kv_len: int         # host-side max(kv_lens), sizes decode grids
+    q_lens: torch.Tensor | None = None  # int32 [B] real tokens of right-padded rows
 
     @property
     def batch(self) -> int:
@@ -251,14 +252,14 @@ class KVCache(BlockTables):
         step = slot_mapping
         pagedkv.append_rope(None, k, v, None, None, None, self.buf[layer_idx, 0],
                             self.buf[layer_idx, 1], self.block_tables, step.rows, step.starts,
-                            self.err_flag)
+                            self.err_flag, step.q_lens)
 
     def append(self, layer_idx, step, q, k, v, rope_cos, rope_sin, q_out):
         """Fused apply_rope(q, k) + write (model.py:92-96): roped q goes to
         q_out, roped k and v into the pool.  rope_cos/sin: bf16 [positions, 128]."""
         pagedkv.append_rope(q, k, v, rope_cos, rope_sin, q_out, self.buf[layer_idx, 0],
                             self.buf[layer_idx, 1], self.block_tables, step.rows, step.starts,
-                            self.err_flag)
+                            self.err_flag, step.q_lens)
 
     def read(self, layer_idx, gather_idx):
         """This layer's K and V as zero-copy PagedKV handles (the reference

@@ -162,6 +162,7 @@ class Qwen2ForCausalLM(torch.nn.Module):
         self._rope = {}  # (device, dtype) -> (cos, sin) tables
         self._rope_retired = []  # outgrown tables stay alive: captured graphs may point at them
         self._graphs = {}  # id(cache) -> DecodeGraphs
+        self._prefill_graphs = {}  # id(cache) -> PrefillGraphs
 
     def rope_tables(self, num_positions, dtype, device):
         key = (str(device), dtype)
@@ -181,9 +182,14 @@ class Qwen2ForCausalLM(torch.nn.Module):
         A T == 1 step for which decode graphs were enabled (enable_decode_graphs)
         replays a captured CUDA graph; everything else runs eagerly."""
         _, T = input_ids.shape
-        runner = self._graphs.get(id(cache)) if T == 1 else None
-        if runner is not None and runner.covers(len(seqs)):
-            return runner.run(input_ids, seqs)[:, None]
+        if T == 1:
+            runner = self._graphs.get(id(cache))
+            if runner is not None and runner.covers(len(seqs)):
+                return runner.run(input_ids, seqs)[:, None]
+        else:
+            runner = self._prefill_graphs.get(id(cache))
+            if runner is not None and runner.covers(len(seqs), T):
+                return runner.run(input_ids, seqs)[:, None]
         if input_ids.device != cache.device:
             input_ids = input_ids.to(cache.device, non_blocking=True)
         starts_list, slot_mapping, gather_idx = cache.prepare(seqs, T)
@@ -203,7 +209,11 @@ class Qwen2ForCausalLM(torch.nn.Module):
         if not self.fused:
             for layer_idx, layer in enumerate(self.layers):
                 x = layer(x, cos, sin, None, is_causal, kv_lens, cache, layer_idx, step, step)
-            x = self.norm(x[:, -1:])
+            if step.q_lens is not None:  # right-padded rows: their last real token
+                x = x[torch.arange(B, device=x.device), step.q_lens.long() - 1][:, None]
+            else:
+                x = x[:, -1:]
+            x = self.norm(x)
             return x @ self.embed_tokens.weight.T
         # fused: residual add + RMSNorm in one kernel, the residual stream x
         # updated in place; same op order as QwenBlock.forward (model.py:131-138)
@@ -222,9 +232,14 @@ class Qwen2ForCausalLM(torch.nn.Module):
                 h = pagedkv.add_rmsnorm(m, xs, self.layers[layer_idx + 1].input_layernorm.weight,
                                         RMS_NORM_EPS, resid_out=xs)
         # last position only (model.py:204-206): x + mlp, then the final norm
-        last = T - 1
-        m_last = m.view(B, T, HIDDEN_SIZE)[:, last]
-        x_last = x.view(B, T, HIDDEN_SIZE)[:, last]
+        if step.q_lens is not None:  # right-padded rows: their last real token
+            rows = torch.arange(B, device=x.device)
+            last = step.q_lens.long() - 1
+            m_last = m.view(B, T, HIDDEN_SIZE)[rows, last]
+            x_last = x.view(B, T, HIDDEN_SIZE)[rows, last]
+        else:
+            m_last = m.view(B, T, HIDDEN_SIZE)[:, T - 1]
+            x_last = x.view(B, T, HIDDEN_SIZE)[:, T - 1]
         h = pagedkv.add_rmsnorm(m_last, x_last, self.norm.weight, RMS_NORM_EPS)
         return (h @ self.embed_tokens.weight.T)[:, None]
 
@@ -268,6 +283,13 @@ class Qwen2ForCausalLM(torch.nn.Module):
         self.fuse_weights_()
         self._graphs[id(cache)] = DecodeGraphs(self, cache, max_batch)
         return self._graphs[id(cache)]
+
+    def enable_prefill_graphs(self, cache, max_len=4096):
+        """Capture one-row prefills (chat.py admits one message per tick) per
+        padded length bucket, lazily on first use."""
+        self.fuse_weights_()
+        self._prefill_graphs[id(cache)] = PrefillGraphs(self, cache, max_len)
+        return self._prefill_graphs[id(cache)]
 
 
 def _buckets(max_batch):
@@ -351,3 +373,71 @@ class DecodeGraphs:
         g.replay()
         self.cache.advance(seqs, 1)
         return logits[:B, 0]
+
+
+class PrefillGraphs:
+    """CUDA graphs of a one-row prefill, one per padded length bucket.
+
+    A prompt of T tokens replays the graph of the smallest bucket Tp >= T:
+    the token ids are right-padded, and the step's q_lens (= T) makes the
+    append kernel store only the real tokens and the prefill kernel attend
+    (and write) only the real queries; the logits come from token T-1.  The
+    padded tail costs some GEMM work but removes the per-layer Python launch
+    overhead and the per-length GEMM heuristics of an eager prefill.
+    """
+
+    def __init__(self, model, cache, max_len):
+        self.model, self.cache = model, cache
+        self.capacity = cache.table_pitch * cache.block_size
+        top = min(max_len, self.capacity)
+        self.buckets = []
+        b = 64
+        while b < top:
+            self.buckets.append(b)
+            b *= 2
+        self.buckets.append(top)
+        self.graphs = {}
+        self.pool = torch.cuda.graph_pool_handle()
+
+    def covers(self, B, T):
+        return B == 1 and 1 < T <= self.buckets[-1]
+
+    def _capture(self, Tp):
+        from kv_cache import PagedStep
+
+        dev = self.cache.device
+        ids = torch.zeros(1, Tp, dtype=torch.int32, device=dev)
+        meta = torch.zeros(4, 1, dtype=torch.int32, device=dev)  # row, start, kv_len, q_len
+        meta[1].fill_(-1)  # inactive until a real prompt is copied in
+        step = PagedStep(self.cache, Tp, [0], meta[0], meta[1], meta[2], self.capacity,
+                         q_lens=meta[3])
+        host = torch.zeros(4 + Tp, dtype=torch.int32, pin_memory=True)
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self.model.forward_step(ids.long(), self.cache, step)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=self.pool):
+            logits = self.model.forward_step(ids.long(), self.cache, step)
+        self.graphs[Tp] = (g, ids, meta, host, logits)
+        return self.graphs[Tp]
+
+    def run(self, input_ids, seqs):
+        T = input_ids.shape[1]
+        Tp = next(b for b in self.buckets if b >= T)
+        g, ids, meta, host, logits = self.graphs.get(Tp) or self._capture(Tp)
+        starts, rows = self.cache.step_rows(seqs, T)
+        self.cache.flush_tables()
+        host[0], host[1], host[2], host[3] = rows[0], starts[0], starts[0] + T, T
+        if not input_ids.is_cuda:
+            host[4:4 + T] = input_ids.view(-1).to(torch.int32)
+        meta.view(-1).copy_(host[:4], non_blocking=True)
+        if input_ids.is_cuda:
+            ids[0, :T].copy_(input_ids.view(-1))
+        else:
+            ids.view(-1).copy_(host[4:4 + Tp], non_blocking=True)
+        g.replay()
+        self.cache.advance(seqs, T)
+        return logits[:, 0]

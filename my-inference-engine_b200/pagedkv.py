@@ -38,15 +38,15 @@ _SIGNATURES = {
     "pkv_last_error": ([], ctypes.c_char_p),
     "pkv_append_rope": (
         [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64,
-         _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _vp,
+         _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _vp,
          _i32, _i32, _i32, _i32, _i32, _vp, _vp], ctypes.c_int),
     "pkv_decode_workspace_size": ([_i32, _i32, _i32, _i32], ctypes.c_size_t),
     "pkv_paged_decode": (
         [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
          ctypes.c_float, _vp, _i64, _i64, _vp, ctypes.c_size_t, _vp, _vp], ctypes.c_int),
     "pkv_paged_prefill": (
-        [_vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
-         _i32, _i32, ctypes.c_float, _vp, _i64, _i64, _i64, _vp, _vp], ctypes.c_int),
+        [_vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
+         _i32, _i32, _i32, ctypes.c_float, _vp, _i64, _i64, _i64, _vp, _vp], ctypes.c_int),
     "pkv_add_rmsnorm": (
         [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, ctypes.c_float, _vp],
         ctypes.c_int),
@@ -139,7 +139,7 @@ def append_rope(q: torch.Tensor | None, k: torch.Tensor, v: torch.Tensor,
                 rope_cos: torch.Tensor | None, rope_sin: torch.Tensor | None,
                 q_out: torch.Tensor | None, k_plane: torch.Tensor, v_plane: torch.Tensor,
                 tables: torch.Tensor, rows: torch.Tensor | None, starts: torch.Tensor,
-                err: torch.Tensor | None = None) -> None:
+                err: torch.Tensor | None = None, q_lens: torch.Tensor | None = None) -> None:
     """pkv_append_rope.  q/k/v/q_out are [B, H, T, 128] bf16 views; the pool
     planes are [num_slots, Hkv, 128] bf16; tables [rows, pitch] int32."""
     B, Hkv, T, D = k.shape
@@ -151,7 +151,7 @@ def append_rope(q: torch.Tensor | None, k: torch.Tensor, v: torch.Tensor,
         _ptr(v), v.stride(0), v.stride(1), v.stride(2),
         _ptr(rope_cos), _ptr(rope_sin), rope_cos.shape[0] if rope_cos is not None else 0,
         _ptr(q_out), qos[0], qos[1], qos[2], _ptr(k_plane), _ptr(v_plane), k_plane.shape[0],
-        _ptr(tables), tables.stride(0), _ptr(rows), _ptr(starts),
+        _ptr(tables), tables.stride(0), _ptr(rows), _ptr(starts), _ptr(q_lens),
         B, Hq, Hkv, T, D, _ptr(err), _stream(k.device))
     _check(st, "pkv_append_rope")
 
@@ -174,12 +174,14 @@ def paged_decode(q: torch.Tensor, k_plane: torch.Tensor, v_plane: torch.Tensor,
 def paged_prefill(q: torch.Tensor, k_plane: torch.Tensor, v_plane: torch.Tensor,
                   tables: torch.Tensor, rows: torch.Tensor | None, kv_lens: torch.Tensor,
                   max_kv_len: int, out: torch.Tensor, causal: bool, sm_scale: float,
-                  num_kv_heads: int, err: torch.Tensor | None = None) -> None:
-    """pkv_paged_prefill.  q, out: [B, Hq, T, 128]."""
+                  num_kv_heads: int, err: torch.Tensor | None = None,
+                  q_lens: torch.Tensor | None = None) -> None:
+    """pkv_paged_prefill.  q, out: [B, Hq, T, 128]; q_lens: right-padded rows."""
     B, Hq, T, D = q.shape
     st = lib().pkv_paged_prefill(
         _ptr(q), q.stride(0), q.stride(1), q.stride(2), _ptr(k_plane), _ptr(v_plane),
-        k_plane.shape[0], _ptr(tables), tables.stride(0), _ptr(rows), _ptr(kv_lens), max_kv_len,
+        k_plane.shape[0], _ptr(tables), tables.stride(0), _ptr(rows), _ptr(kv_lens),
+        _ptr(q_lens), max_kv_len,
         B, T, Hq, num_kv_heads, D, int(causal), sm_scale, _ptr(out), out.stride(0),
         out.stride(1), out.stride(2), _ptr(err), _stream(q.device))
     _check(st, "pkv_paged_prefill")

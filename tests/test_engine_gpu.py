@@ -107,3 +107,38 @@ def test_engine_serves_chats_with_eviction(cuda, small_model):
         chat.MAX_REPLY_TOKENS, chat.STOP_SEQUENCES = saved
         chat._kv_cache = None
         m._graphs.clear()
+
+
+def test_prefill_graph_matches_eager(cuda, small_model):
+    """One-row prefills replayed from padded-length graphs give the eager
+    prefill's logits and K/V (up to GEMM rounding), and only real tokens land
+    in the pool."""
+    from kv_cache import KVCache
+
+    m = small_model.fuse_weights_()
+    g = torch.Generator().manual_seed(2)
+    prompts = [torch.randint(0, 151936, (n,), generator=g).tolist() for n in (70, 5, 200, 64)]
+    res = []
+    for use_graph in (False, True):
+        c = KVCache(96, 16, cuda, torch.bfloat16)
+        if use_graph:
+            m.enable_prefill_graphs(c, max_len=256)
+        seqs = [c.alloc() for _ in prompts]
+        with torch.no_grad():
+            lg = [m(torch.tensor([p], device=cuda), c, [s])[:, -1].float()
+                  for s, p in zip(seqs, prompts)]
+            # a decode step on top (eager) sees the same history
+            lg.append(m(torch.tensor([[1], [2], [3], [4]], device=cuda), c, seqs)[:, -1].float())
+        torch.cuda.synchronize()
+        c.check_errors()
+        res.append((lg, c))
+    m._prefill_graphs.clear()
+    (la, ca), (lb, cb) = res
+    for a, b in zip(la, lb):
+        assert float((a - b).abs().max()) < 0.05
+        assert torch.equal(a.argmax(-1), b.argmax(-1))
+    assert float((ca.buf.float() - cb.buf.float()).abs().max()) < 0.05
+    used = {x for t in cb._block_tables.values() for x in t}
+    unused = [x for x in range(cb.num_blocks) if x not in used]
+    view = cb.buf.view(cb.buf.shape[0], 2, cb.num_blocks, 16, -1)
+    assert int(view[:, :, unused].count_nonzero()) == 0

@@ -61,8 +61,8 @@ def test_entry_points_reject_bad_arguments_without_a_gpu():
                             16, 0, 0, None, 0, None, None)
     assert st == 2 and b"head_dim" in L.pkv_last_error()
     # Hq not a multiple of Hkv -> PKV_ERR_INVALID
-    st = L.pkv_paged_prefill(16, 0, 0, 0, 16, 16, 16, 16, 1, None, 16, 1, 1, 1, 12, 5, 128, 1,
-                             1.0, 16, 0, 0, 0, None, None)
+    st = L.pkv_paged_prefill(16, 0, 0, 0, 16, 16, 16, 16, 1, None, 16, None, 1, 1, 1, 12, 5, 128,
+                             1, 1.0, 16, 0, 0, 0, None, None)
     assert st == 1
     # misaligned pool plane -> PKV_ERR_ALIGN
     st = L.pkv_paged_decode(16, 0, 0, 18, 16, 16, 16, 1, None, 16, 1, 1, 12, 2, 128, 1.0,
@@ -70,5 +70,5 @@ def test_entry_points_reject_bad_arguments_without_a_gpu():
     assert st == 3
     # num_slots not a multiple of 16 -> PKV_ERR_INVALID
     st = L.pkv_append_rope(None, 0, 0, 0, 16, 0, 0, 0, 16, 0, 0, 0, None, None, 0, None, 0, 0, 0,
-                           16, 16, 17, 16, 1, None, 16, 1, 12, 2, 1, 128, None, None)
+                           16, 16, 17, 16, 1, None, 16, None, 1, 12, 2, 1, 128, None, None)
     assert st == 1

@@ -142,3 +142,49 @@ def test_left_padded_batched_prefill(cuda):
                                           k[b:b + 1, :, :n].float().numpy(),
                                           v[b:b + 1, :, :n].float().numpy(), [n], True)
         assert max_err(out[b:b + 1, :, T - n:], want) < TOL
+
+
+def test_right_padded_rows_with_q_lens(cuda):
+    """q_lens: row b has q_lens[b] real queries at the front of a padded T
+    (query i sits at key i + kv_len - q_len); padded output rows are untouched."""
+    import pagedkv
+
+    g = torch.Generator().manual_seed(31)
+    prior, qlen, T = [0, 300, 17, 64], [5, 130, 128, 1], 160
+    B = len(prior)
+    N = sum(math.ceil((p + T) / 16) for p in prior) + 8
+    cache = build_cache(N, torch.randperm(N, generator=g).tolist(), cuda)
+    cache.buf.fill_(cases.PAD_VALUE)
+    seqs = [cache.alloc() for _ in prior]
+    hk = [torch.randn(1, 2, n, 128, generator=g).to(torch.bfloat16) for n in prior]
+    hv = [torch.randn(1, 2, n, 128, generator=g).to(torch.bfloat16) for n in prior]
+    write_history(cache, seqs, hk, hv)
+    kn = torch.randn(B, 2, T, 128, generator=g).to(torch.bfloat16)
+    vn = torch.randn(B, 2, T, 128, generator=g).to(torch.bfloat16)
+    q = torch.randn(B, 12, T, 128, generator=g).to(torch.bfloat16)
+    starts, rows = cache.step_rows(seqs, T)
+    cache.flush_tables()
+    st = torch.tensor(starts, dtype=torch.int32, device=cuda)
+    ql = torch.tensor(qlen, dtype=torch.int32, device=cuda)
+    rows_d = torch.tensor(rows, dtype=torch.int32, device=cuda)
+    pool_before = cache.buf[0].clone()
+    pagedkv.append_rope(None, kn.to(cuda), vn.to(cuda), None, None, None, cache.buf[0, 0],
+                        cache.buf[0, 1], cache.block_tables, rows_d, st, cache.err_flag, ql)
+    out = torch.full((B, 12, T, 128), 7.0, dtype=torch.bfloat16, device=cuda)
+    pagedkv.paged_prefill(q.to(cuda), cache.buf[0, 0], cache.buf[0, 1], cache.block_tables,
+                          rows_d, st + ql, max(p + n for p, n in zip(prior, qlen)), out, True,
+                          1 / math.sqrt(128), 2, cache.err_flag, ql)
+    torch.cuda.synchronize()
+    cache.check_errors()
+    for b in range(B):
+        n = qlen[b]
+        kd = torch.cat([hk[b], kn[b:b + 1, :, :n]], 2)
+        vd = torch.cat([hv[b], vn[b:b + 1, :, :n]], 2)
+        want = attention_ref.attention_np(q[b:b + 1, :, :n].float().numpy(), kd.float().numpy(),
+                                          vd.float().numpy(), [prior[b] + n], True)
+        assert max_err(out[b:b + 1, :, :n], want) < TOL, b
+        assert bool((out[b, :, n:] == 7.0).all()), "padded query rows must not be written"
+    # padded tokens were not stored: only the real tokens' slots changed
+    changed = (cache.buf[0] != pool_before).any(-1).any(-1).any(0)  # [slots]
+    expect = sum(qlen)
+    assert int(changed.sum()) <= expect
