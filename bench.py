@@ -65,6 +65,11 @@ def parse():
     ap.add_argument("--engine-blocks", type=int, default=1024)
     ap.add_argument("--no-engine-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-engine4", action="store_true")
+    ap.add_argument("--engine4-chats", type=int, default=1024)
+    ap.add_argument("--engine4-prompt", type=int, nargs=2, default=[32, 4096])
+    ap.add_argument("--engine4-reply", type=int, default=128)
+    ap.add_argument("--engine4-pool-gb", type=float, default=120.0)
     ap.add_argument("--prefill-steps", type=int, default=20)
     return ap.parse_args()
 
@@ -412,38 +417,39 @@ class _CountingModel:
         return out
 
 
-def engine_run(args, device, seed=0):
-    """BASELINE config 2 through chat.py: N concurrent chats, uniform random
-    prompts, fixed-length replies (EOS and stop sequences off, as
-    metrics/benchmark_concurrency.py:122,143 does), temperature-1 sampling,
-    the reference's 1024-block (448 MB) pool.  Returns tok/s and a roofline."""
+def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_batch,
+               rank=0, world=1, seed=0):
+    """Serve `chats_total` chats through chat.py (uniform random token-id prompts
+    in `prompt_range`, `reply`-token replies with EOS and stop sequences off as
+    metrics/benchmark_concurrency.py:122,143 does, temperature-1 sampling, one
+    prefill per tick).  Rank r serves chats i with i % world == r from one
+    seeded prompt set, on its own model replica and `blocks`-block pool.
+    Returns this rank's tokens, wall time and a roofline."""
     import chat
     import model as M
     from kv_cache import KVCache
 
-    torch.manual_seed(seed)
+    torch.manual_seed(seed + rank)
     m = M.Qwen2ForCausalLM().to(device, torch.bfloat16).eval()
     random_init_(m, seed + 11)
-    cache = KVCache(args.engine_blocks, 16, device, torch.bfloat16)
+    cache = KVCache(blocks, 16, device, torch.bfloat16)
     chat.init(kv_cache=cache, start_worker=False)
     chat.STOP_SEQUENCES = []
-    chat.MAX_REPLY_TOKENS = args.engine_reply
-    runner = m.enable_decode_graphs(cache, max_batch=max(args.engine_chats, 1))
+    lo, hi = prompt_range
+    runner = m.enable_decode_graphs(cache, max_batch=max_batch)
     for b in runner.buckets:  # capture outside the timed region
         runner._capture(b)
-    prunner = m.enable_prefill_graphs(cache, max_len=args.engine_prompt[1])
+    prunner = m.enable_prefill_graphs(cache, max_len=hi)
     for b in prunner.buckets:
         prunner._capture(b)
     g = torch.Generator().manual_seed(seed + 5)
-    lo, hi = args.engine_prompt
-    n = args.engine_chats
     prompts = [torch.randint(0, M.VOCAB_SIZE, (int(torch.randint(lo, hi + 1, (1,), generator=g)),),
-                             generator=g).tolist() for _ in range(n + 1)]
+                             generator=g).tolist() for _ in range(chats_total + 1)]
     tok = SyntheticTokenizer(prompts)
     cm = _CountingModel(m, cache)
 
-    def one_round(idx, reply):
-        chat.MAX_REPLY_TOKENS = reply
+    def one_round(idx, nreply):
+        chat.MAX_REPLY_TOKENS = nreply
         chats = []
         for i in idx:
             c = chat.Chat(tok)
@@ -459,9 +465,10 @@ def engine_run(args, device, seed=0):
             c.release()
         return el, toks
 
-    one_round([n], 4)  # warm-up: eager prefill path, sampling, one graph bucket
+    one_round([chats_total], 4)  # warm-up: sampling, one graph of each kind
     cm.calls.clear()
-    el, toks = one_round(list(range(n)), args.engine_reply)
+    mine = [i for i in range(chats_total) if i % world == rank]
+    el, toks = one_round(mine, reply)
     torch.cuda.synchronize()
     nparams = sum(p.numel() for p in m.parameters())
     wbytes = nparams * 2
@@ -493,8 +500,8 @@ def engine_run(args, device, seed=0):
             "roofline_tok_s": round(toks / t_roof, 1), "frac": round(t_roof / el, 4),
             "roofline_basis": "per call: decode = (weights + KV read) / measured HBM; "
                               "prefill = max(2*params*tokens / measured bf16 peak, bytes / HBM)",
-            "config": f"config2: {n} chats, prompts U[{lo},{hi}] random ids, "
-                      f"{args.engine_reply}-token replies, {args.engine_blocks}-block pool, "
+            "config": f"{label}: {chats_total} chats ({len(mine)} on this GPU), prompts "
+                      f"U[{lo},{hi}] random ids, {reply}-token replies, {blocks}-block pool, "
                       f"random-init bf16 Qwen2.5-1.5B (std 0.02), temperature-1 sampling, "
                       f"one prefill per tick (chat.py), CUDA-graph decode and prefill"}
 
@@ -631,14 +638,35 @@ def main():
     del w
     torch.cuda.empty_cache()
     prefill = None if args.no_prefill else prefill_run(args, dev, seed=args.seed)
-    engine = None
+    engine = engine4 = None
     if not args.no_engine:
-        engine = engine_run(args, dev, seed=args.seed + rank)
+        # config 2 on every GPU (weak scaling: 16 chats per GPU)
+        engine = engine_run(dev, label="config2", chats_total=args.engine_chats,
+                            prompt_range=args.engine_prompt, reply=args.engine_reply,
+                            blocks=args.engine_blocks, max_batch=max(args.engine_chats, 1),
+                            seed=args.seed + rank)
         wall_max, tok_rate = replica_rate(engine["tokens"], engine["wall_s"] * 1e3, dev, world)
         engine["tok_s_all_gpus"] = round(tok_rate, 1)
         engine["wall_s_max_over_gpus"] = round(wall_max / 1e3, 4)
         engine["n_gpus"] = world
         engine["scaling"] = "weak (each GPU serves its own chats)"
+    if not args.no_engine4:
+        # config 4: 1024 chats split round-robin over the GPUs (strong scaling)
+        block_bytes = L * 2 * 16 * HKV * D * 2
+        per_gpu = -(-args.engine4_chats // world)
+        need = per_gpu * -(-(args.engine4_prompt[1] + args.engine4_reply + 1) // 16) + 64
+        blocks = int(min(need, args.engine4_pool_gb * 1e9 // block_bytes))
+        engine4 = engine_run(dev, label="config4", chats_total=args.engine4_chats,
+                             prompt_range=args.engine4_prompt, reply=args.engine4_reply,
+                             blocks=blocks, max_batch=256, rank=rank, world=world,
+                             seed=args.seed)
+        toks_all = cross_rank(engine4["tokens"], torch.distributed.ReduceOp.SUM if world > 1 else None,
+                              dev, world)
+        wall_max = cross_rank(engine4["wall_s"], torch.distributed.ReduceOp.MAX if world > 1 else None,
+                              dev, world)
+        engine4.update({"tok_s_all_gpus": round(toks_all / wall_max, 1),
+                        "tokens_all_gpus": int(toks_all), "wall_s_max_over_gpus": round(wall_max, 4),
+                        "n_gpus": world, "scaling": "strong (1024 chats split over the GPUs)"})
         if rank == 0 and world == 1 and not args.no_engine_cpu:
             torch.set_num_threads(os.cpu_count() or 1)
             engine["cpu_baseline"] = engine_cpu_sample()
@@ -676,7 +704,7 @@ def main():
                 "data": "synthetic", "config": config, "roofline": roofline,
                 "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
                 "gpu_launches": args.steps * layers * 2,
-                "kv_bytes_per_step": step_bytes, "prefill": prefill, "engine": engine}
+                "kv_bytes_per_step": step_bytes, "prefill": prefill, "engine": engine, "engine_config4": engine4}
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
