@@ -51,6 +51,7 @@ struct DecodeParams {
   int32_t group;       // query heads per KV head
   int32_t sub_groups;  // CTAs per KV head (group > 8)
   int32_t max_parts;   // grid.x: partitions available to every row
+  int32_t min_blocks_per_part;
   float scale_log2;
   float* part_o;
   float* part_lse;
@@ -106,11 +107,12 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
     }
     return;
   }
-  // Every row spreads over up to gridDim.x partitions, sized from its own
-  // length (a multiple of the warp count, at least one block per warp): the
-  // grid is planned for the longest row (or a captured capacity), short rows
-  // still get enough CTAs to hide latency.
-  const int per = (nblk + p.max_parts - 1) / p.max_parts;
+  // Every row splits into up to gridDim.x equal partitions of at least
+  // min_blocks_per_part blocks (rounded to the warp count), sized from its own
+  // length: the grid is planned for the longest row (or a captured capacity),
+  // shorter rows use fewer partitions instead of tiny ones.
+  const int np = min(p.max_parts, max(1, nblk / p.min_blocks_per_part));
+  const int per = (nblk + np - 1) / np;
   const int bpp = max(kDecodeWarps, (per + kDecodeWarps - 1) / kDecodeWarps * kDecodeWarps);
   const int nparts = (nblk + bpp - 1) / bpp;
   if (part >= nparts) return;
@@ -379,14 +381,22 @@ int64_t decode_max_units() { return kDecodeMaxUnits; }
 
 namespace {
 
-// The grid's partition count: enough CTAs to give every SM several waves of
-// 2 resident CTAs for the longest row.  Partitions of >= 16 blocks (256
-// tokens) keep the per-CTA set-up and merge cost amortised whenever that
-// still yields kTargetCtas / 4 CTAs; smaller (latency-bound) launches go
-// down to one block per warp.  The kernel sizes each row's partitions from
-// the row's own length within this count.
-constexpr int kTargetCtas = 148 * 2 * 6;
-constexpr int kMinBlocksPerPart = 16;
+// Partition plan.  Every (row, KV head) unit gets up to kMaxParts
+// partitions, enough for kTargetCtas CTAs in total (several waves of 2
+// resident CTAs per SM).  A partition holds at least kMinBlocksPerPart blocks
+// (8 per warp) when the launch has work for kBusyCtas CTAs of that size, so
+// per-CTA set-up and the split-K merge stay amortised; smaller launches (few
+// rows, short contexts: latency-bound) go down to 16 or 4 blocks.
+#ifndef PKV_DECODE_TARGET_CTAS
+#define PKV_DECODE_TARGET_CTAS (148 * 2 * 6)
+#endif
+#ifndef PKV_DECODE_MIN_BLOCKS_PER_PART
+#define PKV_DECODE_MIN_BLOCKS_PER_PART 32
+#endif
+constexpr int kTargetCtas = PKV_DECODE_TARGET_CTAS;
+constexpr int kMinBlocksPerPart = PKV_DECODE_MIN_BLOCKS_PER_PART;
+constexpr int kMaxParts = 16;
+constexpr int64_t kBusyCtas = 600;
 constexpr int kMinBlocksPerPartSmall = kDecodeWarps;
 
 template <bool kPaged>
@@ -417,12 +427,18 @@ DecodePlan plan_decode(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
   const int64_t units = static_cast<int64_t>(batch) * num_kv_heads * pl.sub_groups;
   const int nblk = max(1, (max_kv_len + kBlockTokens - 1) / kBlockTokens);
   const int64_t units1 = units > 0 ? units : 1;
-  int64_t parts = (kTargetCtas + units1 - 1) / units1;
+  const int64_t want = (kTargetCtas + units1 - 1) / units1;
+  const int64_t parts = want < kMaxParts ? want : kMaxParts;
+  int min_bpp = kMinBlocksPerPartSmall;
+  if (units * (nblk / kMinBlocksPerPart) >= kBusyCtas)
+    min_bpp = kMinBlocksPerPart;
+  else if (units * (nblk / 16) >= kBusyCtas)
+    min_bpp = 16;
   int bpp = static_cast<int>((nblk + parts - 1) / parts);
-  const int64_t ctas_at_16 = units * ((nblk + kMinBlocksPerPart - 1) / kMinBlocksPerPart);
-  bpp = max(bpp, ctas_at_16 >= kTargetCtas / 4 ? kMinBlocksPerPart : kMinBlocksPerPartSmall);
+  bpp = max(bpp, min_bpp);
   bpp = (bpp + kDecodeWarps - 1) / kDecodeWarps * kDecodeWarps;
   pl.blocks_per_part = bpp;
+  pl.min_blocks_per_part = min_bpp;
   pl.max_parts = (nblk + bpp - 1) / bpp;
   if (pl.max_parts > 1) {
     const int64_t slots = units * pl.max_parts;
@@ -451,6 +467,7 @@ cudaError_t launch_decode(const DecodeLaunch& a, const KVSource& src, const Deco
   prm.group = a.num_q_heads / a.num_kv_heads;
   prm.sub_groups = plan.sub_groups;
   prm.max_parts = plan.max_parts;
+  prm.min_blocks_per_part = plan.min_blocks_per_part;
   prm.scale_log2 = a.sm_scale * 1.4426950408889634f;
   prm.err = a.err;
   if (plan.max_parts > 1) {

@@ -38,6 +38,7 @@ struct DecodePlan {
   int32_t sub_groups;       // ceil(group / 8): CTAs sharing one KV head
   int32_t blocks_per_part;  // 16-token blocks per split-K partition
   int32_t max_parts;        // grid.x
+  int32_t min_blocks_per_part;  // a row's partitions hold at least this many blocks
   size_t workspace_bytes;   // 0 when max_parts == 1
 };
 
