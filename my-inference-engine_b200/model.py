@@ -376,7 +376,8 @@ class DecodeGraphs:
 
 
 class PrefillGraphs:
-    """CUDA graphs of a one-row prefill, one per padded length bucket.
+    """CUDA graphs of a one-row prefill, one per padded length bucket
+    (64, 128, 256, 512, then every 256 tokens).
 
     A prompt of T tokens replays the graph of the smallest bucket Tp >= T:
     the token ids are right-padded, and the step's q_lens (= T) makes the
@@ -390,11 +391,11 @@ class PrefillGraphs:
         self.model, self.cache = model, cache
         self.capacity = cache.table_pitch * cache.block_size
         top = min(max_len, self.capacity)
-        self.buckets = []
+        self.buckets = []  # 64, 128, 256, 512, then every 256 tokens: < 1/3 padding
         b = 64
         while b < top:
             self.buckets.append(b)
-            b *= 2
+            b = b * 2 if b < 512 else b + 256
         self.buckets.append(top)
         self.graphs = {}
         self.pool = torch.cuda.graph_pool_handle()
