@@ -7,7 +7,8 @@
 // rounded to bf16 before the PV product (fa2.py:145), O / l at the end
 // (fa2.py:151).
 //
-//   grid  = (ceil(T/128), Hq, B): one CTA per 128 query rows of one head
+//   grid  = (Hq, B, ceil(T/128)): one CTA per 128 query rows of one head,
+//           heaviest (last) q-tiles first
 //   block = 6 warps
 //     warp 0    TMA producer (one thread): Q tile once, then 128-key K/V
 //               tiles (eight 16-token blocks each, through the block table)
@@ -164,12 +165,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int b = blockIdx.z;
-  const int hq = blockIdx.y;
+  // grid (Hq, B, q-tiles) with the q-tile index slowest and reversed: the
+  // heaviest causal tiles (most keys) are scheduled first, the light ones
+  // fill in behind them
+  const int hq = blockIdx.x;
+  const int b = blockIdx.y;
   const int kvh = hq / p.group;
-  const int q0 = blockIdx.x * kRows;
+  const int q0 = (gridDim.z - 1 - blockIdx.z) * kRows;
   // this row's real query count (right padding beyond it is not written)
-  const int T = p.q_lens ? min(max(p.q_lens[blockIdx.z], 0), p.T) : p.T;
+  const int T = p.q_lens ? min(max(p.q_lens[b], 0), p.T) : p.T;
   const DevErr err{p.err};
 
   int kv_len = max(p.kv_lens[b], 0);
@@ -178,7 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = p.rows ? p.rows[b] : b;
     trow = p.tables + static_cast<int64_t>(row) * p.pitch;
     if (kv_len > p.pitch * kBlockTokens) {
-      if (tid == 0 && blockIdx.x == 0 && hq == 0) err.raise(PKV_DEVERR_POSITION);
+      if (tid == 0 && q0 == 0 && hq == 0) err.raise(PKV_DEVERR_POSITION);
       kv_len = static_cast<int>(p.pitch) * kBlockTokens;
     }
   }
@@ -509,7 +513,7 @@ cudaError_t launch_prefill_tc(const PrefillLaunch& a, const CUtensorMap& qmap, c
   prm.causal = a.causal;
   prm.scale_log2 = a.sm_scale * 1.4426950408889634f;
   prm.err = a.err;
-  dim3 grid((a.seq_len_q + kRows - 1) / kRows, a.num_q_heads, a.batch);
+  dim3 grid(a.num_q_heads, a.batch, (a.seq_len_q + kRows - 1) / kRows);
   return src.paged ? launch_tc_t<true>(prm, qmap, src, grid, stream)
                    : launch_tc_t<false>(prm, qmap, src, grid, stream);
 }
