@@ -228,6 +228,70 @@ int pkv_paged_decode_static_scratch(const void* q, int64_t q_sb, int64_t q_sh,
                                     void* out, int64_t o_sb, int64_t o_sh,
                                     int32_t* err_flag, void* stream);
 
+/*
+ * Skinny linear layers for decode-sized batches (tcgen05 tensor cores).
+ *
+ * y[m, n] = x[m, :] . w[n, :] (+ bias[n]) for m < rows <= PKV_LINEAR_MAX_ROWS,
+ * the nn.Linear projections of the Qwen2 block (model.py:83-86, :114-116)
+ * when a decode step (or a short prefill) feeds them a few rows: the weight
+ * matrix is read from HBM once, split over the SMs along n and k.  x, w and
+ * y are bf16, rows with element strides (multiples of 8), 16-byte aligned;
+ * n % 128 == 0, k % 64 == 0.  Accumulation is fp32; split-k partial sums are
+ * added in a fixed order, so results are deterministic.
+ *
+ * The workspace (device memory, pkv_linear_workspace_size bytes, 16-byte
+ * aligned) holds fp32 partial sums; every entry below takes it.  The fused
+ * variants apply, to the bf16-rounded GEMM output, exactly the arithmetic of
+ * the separate entry they replace:
+ *   pkv_linear_add_rmsnorm  GEMM, then pkv_add_rmsnorm (o_proj / down_proj
+ *                           followed by the next residual add + RMSNorm)
+ *   pkv_linear_silu_mul     merged gate/up GEMM (w rows [0, inter) gate,
+ *                           [inter, 2 inter) up), then pkv_silu_mul
+ *   pkv_linear_rope_append  merged q/k/v GEMM + bias, then pkv_append_rope
+ *                           (rows = batch * seq_len_q, row b*seq_len_q + t)
+ */
+#define PKV_LINEAR_MAX_ROWS 256
+
+/* Weight layouts (w_layout) of the pkv_linear* entries. */
+#define PKV_W_ROWMAJOR 0 /* w[n][k], element row stride ldw                        */
+#define PKV_W_TILED 1    /* [n/128][k/64][128][64] contiguous (ldw unused): every
+                            128x64 tile one 16 KiB run, so the GEMM streams each
+                            CTA's share of w as one contiguous range of HBM;
+                            made by pkv_linear_pack_weight                         */
+
+size_t pkv_linear_workspace_size(int32_t rows, int32_t n, int32_t k);
+
+/* Copy a row-major w[n][k] (row stride ldw) into the PKV_W_TILED layout
+ * (n * k bf16 elements at w_tiled, 16-byte aligned). */
+int pkv_linear_pack_weight(const void* w, int64_t ldw, int32_t n, int32_t k, void* w_tiled,
+                           void* stream);
+
+int pkv_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, int32_t w_layout,
+               const void* bias, int32_t rows, int32_t n, int32_t k, void* y, int64_t ldy,
+               void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream);
+
+int pkv_linear_add_rmsnorm(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                           int32_t w_layout, int32_t rows, int32_t n, int32_t k,
+                           const void* resid, int64_t r_stride, void* resid_out,
+                           int64_t ro_stride, const void* norm_weight, float eps, void* out,
+                           int64_t o_stride, void* workspace, size_t workspace_bytes,
+                           int32_t* err_flag, void* stream);
+
+int pkv_linear_silu_mul(const void* x, int64_t ldx, const void* w_gate_up, int64_t ldw,
+                        int32_t w_layout, int32_t rows, int32_t inter, int32_t k, void* out,
+                        int64_t o_stride, void* workspace, size_t workspace_bytes,
+                        int32_t* err_flag, void* stream);
+
+int pkv_linear_rope_append(const void* x, int64_t ldx, const void* w_qkv, int64_t ldw,
+                           int32_t w_layout, const void* bias, int32_t k, const void* rope_cos,
+                           const void* rope_sin, int64_t rope_rows, void* q_out, int64_t qo_sb,
+                           int64_t qo_sh, int64_t qo_st, void* k_pool, void* v_pool,
+                           int64_t num_slots, const int32_t* block_tables, int64_t table_pitch,
+                           const int32_t* seq_rows, const int32_t* starts, const int32_t* q_lens,
+                           int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                           int32_t seq_len_q, int32_t head_dim, void* workspace,
+                           size_t workspace_bytes, int32_t* err_flag, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -12,6 +12,9 @@
 //
 // One warp per (row, step token, head-of-{q, k, v}); lane l owns dims
 // {2l, 2l+1} and their rotation partners {64+2l, 64+2l+1}.
+// q/k/v come either from bf16 tensors (any strides) or from the fp32 split-k
+// partial sums of the merged q/k/v GEMM (linear_tc.cu) plus the q/k/v bias,
+// rounded to bf16 once: the value F.linear(x, w_qkv, b_qkv) stores.
 #include "pkv_device.cuh"
 #include "pkv_kernels.h"
 
@@ -30,7 +33,20 @@ __device__ __forceinline__ __nv_bfloat16 rope1(__nv_bfloat16 x, __nv_bfloat16 c,
   return rn(__fadd_rn(bf(xc), bf(rs)));
 }
 
+// bf16(sum of the split-k partials + bias) for columns col, col+1 of one row
+__device__ __forceinline__ __nv_bfloat162 parts_pair(const AppendLaunch& a, int64_t row, int col) {
+  float2 acc = sum_splits2(a.part + row * a.part_ld + col, a.parts, a.part_slice);
+  const __nv_bfloat16* bias = static_cast<const __nv_bfloat16*>(a.qkv_bias);
+  if (bias) {
+    acc.x += bf(bias[col]);
+    acc.y += bf(bias[col + 1]);
+  }
+  return __floats2bfloat162_rn(acc.x, acc.y);
+}
+
 __global__ void __launch_bounds__(256) append_rope_kernel(const AppendLaunch a, int32_t num_blocks) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int lane = threadIdx.x & 31;
   const int64_t item = gid >> 5;
@@ -51,11 +67,14 @@ __global__ void __launch_bounds__(256) append_rope_kernel(const AppendLaunch a, 
   const int nq = a.q_out ? a.num_q_heads : 0;
 
   // source row and destination row for this item
-  const __nv_bfloat16* src;
+  const __nv_bfloat16* src = nullptr;
   __nv_bfloat16* dst;
   bool do_rope = rope;
+  int col0;  // partial mode: first column of this head in the q/k/v GEMM output
   if (which < nq) {
-    src = static_cast<const __nv_bfloat16*>(a.q) + b * a.q_sb + which * a.q_sh + tt * a.q_st;
+    col0 = which * kHeadDim;
+    if (!a.part)
+      src = static_cast<const __nv_bfloat16*>(a.q) + b * a.q_sb + which * a.q_sh + tt * a.q_st;
     dst = static_cast<__nv_bfloat16*>(a.q_out) + b * a.qo_sb + which * a.qo_sh + tt * a.qo_st;
   } else {
     const bool is_k = which < nq + a.num_kv_heads;
@@ -74,18 +93,29 @@ __global__ void __launch_bounds__(256) append_rope_kernel(const AppendLaunch a, 
     }
     const int64_t slot = static_cast<int64_t>(blk) * kBlockTokens + (pos & 15);
     if (is_k) {
-      src = static_cast<const __nv_bfloat16*>(a.k) + b * a.k_sb + h * a.k_sh + tt * a.k_st;
+      col0 = (a.num_q_heads + h) * kHeadDim;
+      if (!a.part)
+        src = static_cast<const __nv_bfloat16*>(a.k) + b * a.k_sb + h * a.k_sh + tt * a.k_st;
       dst = static_cast<__nv_bfloat16*>(a.k_pool) + (slot * a.num_kv_heads + h) * kHeadDim;
     } else {
-      src = static_cast<const __nv_bfloat16*>(a.v) + b * a.v_sb + h * a.v_sh + tt * a.v_st;
+      col0 = (a.num_q_heads + a.num_kv_heads + h) * kHeadDim;
+      if (!a.part)
+        src = static_cast<const __nv_bfloat16*>(a.v) + b * a.v_sb + h * a.v_sh + tt * a.v_st;
       dst = static_cast<__nv_bfloat16*>(a.v_pool) + (slot * a.num_kv_heads + h) * kHeadDim;
       do_rope = false;
     }
   }
 
   const int d = 2 * lane;
-  const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(src + d);
-  const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(src + 64 + d);
+  __nv_bfloat162 lo, hi;
+  if (a.part) {
+    const int64_t prow = static_cast<int64_t>(b) * a.seq_len_q + tt;
+    lo = parts_pair(a, prow, col0 + d);
+    hi = parts_pair(a, prow, col0 + 64 + d);
+  } else {
+    lo = *reinterpret_cast<const __nv_bfloat162*>(src + d);
+    hi = *reinterpret_cast<const __nv_bfloat162*>(src + 64 + d);
+  }
   if (!do_rope) {
     *reinterpret_cast<__nv_bfloat162*>(dst + d) = lo;
     *reinterpret_cast<__nv_bfloat162*>(dst + 64 + d) = hi;
@@ -119,8 +149,8 @@ cudaError_t launch_append(const AppendLaunch& a, cudaStream_t stream) {
   if (warps == 0) return cudaSuccess;
   const int64_t blocks = (warps * 32 + 255) / 256;
   const int32_t num_blocks = static_cast<int32_t>(a.num_slots / kBlockTokens);
-  append_rope_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a, num_blocks);
-  return cudaGetLastError();
+  return launch_k(append_rope_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, a,
+                  num_blocks);
 }
 
 }  // namespace pkv

@@ -133,6 +133,92 @@ int launch_status(cudaError_t e, const char* what) {
   return ok();
 }
 
+// Rows of a [rows][k] bf16 matrix (element row stride ld) -> 2-D map,
+// box {64, box_rows}, 128B swizzle; rows past `rows` read as zeros.
+int encode_rows(CUtensorMap* m, const void* base, int64_t rows, int64_t k, int64_t ld,
+                int32_t box_rows) {
+  EncodeFn fn = encode_fn();
+  if (!fn) return fail(PKV_ERR_DRIVER, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PKV_ERR_DRIVER, "matrix tensor map encode failed (%d)", (int)r);
+  return PKV_OK;
+}
+
+// PKV_W_TILED weight [n/128][k/64][128][64] -> 3-D map over {64, 128, tiles*chunks},
+// box {64, 128, 1}: one contiguous 16 KiB run per box.
+int encode_tiled(CUtensorMap* m, const void* base, int32_t n, int32_t k) {
+  EncodeFn fn = encode_fn();
+  if (!fn) return fail(PKV_ERR_DRIVER, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[3] = {64, 128, static_cast<cuuint64_t>(n / 128) * (k / 64)};
+  cuuint64_t strides[2] = {128, 128 * 128};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PKV_ERR_DRIVER, "tiled weight map encode failed (%d)", (int)r);
+  return PKV_OK;
+}
+
+int check_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, int32_t w_layout,
+                 int32_t rows, int32_t n, int32_t k) {
+  if (!x || !w) return fail(PKV_ERR_INVALID, "null x or w");
+  if (w_layout != PKV_W_ROWMAJOR && w_layout != PKV_W_TILED)
+    return fail(PKV_ERR_INVALID, "unknown weight layout %d", w_layout);
+  if (w_layout == PKV_W_TILED) ldw = k;
+  if (rows < 0 || rows > PKV_LINEAR_MAX_ROWS)
+    return fail(PKV_ERR_UNSUPPORTED, "rows must be in [0, %d] (got %d)", PKV_LINEAR_MAX_ROWS, rows);
+  if (n <= 0 || n % 128 != 0 || k <= 0 || k % 64 != 0)
+    return fail(PKV_ERR_UNSUPPORTED, "n must be a positive multiple of 128 and k of 64 (got %d, %d)",
+                n, k);
+  if (ldx < k || ldw < k) return fail(PKV_ERR_INVALID, "row strides smaller than k");
+  if (!aligned16(x) || !aligned16(w) || !mult8(ldx) || !mult8(ldw))
+    return fail(PKV_ERR_ALIGN, "x / w must be 16-byte aligned with strides that are multiples of 8");
+  return PKV_OK;
+}
+
+// The GEMM half of every pkv_linear* entry.  direct: y (+ bias) in bf16 when
+// the plan has one split; otherwise fp32 partials into the workspace.
+int run_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, int32_t w_layout,
+               int32_t rows, int32_t n, int32_t k, bool allow_direct, void* y, int64_t ldy, const void* bias,
+               void* workspace, size_t workspace_bytes, int32_t* err, cudaStream_t stream,
+               pkv::LinearPlan* plan_out, bool* direct_out) {
+  const pkv::LinearPlan pl = pkv::plan_linear(rows, n, k);
+  const bool direct = allow_direct && pl.splits == 1;
+  if (!direct) {
+    if (!workspace || workspace_bytes < pl.part_bytes)
+      return fail(PKV_ERR_WORKSPACE, "linear needs %zu workspace bytes, got %zu", pl.part_bytes,
+                  workspace ? workspace_bytes : (size_t)0);
+    if (!aligned16(workspace)) return fail(PKV_ERR_ALIGN, "workspace not 16-byte aligned");
+  }
+  CUtensorMap wmap, xmap;
+  int st = w_layout == PKV_W_TILED ? encode_tiled(&wmap, w, n, k)
+                                   : encode_rows(&wmap, w, n, k, ldw, 128);
+  if (st) return st;
+  if ((st = encode_rows(&xmap, x, rows, k, ldx, pl.mpad))) return st;
+  pkv::LinearLaunch a{};
+  a.M = rows;
+  a.N = n;
+  a.direct = direct ? 1 : 0;
+  a.y = y;
+  a.ldy = ldy;
+  a.bias = bias;
+  a.part = static_cast<float*>(workspace);
+  a.w_tiled = w_layout == PKV_W_TILED ? 1 : 0;
+  a.err = err;
+  st = launch_status(pkv::launch_linear(a, pl, wmap, xmap, stream), "linear_tc");
+  if (st) return st;
+  *plan_out = pl;
+  *direct_out = direct;
+  return PKV_OK;
+}
+
 int launch_prefill_any(const pkv::PrefillLaunch& a, const pkv::KVSource& src, cudaStream_t s) {
   CUtensorMap qmap;
   int st = encode_q(&qmap, a.q, a.batch, a.num_q_heads, a.seq_len_q, a.q_sb, a.q_sh, a.q_st);
@@ -402,6 +488,155 @@ int pkv_paged_decode_static_scratch(const void* q, int64_t q_sb, int64_t q_sh, c
   a.max_kv_len = max_kv_len; a.sm_scale = sm_scale; a.err = err_flag;
   return launch_status(pkv::launch_decode_static(a, src, plan, static_cast<cudaStream_t>(stream)),
                        "paged_decode_static_scratch");
+}
+
+size_t pkv_linear_workspace_size(int32_t rows, int32_t n, int32_t k) {
+  if (rows <= 0 || rows > PKV_LINEAR_MAX_ROWS || n <= 0 || n % 128 != 0 || k <= 0 || k % 64 != 0)
+    return 0;
+  return pkv::plan_linear(rows, n, k).part_bytes;
+}
+
+int pkv_linear_pack_weight(const void* w, int64_t ldw, int32_t n, int32_t k, void* w_tiled,
+                           void* stream) {
+  if (!w || !w_tiled) return fail(PKV_ERR_INVALID, "null w or w_tiled");
+  if (n <= 0 || n % 128 != 0 || k <= 0 || k % 64 != 0)
+    return fail(PKV_ERR_UNSUPPORTED, "n must be a positive multiple of 128 and k of 64 (got %d, %d)",
+                n, k);
+  if (ldw < k) return fail(PKV_ERR_INVALID, "row stride smaller than k");
+  if (!aligned16(w) || !aligned16(w_tiled) || !mult8(ldw))
+    return fail(PKV_ERR_ALIGN, "w / w_tiled must be 16-byte aligned, ldw a multiple of 8");
+  return launch_status(pkv::launch_pack_weight(w, ldw, n, k, w_tiled,
+                                               static_cast<cudaStream_t>(stream)),
+                       "pack_weight");
+}
+
+int pkv_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, int32_t w_layout,
+               const void* bias, int32_t rows, int32_t n, int32_t k, void* y, int64_t ldy,
+               void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream) {
+  int st = check_linear(x, ldx, w, ldw, w_layout, rows, n, k);
+  if (st) return st;
+  if (!y) return fail(PKV_ERR_INVALID, "null y");
+  if (!aligned16(y) || !mult8(ldy) || ldy < n || (bias && !aligned16(bias)))
+    return fail(PKV_ERR_ALIGN, "y / bias must be 16-byte aligned, ldy a multiple of 8 >= n");
+  if (rows == 0) return ok();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  pkv::LinearPlan pl;
+  bool direct;
+  if ((st = run_linear(x, ldx, w, ldw, w_layout, rows, n, k, true, y, ldy, bias, workspace,
+                       workspace_bytes, err_flag, s, &pl, &direct)))
+    return st;
+  if (direct) return ok();
+  return launch_status(pkv::launch_splitk_reduce(static_cast<const float*>(workspace), pl.splits,
+                                                 rows, n, bias, y, ldy, s),
+                       "splitk_reduce");
+}
+
+int pkv_linear_add_rmsnorm(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                           int32_t w_layout, int32_t rows, int32_t n, int32_t k,
+                           const void* resid, int64_t r_stride, void* resid_out,
+                           int64_t ro_stride, const void* norm_weight, float eps, void* out,
+                           int64_t o_stride, void* workspace, size_t workspace_bytes,
+                           int32_t* err_flag, void* stream) {
+  int st = check_linear(x, ldx, w, ldw, w_layout, rows, n, k);
+  if (st) return st;
+  if (!norm_weight || !out) return fail(PKV_ERR_INVALID, "null norm weight or out");
+  if (n > 4096) return fail(PKV_ERR_UNSUPPORTED, "add_rmsnorm dim must be <= 4096 (got %d)", n);
+  if (!aligned16(norm_weight) || !aligned16(out) || (resid && !aligned16(resid)) ||
+      (resid_out && !aligned16(resid_out)) || !mult8(o_stride) || (resid && !mult8(r_stride)) ||
+      (resid_out && !mult8(ro_stride)))
+    return fail(PKV_ERR_ALIGN, "add_rmsnorm rows must be 16-byte aligned");
+  if (rows == 0) return ok();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  pkv::LinearPlan pl;
+  bool direct;
+  if ((st = run_linear(x, ldx, w, ldw, w_layout, rows, n, k, false, nullptr, 0, nullptr,
+                       workspace, workspace_bytes, err_flag, s, &pl, &direct)))
+    return st;
+  pkv::NormLaunch p{};
+  p.a = nullptr; p.a_stride = n;
+  p.resid = resid; p.r_stride = r_stride; p.resid_out = resid_out; p.ro_stride = ro_stride;
+  p.weight = norm_weight; p.out = out; p.o_stride = o_stride;
+  p.rows = rows; p.dim = n; p.eps = eps;
+  p.part = static_cast<const float*>(workspace);
+  p.parts = pl.splits;
+  p.part_slice = static_cast<int64_t>(rows) * n;
+  return launch_status(pkv::launch_add_rmsnorm(p, s), "add_rmsnorm");
+}
+
+int pkv_linear_silu_mul(const void* x, int64_t ldx, const void* w_gate_up, int64_t ldw,
+                        int32_t w_layout, int32_t rows, int32_t inter, int32_t k, void* out,
+                        int64_t o_stride, void* workspace, size_t workspace_bytes,
+                        int32_t* err_flag, void* stream) {
+  if (inter <= 0 || inter % 64 != 0)
+    return fail(PKV_ERR_UNSUPPORTED, "inter must be a positive multiple of 64 (got %d)", inter);
+  const int32_t n = 2 * inter;
+  int st = check_linear(x, ldx, w_gate_up, ldw, w_layout, rows, n, k);
+  if (st) return st;
+  if (!out) return fail(PKV_ERR_INVALID, "null out");
+  if (!aligned16(out) || !mult8(o_stride)) return fail(PKV_ERR_ALIGN, "silu_mul rows must be 16-byte aligned");
+  if (rows == 0) return ok();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  pkv::LinearPlan pl;
+  bool direct;
+  if ((st = run_linear(x, ldx, w_gate_up, ldw, w_layout, rows, n, k, false, nullptr, 0, nullptr,
+                       workspace, workspace_bytes, err_flag, s, &pl, &direct)))
+    return st;
+  return launch_status(pkv::launch_silu_mul(nullptr, n, out, o_stride, rows, inter, s,
+                                            static_cast<const float*>(workspace), pl.splits,
+                                            static_cast<int64_t>(rows) * n),
+                       "silu_mul");
+}
+
+int pkv_linear_rope_append(const void* x, int64_t ldx, const void* w_qkv, int64_t ldw,
+                           int32_t w_layout, const void* bias, int32_t k, const void* rope_cos,
+                           const void* rope_sin, int64_t rope_rows, void* q_out, int64_t qo_sb,
+                           int64_t qo_sh, int64_t qo_st, void* k_pool, void* v_pool,
+                           int64_t num_slots,
+                           const int32_t* block_tables, int64_t table_pitch,
+                           const int32_t* seq_rows, const int32_t* starts, const int32_t* q_lens,
+                           int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                           int32_t seq_len_q, int32_t head_dim, void* workspace,
+                           size_t workspace_bytes, int32_t* err_flag, void* stream) {
+  int st = check_heads(num_q_heads, num_kv_heads, head_dim);
+  if (st) return st;
+  if ((st = check_pool(k_pool, v_pool, num_slots, block_tables, table_pitch))) return st;
+  if (batch < 0 || seq_len_q < 0) return fail(PKV_ERR_INVALID, "negative batch / seq_len_q");
+  const int64_t rows64 = static_cast<int64_t>(batch) * seq_len_q;
+  if (rows64 > PKV_LINEAR_MAX_ROWS)
+    return fail(PKV_ERR_UNSUPPORTED, "batch * seq_len_q must be <= %d (got %lld)",
+                PKV_LINEAR_MAX_ROWS, (long long)rows64);
+  const int32_t rows = static_cast<int32_t>(rows64);
+  const int32_t n = (num_q_heads + 2 * num_kv_heads) * head_dim;
+  if ((st = check_linear(x, ldx, w_qkv, ldw, w_layout, rows, n, k))) return st;
+  if (!starts || !q_out || !rope_cos || !rope_sin)
+    return fail(PKV_ERR_INVALID, "null starts, q_out or rope tables");
+  if (rope_rows <= 0) return fail(PKV_ERR_INVALID, "rope_rows must be positive");
+  if ((reinterpret_cast<uintptr_t>(q_out) | reinterpret_cast<uintptr_t>(rope_cos) |
+       reinterpret_cast<uintptr_t>(rope_sin)) & 3u ||
+      (bias && (reinterpret_cast<uintptr_t>(bias) & 3u)))
+    return fail(PKV_ERR_ALIGN, "append pointers must be 4-byte aligned");
+  if ((qo_sb | qo_sh | qo_st) & 1) return fail(PKV_ERR_ALIGN, "q_out strides must be even");
+  if (rows == 0) return ok();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  pkv::LinearPlan pl;
+  bool direct;
+  if ((st = run_linear(x, ldx, w_qkv, ldw, w_layout, rows, n, k, false, nullptr, 0, nullptr,
+                       workspace, workspace_bytes, err_flag, s, &pl, &direct)))
+    return st;
+  pkv::AppendLaunch a{};
+  a.rope_cos = rope_cos; a.rope_sin = rope_sin; a.rope_rows = rope_rows;
+  a.q_out = q_out; a.qo_sb = qo_sb; a.qo_sh = qo_sh; a.qo_st = qo_st;
+  a.k_pool = k_pool; a.v_pool = v_pool; a.num_slots = num_slots;
+  a.tables = block_tables; a.pitch = table_pitch; a.rows = seq_rows; a.starts = starts;
+  a.q_lens = q_lens;
+  a.batch = batch; a.num_q_heads = num_q_heads; a.num_kv_heads = num_kv_heads;
+  a.seq_len_q = seq_len_q; a.err = err_flag;
+  a.part = static_cast<const float*>(workspace);
+  a.parts = pl.splits;
+  a.part_slice = static_cast<int64_t>(rows) * n;
+  a.part_ld = n;
+  a.qkv_bias = bias;
+  return launch_status(pkv::launch_append(a, s), "append_rope");
 }
 
 }  // extern "C"

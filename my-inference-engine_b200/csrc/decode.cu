@@ -84,6 +84,8 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
   const int nheads = min(kMaxHeadsPerCta, p.group - sub * kMaxHeadsPerCta);
   const int part = blockIdx.x;
   const DevErr err{p.err};
+  pdl_trigger();
+  pdl_wait();
 
   int kv_len = max(p.kv_lens[b], 0);
   int nblk = (kv_len + kBlockTokens - 1) / kBlockTokens;
@@ -413,8 +415,8 @@ cudaError_t launch_decode_t(const DecodeParams& prm, const KVSource& src, dim3 g
     if (e != cudaSuccess) return e;
     configured_device = dev;
   }
-  kern<<<grid, kDecodeWarps * 32, smem, stream>>>(prm, src.kmap, src.vmap);
-  return cudaGetLastError();
+  return launch_k(kern, grid, dim3(kDecodeWarps * 32), static_cast<size_t>(smem), stream, prm,
+                  src.kmap, src.vmap);
 }
 
 }  // namespace

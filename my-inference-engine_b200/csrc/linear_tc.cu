@@ -1,0 +1,318 @@
+// Skinny linear layers on the 5th-generation tensor cores (tcgen05 + TMEM,
+// sm_100a): y[M, N] = x[M, K] . W[N, K]^T for the row counts of a decode
+// step (M <= 256), where reading W once from HBM is the whole cost.
+//
+// The Qwen2 block's projections (model.py:83-86 q/k/v/o, :114-116 gate/up/down)
+// are nn.Linear layers; torch runs them as cuBLAS GEMMs whose tiles are shaped
+// for large M.  Here the roles are swapped: the weight tile is the MMA's
+// M side (128 rows of W) and the batch rows are its N side (M padded to a
+// multiple of 16 by TMA zero fill), so one tcgen05.mma per 16-wide K step
+// covers the whole batch and every CTA streams its own slice of W exactly once.
+//
+//   grid  = (N / 128, splits): CTA (t, s) owns W rows [128t, 128t+128) and an
+//           equal share of the K/64 chunks; splits is chosen so that the grid
+//           fills the SMs once
+//   block = 6 warps
+//     warp 0    TMA producer (one thread): per chunk one 128x64 W box
+//               (evict-first: streamed once) and one Mpad x 64 x box
+//               (evict-last: every CTA reads it) into a stages-deep ring.
+//               W is row-major [N][K] (a box = 128 pieces of 128 B, one per
+//               row) or packed as [N/128][K/64][128][64] (PKV_W_TILED), where
+//               a box is one contiguous 16 KiB run and a CTA's chunks are
+//               adjacent: each CTA then streams one contiguous range of HBM
+//     warp 1    owns TMEM (Mpad columns, fp32) and issues the MMAs:
+//               D[128, Mpad] += W[128, 16] . x[Mpad, 16]^T, 4 per chunk
+//     warps 2-5 epilogue: warp w reads TMEM lanes 32*(w%4).., i.e. one W row
+//               (one output feature n) per thread, all batch rows as columns
+// Output: either y itself in bf16 (+ bias) when there is one split, or fp32
+// partial sums part[s][m][n] that the consumer kernel adds up in split order
+// (deterministic) before its own epilogue: plain bias + bf16 store here, or
+// the residual add + RMSNorm, SwiGLU and RoPE + K/V append kernels.
+// Every wait is bounded.
+#include "pkv_device.cuh"
+#include "pkv_kernels.h"
+#include "tc_device.cuh"
+
+namespace pkv {
+namespace {
+
+constexpr int kTileN = 128;            // W rows per CTA (MMA M)
+constexpr int kChunkK = 64;            // K elements per stage: one 128 B swizzle row
+constexpr int kWBytes = kTileN * 128;  // 16 KiB W box per stage
+constexpr int kLinThreads = 192;
+constexpr int kMaxStages = 8;
+constexpr int kSmemCap = 227 * 1024;
+
+__device__ __forceinline__ float bf(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+struct LinParams {
+  void* out;  // bf16 [M][ldo] (direct) or fp32 [splits][M][N] partials
+  int64_t ldo;
+  const __nv_bfloat16* bias;  // direct mode only; nullable
+  int32_t M, N, chunks, splits, stages, mpad;
+  uint32_t tmem_cols, idesc;
+  int32_t direct;
+  int32_t w_tiled;  // W packed as [N/128][K/64][128][64]: one contiguous 16 KiB box per chunk
+  int32_t* err;
+};
+
+__global__ void __launch_bounds__(kLinThreads, 1)
+    linear_tc_kernel(const LinParams p, const __grid_constant__ CUtensorMap wmap,
+                     const __grid_constant__ CUtensorMap xmap) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const int stage_bytes = kWBytes + p.mpad * 128;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * stage_bytes);
+  uint64_t* empty = full + p.stages;
+  uint64_t* done = empty + p.stages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x, split = blockIdx.y;
+  const int c0 = static_cast<int>(static_cast<int64_t>(split) * p.chunks / p.splits);
+  const int nc = static_cast<int>(static_cast<int64_t>(split + 1) * p.chunks / p.splits) - c0;
+  const DevErr err{p.err};
+  pdl_trigger();
+
+  if (tid == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&full[s], 1);   // producer's arrive.expect_tx
+      mbar_init(&empty[s], 1);  // tcgen05.commit after the chunk's MMAs
+    }
+    mbar_init(done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, p.tmem_cols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&wmap);
+      prefetch_tmap(&xmap);
+      const uint64_t once = policy_evict_first();
+      const uint64_t keep = policy_evict_last();
+      const uint32_t bytes = static_cast<uint32_t>(stage_bytes);
+      auto load_w = [&](int i, int st) {
+        uint8_t* sw = smem + st * stage_bytes;
+        mbar_arrive_expect_tx(&full[st], bytes);  // W + x land on the same barrier
+        if (p.w_tiled)
+          tma_load_3d(sw, &wmap, &full[st], 0, 0, tile * p.chunks + c0 + i, once);
+        else
+          tma_load_2d(sw, &wmap, &full[st], (c0 + i) * kChunkK, tile * kTileN, once);
+      };
+      auto load_x = [&](int i, int st) {
+        tma_load_2d(smem + st * stage_bytes + kWBytes, &xmap, &full[st], (c0 + i) * kChunkK, 0, keep);
+      };
+      // The weights do not depend on earlier kernels: fill the ring with W
+      // before waiting for the predecessor grid, then load x.
+      const int pre = nc < p.stages ? nc : p.stages;
+      for (int i = 0; i < pre; ++i) load_w(i, i);
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) load_x(i, i);
+      for (int i = pre; i < nc; ++i) {
+        const int st = i % p.stages;
+        if (!mbar_wait(&empty[st], ((i / p.stages) - 1) & 1, err)) break;
+        load_w(i, st);
+        load_x(i, st);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      for (int i = 0; i < nc; ++i) {
+        const int st = i % p.stages;
+        if (!mbar_wait(&full[st], (i / p.stages) & 1, err)) break;
+        tc_fence_after();
+        const uint32_t sw = smem_u32(smem + st * stage_bytes);
+        const uint32_t sx = sw + kWBytes;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma(tmem, sdesc(sw + kk * 32, 16, 1024), sdesc(sx + kk * 32, 16, 1024), p.idesc,
+               (i > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&empty[st]);
+      }
+      umma_commit(done);
+      mbar_wait(done, 0, err);  // every MMA retired before TMEM is freed
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int n = tile * kTileN + quarter * 32 + lane;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    if (__all_sync(0xffffffffu, mbar_wait(done, 0, err))) {
+      tc_fence_after();
+      if (p.direct) {
+        const float b = p.bias ? bf(p.bias[n]) : 0.f;
+        __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.out) + n;
+        for (int c = 0; c < p.mpad; c += 16) {
+          float v[16];
+          tmem_ld16(taddr + c, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (c + e < p.M) y[(c + e) * p.ldo] = __float2bfloat16_rn(v[e] + b);
+        }
+      } else {
+        float* y = static_cast<float*>(p.out) + static_cast<int64_t>(split) * p.M * p.N + n;
+        for (int c = 0; c < p.mpad; c += 16) {
+          float v[16];
+          tmem_ld16(taddr + c, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (c + e < p.M) y[static_cast<int64_t>(c + e) * p.N] = v[e];
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, p.tmem_cols);
+  }
+}
+
+// y[m][n] = bf16(sum_s part[s][m][n] + bias[n]), splits summed in order.
+__global__ void __launch_bounds__(256)
+    splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N,
+                         const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ y,
+                         int64_t ldy) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int per_row = N / 4;
+  if (i >= static_cast<int64_t>(M) * per_row) return;
+  const int m = static_cast<int>(i / per_row);
+  const int n = static_cast<int>(i % per_row) * 4;
+  const int64_t slice = static_cast<int64_t>(M) * N;
+  const float4 acc = sum_splits4(part + static_cast<int64_t>(m) * N + n, splits, slice);
+  float4 v = acc;
+  if (bias) {
+    v.x += bf(bias[n + 0]);
+    v.y += bf(bias[n + 1]);
+    v.z += bf(bias[n + 2]);
+    v.w += bf(bias[n + 3]);
+  }
+  uint2 o;
+  o.x = pack_bf16(v.x, v.y);
+  o.y = pack_bf16(v.z, v.w);
+  *reinterpret_cast<uint2*>(y + static_cast<int64_t>(m) * ldy + n) = o;
+}
+
+// w[n][k] (row stride ldw) -> [n/128][k/64][128][64]; one thread per 16 bytes
+__global__ void __launch_bounds__(256)
+    pack_weight_kernel(const __nv_bfloat16* __restrict__ w, int64_t ldw, int chunks,
+                       int64_t total16, __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total16) return;
+  const int j8 = static_cast<int>(i & 7);
+  const int r = static_cast<int>((i >> 3) & 127);
+  const int64_t tc = i >> 10;  // tile * chunks + chunk
+  const int c = static_cast<int>(tc % chunks);
+  const int64_t t = tc / chunks;
+  const uint4 v = *reinterpret_cast<const uint4*>(w + (t * kTileN + r) * ldw + c * kChunkK + j8 * 8);
+  *reinterpret_cast<uint4*>(out + i * 8) = v;
+}
+
+int sm_count() {
+  static int count = 0;
+  if (count == 0) {
+    int dev = 0, c = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && c > 0)
+      count = c;
+    else
+      return 148;
+  }
+  return count;
+}
+
+}  // namespace
+
+LinearPlan plan_linear(int32_t M, int32_t N, int32_t K) {
+  LinearPlan pl{};
+  pl.mpad = (M + 15) / 16 * 16;
+  if (pl.mpad < 16) pl.mpad = 16;
+  pl.tiles = N / kTileN;
+  pl.chunks = K / kChunkK;
+  const int stage_bytes = kWBytes + pl.mpad * 128;
+  // two CTAs per SM while the ring still holds >= 4 stages, else one
+  const int per_sm = (pl.mpad <= 64) ? 2 : 1;
+  const int budget = (per_sm == 2 ? kSmemCap / 2 : kSmemCap) - 1024 - 256;
+  pl.stages = budget / stage_bytes;
+  if (pl.stages > kMaxStages) pl.stages = kMaxStages;
+  pl.smem_bytes = pl.stages * stage_bytes + (2 * pl.stages + 1) * 8 + 16 + 1024;
+  // as many splits as still fit one wave of CTAs (a second wave would run alone)
+  const int wave = sm_count() * per_sm;
+  int splits = wave / (pl.tiles > 0 ? pl.tiles : 1);
+  const int max_splits = pl.chunks / 2 > 0 ? pl.chunks / 2 : 1;
+  if (splits > max_splits) splits = max_splits;
+  if (splits < 1) splits = 1;
+  pl.splits = splits;
+  uint32_t cols = 32;
+  while (cols < static_cast<uint32_t>(pl.mpad)) cols <<= 1;
+  pl.tmem_cols = cols;
+  pl.part_bytes = static_cast<size_t>(splits) * M * N * sizeof(float);
+  return pl;
+}
+
+cudaError_t launch_linear(const LinearLaunch& a, const LinearPlan& pl, const CUtensorMap& wmap,
+                          const CUtensorMap& xmap, cudaStream_t stream) {
+  static int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(linear_tc_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap);
+    if (e != cudaSuccess) return e;
+    configured_device = dev;
+  }
+  LinParams p{};
+  p.direct = a.direct;
+  p.w_tiled = a.w_tiled;
+  p.out = a.direct ? a.y : a.part;
+  p.ldo = a.ldy;
+  p.bias = static_cast<const __nv_bfloat16*>(a.bias);
+  p.M = a.M;
+  p.N = a.N;
+  p.chunks = pl.chunks;
+  p.splits = pl.splits;
+  p.stages = pl.stages;
+  p.mpad = pl.mpad;
+  p.tmem_cols = pl.tmem_cols;
+  // kind::f16 instruction descriptor: fp32 D, bf16 A and B, both K-major,
+  // N = mpad (>> 3 at bit 17), M = 128 (>> 4 at bit 24)
+  p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((static_cast<uint32_t>(pl.mpad) >> 3) << 17) |
+            ((static_cast<uint32_t>(kTileN) >> 4) << 24);
+  p.err = a.err;
+  return launch_k(linear_tc_kernel, dim3(pl.tiles, pl.splits), dim3(kLinThreads),
+                  static_cast<size_t>(pl.smem_bytes), stream, p, wmap, xmap);
+}
+
+cudaError_t launch_pack_weight(const void* w, int64_t ldw, int32_t n, int32_t k, void* out,
+                               cudaStream_t stream) {
+  const int64_t total16 = static_cast<int64_t>(n) * k / 8;
+  return launch_k(pack_weight_kernel, dim3(static_cast<unsigned>((total16 + 255) / 256)),
+                  dim3(256), 0, stream, static_cast<const __nv_bfloat16*>(w), ldw, k / kChunkK,
+                  total16, static_cast<__nv_bfloat16*>(out));
+}
+
+cudaError_t launch_splitk_reduce(const float* part, int32_t splits, int32_t M, int32_t N,
+                                 const void* bias, void* y, int64_t ldy, cudaStream_t stream) {
+  const int64_t n = static_cast<int64_t>(M) * (N / 4);
+  if (n == 0) return cudaSuccess;
+  return launch_k(splitk_reduce_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256),
+                  0, stream, part, splits, M, N, static_cast<const __nv_bfloat16*>(bias),
+                  static_cast<__nv_bfloat16*>(y), ldy);
+}
+
+}  // namespace pkv

@@ -11,6 +11,9 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
+
+#include <utility>
 
 #include "../../include/pagedkv.h"
 
@@ -72,7 +75,53 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   return false;
 }
 
+// ---------------------------------------------------------------- PDL
+// Programmatic dependent launch: every kernel of the library is launched
+// with programmatic stream serialisation, so it may start while its
+// predecessor on the stream is still running.  pdl_trigger lets the next
+// kernel launch; pdl_wait blocks until the predecessor grid has completed and
+// its writes are visible.  A kernel touches no memory that an earlier kernel
+// writes or reads before its pdl_wait (constant weights excepted); without the
+// launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Host: launch `kern` with the programmatic-serialisation attribute (unless
+// the environment sets PKV_PDL=0).
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("PKV_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                     cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // ---------------------------------------------------------------- TMA
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "l"(policy)
+      : "memory");
+}
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1, int c2, uint64_t policy) {
   asm volatile(
@@ -141,6 +190,54 @@ __device__ __forceinline__ float ex2(float x) {
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Sum of the fp32 split-k partials p[s * slice] (4 or 2 consecutive floats)
+// over s = 0..n-1, added strictly in split order (so every consumer rounds
+// the same value); loads are issued four splits ahead of the adds.
+__device__ __forceinline__ float4 sum_splits4(const float* p, int n, int64_t slice) {
+  float4 a = *reinterpret_cast<const float4*>(p);
+  int s = 1;
+  for (; s + 4 <= n; s += 4) {
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const float4*>(p + (s + u) * slice);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      a.x += v[u].x;
+      a.y += v[u].y;
+      a.z += v[u].z;
+      a.w += v[u].w;
+    }
+  }
+  for (; s < n; ++s) {
+    const float4 v = *reinterpret_cast<const float4*>(p + s * slice);
+    a.x += v.x;
+    a.y += v.y;
+    a.z += v.z;
+    a.w += v.w;
+  }
+  return a;
+}
+__device__ __forceinline__ float2 sum_splits2(const float* p, int n, int64_t slice) {
+  float2 a = *reinterpret_cast<const float2*>(p);
+  int s = 1;
+  for (; s + 4 <= n; s += 4) {
+    float2 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const float2*>(p + (s + u) * slice);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      a.x += v[u].x;
+      a.y += v[u].y;
+    }
+  }
+  for (; s < n; ++s) {
+    const float2 v = *reinterpret_cast<const float2*>(p + s * slice);
+    a.x += v.x;
+    a.y += v.y;
+  }
+  return a;
 }
 
 // Byte offset of 16-byte chunk `chunk` (0..7) of row `row` inside a

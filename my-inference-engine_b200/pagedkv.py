@@ -25,6 +25,8 @@ PKV_DEVERR_TIMEOUT = 4
 
 HEAD_DIM = 128
 BLOCK_TOKENS = 16
+LINEAR_MAX_ROWS = 256  # PKV_LINEAR_MAX_ROWS
+W_ROWMAJOR, W_TILED = 0, 1  # PKV_W_ROWMAJOR, PKV_W_TILED
 
 _c_i32p = ctypes.POINTER(ctypes.c_int32)
 _vp = ctypes.c_void_p
@@ -54,6 +56,21 @@ _SIGNATURES = {
     "pkv_paged_decode_static_scratch": (
         [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
          ctypes.c_float, _vp, _i64, _i64, _vp, _vp], ctypes.c_int),
+    "pkv_linear_workspace_size": ([_i32, _i32, _i32], ctypes.c_size_t),
+    "pkv_linear_pack_weight": ([_vp, _i64, _i32, _i32, _vp, _vp], ctypes.c_int),
+    "pkv_linear": (
+        [_vp, _i64, _vp, _i64, _i32, _vp, _i32, _i32, _i32, _vp, _i64, _vp, ctypes.c_size_t, _vp,
+         _vp], ctypes.c_int),
+    "pkv_linear_add_rmsnorm": (
+        [_vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, ctypes.c_float,
+         _vp, _i64, _vp, ctypes.c_size_t, _vp, _vp], ctypes.c_int),
+    "pkv_linear_silu_mul": (
+        [_vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i64, _vp, ctypes.c_size_t, _vp, _vp],
+        ctypes.c_int),
+    "pkv_linear_rope_append": (
+        [_vp, _i64, _vp, _i64, _i32, _vp, _i32, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp,
+         _i64, _vp, _i64, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, ctypes.c_size_t, _vp,
+         _vp], ctypes.c_int),
     "pkv_dense_attention": (
         [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i32, _i32,
          _i32, _i32, _i32, _i32, _i32, ctypes.c_float, _vp, _i64, _i64, _i64, _vp,
@@ -131,6 +148,24 @@ def decode_workspace(batch: int, num_q_heads: int, num_kv_heads: int, max_kv_len
         size = max(need, 2 * (ws.numel() if ws is not None else 0))
         ws = torch.zeros(size, dtype=torch.uint8, device=torch.device("cuda", idx))
         _workspaces[idx] = ws
+    return ws
+
+
+_lin_workspaces: dict[int, torch.Tensor] = {}
+
+
+def linear_workspace(rows: int, n: int, k: int, device: torch.device) -> torch.Tensor:
+    """Grow-only fp32 split-k scratch of the skinny linear entries for `device`
+    (the same retire-but-keep-alive rule as decode_workspace)."""
+    need = max(int(lib().pkv_linear_workspace_size(rows, n, k)), 16)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _lin_workspaces.get(idx)
+    if ws is None or ws.numel() < need:
+        if ws is not None:
+            _retired_workspaces.append(ws)
+        size = max(need, 2 * (ws.numel() if ws is not None else 0), 1 << 20)
+        ws = torch.empty(size, dtype=torch.uint8, device=torch.device("cuda", idx))
+        _lin_workspaces[idx] = ws
     return ws
 
 
@@ -228,6 +263,103 @@ def silu_mul(gu: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
                             _stream(gu.device))
     _check(st, "pkv_silu_mul")
     return out
+
+
+class TiledWeight:
+    """A weight w[n, k] packed into the PKV_W_TILED layout ([n/128][k/64][128][64]),
+    so the skinny GEMM streams it as contiguous 16 KiB runs.  `shape` is the
+    logical [n, k]."""
+
+    def __init__(self, w: torch.Tensor):
+        n, k = w.shape
+        self.shape = torch.Size((n, k))
+        self.data = torch.empty(n * k, dtype=w.dtype, device=w.device)
+        st = lib().pkv_linear_pack_weight(_ptr(w), w.stride(0), n, k, _ptr(self.data),
+                                          _stream(w.device))
+        _check(st, "pkv_linear_pack_weight")
+
+
+def _w_args(w) -> tuple[int, int, int]:
+    """(pointer, ldw, layout) of a plain row-major weight or a TiledWeight."""
+    if isinstance(w, TiledWeight):
+        return w.data.data_ptr(), w.shape[1], W_TILED
+    return w.data_ptr(), w.stride(0), W_ROWMAJOR
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
+           out: torch.Tensor | None = None, err: torch.Tensor | None = None) -> torch.Tensor:
+    """pkv_linear: x [rows, k] . w[n, k]^T (+ bias) -> [rows, n] bf16, rows <= 256."""
+    rows, k = x.shape
+    n = w.shape[0]
+    if out is None:
+        out = torch.empty(rows, n, dtype=x.dtype, device=x.device)
+    ws = linear_workspace(rows, n, k, x.device)
+    wp, ldw, lay = _w_args(w)
+    st = lib().pkv_linear(_ptr(x), x.stride(0), wp, ldw, lay, _ptr(bias), rows, n, k,
+                          _ptr(out), out.stride(0), _ptr(ws), ws.numel(), _ptr(err),
+                          _stream(x.device))
+    _check(st, "pkv_linear")
+    return out
+
+
+def linear_add_rmsnorm(x: torch.Tensor, w: torch.Tensor, resid: torch.Tensor | None,
+                       weight: torch.Tensor, eps: float, resid_out: torch.Tensor | None = None,
+                       out: torch.Tensor | None = None,
+                       err: torch.Tensor | None = None) -> torch.Tensor:
+    """pkv_linear_add_rmsnorm: add_rmsnorm(x . w^T, resid, weight) in two launches."""
+    rows, k = x.shape
+    n = w.shape[0]
+    if out is None:
+        out = torch.empty(rows, n, dtype=x.dtype, device=x.device)
+    ws = linear_workspace(rows, n, k, x.device)
+    wp, ldw, lay = _w_args(w)
+    st = lib().pkv_linear_add_rmsnorm(
+        _ptr(x), x.stride(0), wp, ldw, lay, rows, n, k,
+        _ptr(resid), resid.stride(0) if resid is not None else 0,
+        _ptr(resid_out), resid_out.stride(0) if resid_out is not None else 0,
+        _ptr(weight), eps, _ptr(out), out.stride(0), _ptr(ws), ws.numel(), _ptr(err),
+        _stream(x.device))
+    _check(st, "pkv_linear_add_rmsnorm")
+    return out
+
+
+def linear_silu_mul(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor | None = None,
+                    err: torch.Tensor | None = None) -> torch.Tensor:
+    """pkv_linear_silu_mul: silu_mul(x . w_gate_up^T) -> [rows, inter]."""
+    rows, k = x.shape
+    inter = w_gate_up.shape[0] // 2
+    if out is None:
+        out = torch.empty(rows, inter, dtype=x.dtype, device=x.device)
+    ws = linear_workspace(rows, 2 * inter, k, x.device)
+    wp, ldw, lay = _w_args(w_gate_up)
+    st = lib().pkv_linear_silu_mul(_ptr(x), x.stride(0), wp, ldw, lay, rows, inter, k,
+                                   _ptr(out), out.stride(0), _ptr(ws),
+                                   ws.numel(), _ptr(err), _stream(x.device))
+    _check(st, "pkv_linear_silu_mul")
+    return out
+
+
+def linear_rope_append(x: torch.Tensor, w_qkv: torch.Tensor, bias: torch.Tensor | None,
+                       rope_cos: torch.Tensor, rope_sin: torch.Tensor, q_out: torch.Tensor,
+                       k_plane: torch.Tensor, v_plane: torch.Tensor, tables: torch.Tensor,
+                       rows: torch.Tensor | None, starts: torch.Tensor, num_kv_heads: int,
+                       err: torch.Tensor | None = None,
+                       q_lens: torch.Tensor | None = None) -> None:
+    """pkv_linear_rope_append: the merged q/k/v GEMM (+ bias) then append_rope.
+    x: [B*T, k] rows in (b, t) order; q_out: [B, Hq, T, 128] view."""
+    B, Hq, T, D = q_out.shape
+    n_rows, k = x.shape
+    n = w_qkv.shape[0]
+    ws = linear_workspace(n_rows, n, k, x.device)
+    qs = q_out.stride()
+    wp, ldw, lay = _w_args(w_qkv)
+    st = lib().pkv_linear_rope_append(
+        _ptr(x), x.stride(0), wp, ldw, lay, _ptr(bias), k, _ptr(rope_cos),
+        _ptr(rope_sin), rope_cos.shape[0], _ptr(q_out), qs[0], qs[1], qs[2], _ptr(k_plane),
+        _ptr(v_plane), k_plane.shape[0], _ptr(tables), tables.stride(0), _ptr(rows),
+        _ptr(starts), _ptr(q_lens), B, Hq, num_kv_heads, T, D, _ptr(ws), ws.numel(), _ptr(err),
+        _stream(x.device))
+    _check(st, "pkv_linear_rope_append")
 
 
 def default_scale(d: int = HEAD_DIM) -> float:

@@ -26,7 +26,7 @@ def small_model(cuda):
 def test_decode_graph_matches_eager(cuda, small_model):
     from kv_cache import KVCache
 
-    m = small_model
+    m = small_model.fuse_weights_()  # both arms on the engine's fused path
     g = torch.Generator().manual_seed(1)
     prompts = [torch.randint(0, 151936, (n,), generator=g).tolist() for n in (5, 40, 17)]
     caches, logits = [], []

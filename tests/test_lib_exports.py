@@ -72,3 +72,30 @@ def test_entry_points_reject_bad_arguments_without_a_gpu():
     st = L.pkv_append_rope(None, 0, 0, 0, 16, 0, 0, 0, 16, 0, 0, 0, None, None, 0, None, 0, 0, 0,
                            16, 16, 17, 16, 1, None, 16, None, 1, 12, 2, 1, 128, None, None)
     assert st == 1
+
+
+def test_linear_workspace_plan_and_validation_without_a_gpu():
+    import pagedkv
+
+    L = pagedkv.lib()
+    # fp32 partials: splits * rows * n * 4 bytes, at least one split
+    for rows, n, k in ((1, 2048, 1536), (16, 1536, 8960), (256, 17920, 1536)):
+        need = L.pkv_linear_workspace_size(rows, n, k)
+        assert need >= rows * n * 4 and need % (rows * n * 4) == 0, (rows, n, k, need)
+    # a long k splits further than a short one for the same output
+    assert L.pkv_linear_workspace_size(16, 1536, 8960) > L.pkv_linear_workspace_size(16, 1536, 128)
+    for bad in ((0, 2048, 1536), (257, 2048, 1536), (16, 2000, 1536), (16, 2048, 1000)):
+        assert L.pkv_linear_workspace_size(*bad) == 0
+    # argument checks come before any CUDA call
+    st = L.pkv_linear(16, 1536, 16, 1536, 0, None, 300, 2048, 1536, 16, 2048, None, 0, None, None)
+    assert st == 2  # PKV_ERR_UNSUPPORTED: more than 256 rows
+    st = L.pkv_linear(16, 1536, 16, 1536, 0, None, 16, 2048, 1000, 16, 2048, None, 0, None, None)
+    assert st == 2  # k not a multiple of 64
+    st = L.pkv_linear(8, 1536, 16, 1536, 0, None, 16, 2048, 1536, 16, 2048, None, 0, None, None)
+    assert st == 3  # PKV_ERR_ALIGN: x not 16-byte aligned
+    st = L.pkv_linear_silu_mul(16, 1536, 16, 1536, 0, 16, 100, 1536, 16, 100, None, 0, None, None)
+    assert st == 2  # inter not a multiple of 64
+    st = L.pkv_linear(16, 1536, 16, 1536, 7, None, 16, 2048, 1536, 16, 2048, None, 0, None, None)
+    assert st == 1  # unknown weight layout
+    st = L.pkv_linear_pack_weight(16, 1536, 2000, 1536, 16, None)
+    assert st == 2  # n not a multiple of 128
