@@ -236,19 +236,21 @@ int pkv_paged_decode_static_scratch(const void* q, int64_t q_sb, int64_t q_sh,
  * when a decode step (or a short prefill) feeds them a few rows: the weight
  * matrix is read from HBM once, split over the SMs along n and k.  x, w and
  * y are bf16, rows with element strides (multiples of 8), 16-byte aligned;
- * n % 128 == 0, k % 64 == 0.  Accumulation is fp32; split-k partial sums are
- * added in a fixed order, so results are deterministic.
+ * n % 128 == 0, k % 64 == 0.  Accumulation is fp32; the k-split partial sums
+ * are added on chip (thread-block cluster) in a fixed order and rounded to
+ * bf16 once, so results are deterministic.
  *
- * The workspace (device memory, pkv_linear_workspace_size bytes, 16-byte
- * aligned) holds fp32 partial sums; every entry below takes it.  The fused
- * variants apply, to the bf16-rounded GEMM output, exactly the arithmetic of
- * the separate entry they replace:
+ * pkv_linear needs no workspace (the arguments may be NULL / 0).  The fused
+ * variants keep the bf16 GEMM output [rows][n] in the workspace
+ * (pkv_linear_workspace_size bytes = rows * n * 2, 16-byte aligned) and then
+ * apply exactly the arithmetic of the separate entry they replace:
  *   pkv_linear_add_rmsnorm  GEMM, then pkv_add_rmsnorm (o_proj / down_proj
  *                           followed by the next residual add + RMSNorm)
  *   pkv_linear_silu_mul     merged gate/up GEMM (w rows [0, inter) gate,
  *                           [inter, 2 inter) up), then pkv_silu_mul
  *   pkv_linear_rope_append  merged q/k/v GEMM + bias, then pkv_append_rope
  *                           (rows = batch * seq_len_q, row b*seq_len_q + t)
+ * where n is the GEMM's width: dim, 2 * inter, (hq + 2 hkv) * head_dim.
  */
 #define PKV_LINEAR_MAX_ROWS 256
 

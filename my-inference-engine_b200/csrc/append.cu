@@ -12,9 +12,6 @@
 //
 // One warp per (row, step token, head-of-{q, k, v}); lane l owns dims
 // {2l, 2l+1} and their rotation partners {64+2l, 64+2l+1}.
-// q/k/v come either from bf16 tensors (any strides) or from the fp32 split-k
-// partial sums of the merged q/k/v GEMM (linear_tc.cu) plus the q/k/v bias,
-// rounded to bf16 once: the value F.linear(x, w_qkv, b_qkv) stores.
 #include "pkv_device.cuh"
 #include "pkv_kernels.h"
 
@@ -31,17 +28,6 @@ __device__ __forceinline__ __nv_bfloat16 rope1(__nv_bfloat16 x, __nv_bfloat16 c,
   const __nv_bfloat16 xc = rn(__fmul_rn(bf(x), bf(c)));
   const __nv_bfloat16 rs = rn(__fmul_rn(bf(r), bf(s)));
   return rn(__fadd_rn(bf(xc), bf(rs)));
-}
-
-// bf16(sum of the split-k partials + bias) for columns col, col+1 of one row
-__device__ __forceinline__ __nv_bfloat162 parts_pair(const AppendLaunch& a, int64_t row, int col) {
-  float2 acc = sum_splits2(a.part + row * a.part_ld + col, a.parts, a.part_slice);
-  const __nv_bfloat16* bias = static_cast<const __nv_bfloat16*>(a.qkv_bias);
-  if (bias) {
-    acc.x += bf(bias[col]);
-    acc.y += bf(bias[col + 1]);
-  }
-  return __floats2bfloat162_rn(acc.x, acc.y);
 }
 
 __global__ void __launch_bounds__(256) append_rope_kernel(const AppendLaunch a, int32_t num_blocks) {
@@ -67,14 +53,11 @@ __global__ void __launch_bounds__(256) append_rope_kernel(const AppendLaunch a, 
   const int nq = a.q_out ? a.num_q_heads : 0;
 
   // source row and destination row for this item
-  const __nv_bfloat16* src = nullptr;
+  const __nv_bfloat16* src;
   __nv_bfloat16* dst;
   bool do_rope = rope;
-  int col0;  // partial mode: first column of this head in the q/k/v GEMM output
   if (which < nq) {
-    col0 = which * kHeadDim;
-    if (!a.part)
-      src = static_cast<const __nv_bfloat16*>(a.q) + b * a.q_sb + which * a.q_sh + tt * a.q_st;
+    src = static_cast<const __nv_bfloat16*>(a.q) + b * a.q_sb + which * a.q_sh + tt * a.q_st;
     dst = static_cast<__nv_bfloat16*>(a.q_out) + b * a.qo_sb + which * a.qo_sh + tt * a.qo_st;
   } else {
     const bool is_k = which < nq + a.num_kv_heads;
@@ -93,29 +76,18 @@ __global__ void __launch_bounds__(256) append_rope_kernel(const AppendLaunch a, 
     }
     const int64_t slot = static_cast<int64_t>(blk) * kBlockTokens + (pos & 15);
     if (is_k) {
-      col0 = (a.num_q_heads + h) * kHeadDim;
-      if (!a.part)
-        src = static_cast<const __nv_bfloat16*>(a.k) + b * a.k_sb + h * a.k_sh + tt * a.k_st;
+      src = static_cast<const __nv_bfloat16*>(a.k) + b * a.k_sb + h * a.k_sh + tt * a.k_st;
       dst = static_cast<__nv_bfloat16*>(a.k_pool) + (slot * a.num_kv_heads + h) * kHeadDim;
     } else {
-      col0 = (a.num_q_heads + a.num_kv_heads + h) * kHeadDim;
-      if (!a.part)
-        src = static_cast<const __nv_bfloat16*>(a.v) + b * a.v_sb + h * a.v_sh + tt * a.v_st;
+      src = static_cast<const __nv_bfloat16*>(a.v) + b * a.v_sb + h * a.v_sh + tt * a.v_st;
       dst = static_cast<__nv_bfloat16*>(a.v_pool) + (slot * a.num_kv_heads + h) * kHeadDim;
       do_rope = false;
     }
   }
 
   const int d = 2 * lane;
-  __nv_bfloat162 lo, hi;
-  if (a.part) {
-    const int64_t prow = static_cast<int64_t>(b) * a.seq_len_q + tt;
-    lo = parts_pair(a, prow, col0 + d);
-    hi = parts_pair(a, prow, col0 + 64 + d);
-  } else {
-    lo = *reinterpret_cast<const __nv_bfloat162*>(src + d);
-    hi = *reinterpret_cast<const __nv_bfloat162*>(src + 64 + d);
-  }
+  const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(src + d);
+  const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(src + 64 + d);
   if (!do_rope) {
     *reinterpret_cast<__nv_bfloat162*>(dst + d) = lo;
     *reinterpret_cast<__nv_bfloat162*>(dst + 64 + d) = hi;

@@ -3,6 +3,7 @@
 // Nothing here allocates device memory.
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <cuda_bf16.h>
 #include <stdarg.h>
 #include <stdio.h>
 
@@ -183,20 +184,11 @@ int check_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, int32_t
   return PKV_OK;
 }
 
-// The GEMM half of every pkv_linear* entry.  direct: y (+ bias) in bf16 when
-// the plan has one split; otherwise fp32 partials into the workspace.
+// The GEMM half of every pkv_linear* entry: bf16 y (+ bias).
 int run_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, int32_t w_layout,
-               int32_t rows, int32_t n, int32_t k, bool allow_direct, void* y, int64_t ldy, const void* bias,
-               void* workspace, size_t workspace_bytes, int32_t* err, cudaStream_t stream,
-               pkv::LinearPlan* plan_out, bool* direct_out) {
+               int32_t rows, int32_t n, int32_t k, void* y, int64_t ldy, const void* bias,
+               int32_t* err, cudaStream_t stream) {
   const pkv::LinearPlan pl = pkv::plan_linear(rows, n, k);
-  const bool direct = allow_direct && pl.splits == 1;
-  if (!direct) {
-    if (!workspace || workspace_bytes < pl.part_bytes)
-      return fail(PKV_ERR_WORKSPACE, "linear needs %zu workspace bytes, got %zu", pl.part_bytes,
-                  workspace ? workspace_bytes : (size_t)0);
-    if (!aligned16(workspace)) return fail(PKV_ERR_ALIGN, "workspace not 16-byte aligned");
-  }
   CUtensorMap wmap, xmap;
   int st = w_layout == PKV_W_TILED ? encode_tiled(&wmap, w, n, k)
                                    : encode_rows(&wmap, w, n, k, ldw, 128);
@@ -205,17 +197,21 @@ int run_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, int32_t w
   pkv::LinearLaunch a{};
   a.M = rows;
   a.N = n;
-  a.direct = direct ? 1 : 0;
   a.y = y;
   a.ldy = ldy;
   a.bias = bias;
-  a.part = static_cast<float*>(workspace);
   a.w_tiled = w_layout == PKV_W_TILED ? 1 : 0;
   a.err = err;
-  st = launch_status(pkv::launch_linear(a, pl, wmap, xmap, stream), "linear_tc");
-  if (st) return st;
-  *plan_out = pl;
-  *direct_out = direct;
+  return launch_status(pkv::launch_linear(a, pl, wmap, xmap, stream), "linear_tc");
+}
+
+// The fused entries' intermediate y [rows][n] bf16 lives in the workspace.
+int check_linear_ws(void* workspace, size_t workspace_bytes, int32_t rows, int32_t n) {
+  const size_t need = static_cast<size_t>(rows) * n * 2;
+  if (!workspace || workspace_bytes < need)
+    return fail(PKV_ERR_WORKSPACE, "linear needs %zu workspace bytes, got %zu", need,
+                workspace ? workspace_bytes : (size_t)0);
+  if (!aligned16(workspace)) return fail(PKV_ERR_ALIGN, "workspace not 16-byte aligned");
   return PKV_OK;
 }
 
@@ -493,7 +489,7 @@ int pkv_paged_decode_static_scratch(const void* q, int64_t q_sb, int64_t q_sh, c
 size_t pkv_linear_workspace_size(int32_t rows, int32_t n, int32_t k) {
   if (rows <= 0 || rows > PKV_LINEAR_MAX_ROWS || n <= 0 || n % 128 != 0 || k <= 0 || k % 64 != 0)
     return 0;
-  return pkv::plan_linear(rows, n, k).part_bytes;
+  return static_cast<size_t>(rows) * n * 2;
 }
 
 int pkv_linear_pack_weight(const void* w, int64_t ldw, int32_t n, int32_t k, void* w_tiled,
@@ -513,22 +509,18 @@ int pkv_linear_pack_weight(const void* w, int64_t ldw, int32_t n, int32_t k, voi
 int pkv_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, int32_t w_layout,
                const void* bias, int32_t rows, int32_t n, int32_t k, void* y, int64_t ldy,
                void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
   int st = check_linear(x, ldx, w, ldw, w_layout, rows, n, k);
   if (st) return st;
   if (!y) return fail(PKV_ERR_INVALID, "null y");
   if (!aligned16(y) || !mult8(ldy) || ldy < n || (bias && !aligned16(bias)))
     return fail(PKV_ERR_ALIGN, "y / bias must be 16-byte aligned, ldy a multiple of 8 >= n");
   if (rows == 0) return ok();
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  pkv::LinearPlan pl;
-  bool direct;
-  if ((st = run_linear(x, ldx, w, ldw, w_layout, rows, n, k, true, y, ldy, bias, workspace,
-                       workspace_bytes, err_flag, s, &pl, &direct)))
+  if ((st = run_linear(x, ldx, w, ldw, w_layout, rows, n, k, y, ldy, bias, err_flag,
+                       static_cast<cudaStream_t>(stream))))
     return st;
-  if (direct) return ok();
-  return launch_status(pkv::launch_splitk_reduce(static_cast<const float*>(workspace), pl.splits,
-                                                 rows, n, bias, y, ldy, s),
-                       "splitk_reduce");
+  return ok();
 }
 
 int pkv_linear_add_rmsnorm(const void* x, int64_t ldx, const void* w, int64_t ldw,
@@ -546,20 +538,12 @@ int pkv_linear_add_rmsnorm(const void* x, int64_t ldx, const void* w, int64_t ld
       (resid_out && !mult8(ro_stride)))
     return fail(PKV_ERR_ALIGN, "add_rmsnorm rows must be 16-byte aligned");
   if (rows == 0) return ok();
+  if ((st = check_linear_ws(workspace, workspace_bytes, rows, n))) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  pkv::LinearPlan pl;
-  bool direct;
-  if ((st = run_linear(x, ldx, w, ldw, w_layout, rows, n, k, false, nullptr, 0, nullptr,
-                       workspace, workspace_bytes, err_flag, s, &pl, &direct)))
+  if ((st = run_linear(x, ldx, w, ldw, w_layout, rows, n, k, workspace, n, nullptr, err_flag, s)))
     return st;
-  pkv::NormLaunch p{};
-  p.a = nullptr; p.a_stride = n;
-  p.resid = resid; p.r_stride = r_stride; p.resid_out = resid_out; p.ro_stride = ro_stride;
-  p.weight = norm_weight; p.out = out; p.o_stride = o_stride;
-  p.rows = rows; p.dim = n; p.eps = eps;
-  p.part = static_cast<const float*>(workspace);
-  p.parts = pl.splits;
-  p.part_slice = static_cast<int64_t>(rows) * n;
+  pkv::NormLaunch p{workspace, n, resid, r_stride, resid_out, ro_stride, norm_weight, out,
+                    o_stride, rows, n, eps};
   return launch_status(pkv::launch_add_rmsnorm(p, s), "add_rmsnorm");
 }
 
@@ -575,15 +559,12 @@ int pkv_linear_silu_mul(const void* x, int64_t ldx, const void* w_gate_up, int64
   if (!out) return fail(PKV_ERR_INVALID, "null out");
   if (!aligned16(out) || !mult8(o_stride)) return fail(PKV_ERR_ALIGN, "silu_mul rows must be 16-byte aligned");
   if (rows == 0) return ok();
+  if ((st = check_linear_ws(workspace, workspace_bytes, rows, n))) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  pkv::LinearPlan pl;
-  bool direct;
-  if ((st = run_linear(x, ldx, w_gate_up, ldw, w_layout, rows, n, k, false, nullptr, 0, nullptr,
-                       workspace, workspace_bytes, err_flag, s, &pl, &direct)))
+  if ((st = run_linear(x, ldx, w_gate_up, ldw, w_layout, rows, n, k, workspace, n, nullptr,
+                       err_flag, s)))
     return st;
-  return launch_status(pkv::launch_silu_mul(nullptr, n, out, o_stride, rows, inter, s,
-                                            static_cast<const float*>(workspace), pl.splits,
-                                            static_cast<int64_t>(rows) * n),
+  return launch_status(pkv::launch_silu_mul(workspace, n, out, o_stride, rows, inter, s),
                        "silu_mul");
 }
 
@@ -591,8 +572,7 @@ int pkv_linear_rope_append(const void* x, int64_t ldx, const void* w_qkv, int64_
                            int32_t w_layout, const void* bias, int32_t k, const void* rope_cos,
                            const void* rope_sin, int64_t rope_rows, void* q_out, int64_t qo_sb,
                            int64_t qo_sh, int64_t qo_st, void* k_pool, void* v_pool,
-                           int64_t num_slots,
-                           const int32_t* block_tables, int64_t table_pitch,
+                           int64_t num_slots, const int32_t* block_tables, int64_t table_pitch,
                            const int32_t* seq_rows, const int32_t* starts, const int32_t* q_lens,
                            int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
                            int32_t seq_len_q, int32_t head_dim, void* workspace,
@@ -613,17 +593,21 @@ int pkv_linear_rope_append(const void* x, int64_t ldx, const void* w_qkv, int64_
   if (rope_rows <= 0) return fail(PKV_ERR_INVALID, "rope_rows must be positive");
   if ((reinterpret_cast<uintptr_t>(q_out) | reinterpret_cast<uintptr_t>(rope_cos) |
        reinterpret_cast<uintptr_t>(rope_sin)) & 3u ||
-      (bias && (reinterpret_cast<uintptr_t>(bias) & 3u)))
-    return fail(PKV_ERR_ALIGN, "append pointers must be 4-byte aligned");
+      (bias && !aligned16(bias)))
+    return fail(PKV_ERR_ALIGN, "append pointers must be 4-byte aligned, bias 16-byte aligned");
   if ((qo_sb | qo_sh | qo_st) & 1) return fail(PKV_ERR_ALIGN, "q_out strides must be even");
   if (rows == 0) return ok();
+  if ((st = check_linear_ws(workspace, workspace_bytes, rows, n))) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  pkv::LinearPlan pl;
-  bool direct;
-  if ((st = run_linear(x, ldx, w_qkv, ldw, w_layout, rows, n, k, false, nullptr, 0, nullptr,
-                       workspace, workspace_bytes, err_flag, s, &pl, &direct)))
+  if ((st = run_linear(x, ldx, w_qkv, ldw, w_layout, rows, n, k, workspace, n, bias, err_flag, s)))
     return st;
+  // the GEMM output [batch][seq_len_q][q heads | k heads | v heads][128]
+  const int64_t tok = n, head = head_dim, row = static_cast<int64_t>(seq_len_q) * n;
+  const __nv_bfloat16* qkv = static_cast<const __nv_bfloat16*>(workspace);
   pkv::AppendLaunch a{};
+  a.q = qkv; a.q_sb = row; a.q_sh = head; a.q_st = tok;
+  a.k = qkv + num_q_heads * head; a.k_sb = row; a.k_sh = head; a.k_st = tok;
+  a.v = qkv + (num_q_heads + num_kv_heads) * head; a.v_sb = row; a.v_sh = head; a.v_st = tok;
   a.rope_cos = rope_cos; a.rope_sin = rope_sin; a.rope_rows = rope_rows;
   a.q_out = q_out; a.qo_sb = qo_sb; a.qo_sh = qo_sh; a.qo_st = qo_st;
   a.k_pool = k_pool; a.v_pool = v_pool; a.num_slots = num_slots;
@@ -631,11 +615,6 @@ int pkv_linear_rope_append(const void* x, int64_t ldx, const void* w_qkv, int64_
   a.q_lens = q_lens;
   a.batch = batch; a.num_q_heads = num_q_heads; a.num_kv_heads = num_kv_heads;
   a.seq_len_q = seq_len_q; a.err = err_flag;
-  a.part = static_cast<const float*>(workspace);
-  a.parts = pl.splits;
-  a.part_slice = static_cast<int64_t>(rows) * n;
-  a.part_ld = n;
-  a.qkv_bias = bias;
   return launch_status(pkv::launch_append(a, s), "append_rope");
 }
 

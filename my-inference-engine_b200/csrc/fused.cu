@@ -9,9 +9,6 @@
 //   model.py:120      down_proj(silu(gate_proj(x)) * up_proj(x))
 // One CTA per row for the norm (warp + shared-memory reduction of the sum
 // of squares); the SiLU product is a flat 8-wide vectorised loop.
-// Both read their input either as bf16 rows or as the fp32 split-k partial
-// sums of the skinny GEMM (linear_tc.cu): then input = bf16(sum of the
-// partials in split order), the value that GEMM would have stored.
 #include "pkv_device.cuh"
 #include "pkv_kernels.h"
 
@@ -23,41 +20,10 @@ __device__ __forceinline__ __nv_bfloat16 rn(float x) { return __float2bfloat16_r
 
 constexpr int kNormThreads = 256;
 
-// Split-k partial sums: element (row, col) of split s at
-// p[s * slice + row * ld + col]; summed in split order, rounded to bf16.
-struct Parts {
-  const float* p;
-  int32_t n;
-  int64_t slice;
-};
-__device__ __forceinline__ void sum8(const Parts& pa, int64_t off, float (&acc)[8]) {
-  const float4 a0 = sum_splits4(pa.p + off, pa.n, pa.slice);
-  const float4 a1 = sum_splits4(pa.p + off + 4, pa.n, pa.slice);
-  acc[0] = a0.x; acc[1] = a0.y; acc[2] = a0.z; acc[3] = a0.w;
-  acc[4] = a1.x; acc[5] = a1.y; acc[6] = a1.z; acc[7] = a1.w;
-}
-// 8 bf16 input values at (row offset off): from bf16 rows or partial sums
-template <bool kParts>
-__device__ __forceinline__ uint4 load8(const __nv_bfloat16* a, const Parts& pa, int64_t off) {
-  if constexpr (kParts) {
-    float acc[8];
-    sum8(pa, off, acc);
-    uint4 v;
-    v.x = pack_bf16(acc[0], acc[1]);
-    v.y = pack_bf16(acc[2], acc[3]);
-    v.z = pack_bf16(acc[4], acc[5]);
-    v.w = pack_bf16(acc[6], acc[7]);
-    return v;
-  } else {
-    return *reinterpret_cast<const uint4*>(a + off);
-  }
-}
-
 // One CTA per row: thread i owns elements [8i, 8i+8) (+ 2048 for dim > 2048).
 // h = a (+ resid) in bf16; resid_out = h; out = weight * bf16(h * rsqrt(mean(h^2) + eps))
-template <bool kParts>
 __global__ void __launch_bounds__(kNormThreads)
-    add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ a, const Parts pa, int64_t a_stride,
+    add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ a, int64_t a_stride,
                        const __nv_bfloat16* resid, int64_t r_stride, __nv_bfloat16* resid_out,
                        int64_t ro_stride, const __nv_bfloat16* __restrict__ weight,
                        __nv_bfloat16* __restrict__ out, int64_t o_stride, int rows, int dim,
@@ -73,7 +39,7 @@ __global__ void __launch_bounds__(kNormThreads)
   for (int c = 0; c < 2; ++c) {
     const int col = (c * kNormThreads + tid) * 8;
     if (col < dim) {
-      const uint4 av = load8<kParts>(a, pa, row * a_stride + col);
+      const uint4 av = *reinterpret_cast<const uint4*>(a + row * a_stride + col);
       const __nv_bfloat16* ap = reinterpret_cast<const __nv_bfloat16*>(&av);
       uint4 hv;
       __nv_bfloat16* hp = reinterpret_cast<__nv_bfloat16*>(&hv);
@@ -116,9 +82,8 @@ __global__ void __launch_bounds__(kNormThreads)
   }
 }
 
-template <bool kParts>
 __global__ void __launch_bounds__(256)
-    silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, const Parts pa, int64_t gu_stride,
+    silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int64_t gu_stride,
                     __nv_bfloat16* __restrict__ out, int64_t o_stride, int rows, int inter) {
   pdl_trigger();
   pdl_wait();
@@ -127,8 +92,8 @@ __global__ void __launch_bounds__(256)
   if (i >= static_cast<int64_t>(rows) * per_row) return;
   const int row = static_cast<int>(i / per_row);
   const int col = static_cast<int>(i % per_row) * 8;
-  const uint4 gv = load8<kParts>(gu, pa, row * gu_stride + col);
-  const uint4 uv = load8<kParts>(gu, pa, row * gu_stride + inter + col);
+  const uint4 gv = *reinterpret_cast<const uint4*>(gu + row * gu_stride + col);
+  const uint4 uv = *reinterpret_cast<const uint4*>(gu + row * gu_stride + inter + col);
   const __nv_bfloat16* gp = reinterpret_cast<const __nv_bfloat16*>(&gv);
   const __nv_bfloat16* up = reinterpret_cast<const __nv_bfloat16*>(&uv);
   uint4 ov;
@@ -145,10 +110,8 @@ __global__ void __launch_bounds__(256)
 }  // namespace
 
 cudaError_t launch_add_rmsnorm(const NormLaunch& p, cudaStream_t stream) {
-  const Parts pa{p.part, p.parts, p.part_slice};
-  auto kern = p.part ? add_rmsnorm_kernel<true> : add_rmsnorm_kernel<false>;
-  return launch_k(kern, dim3(p.rows), dim3(kNormThreads), 0, stream,
-                  static_cast<const __nv_bfloat16*>(p.a), pa, p.a_stride,
+  return launch_k(add_rmsnorm_kernel, dim3(p.rows), dim3(kNormThreads), 0, stream,
+                  static_cast<const __nv_bfloat16*>(p.a), p.a_stride,
                   static_cast<const __nv_bfloat16*>(p.resid), p.r_stride,
                   static_cast<__nv_bfloat16*>(p.resid_out), p.ro_stride,
                   static_cast<const __nv_bfloat16*>(p.weight), static_cast<__nv_bfloat16*>(p.out),
@@ -156,14 +119,11 @@ cudaError_t launch_add_rmsnorm(const NormLaunch& p, cudaStream_t stream) {
 }
 
 cudaError_t launch_silu_mul(const void* gu, int64_t gu_stride, void* out, int64_t o_stride,
-                            int32_t rows, int32_t inter, cudaStream_t stream, const float* part,
-                            int32_t parts, int64_t part_slice) {
+                            int32_t rows, int32_t inter, cudaStream_t stream) {
   const int64_t n = static_cast<int64_t>(rows) * (inter / 8);
   if (n == 0) return cudaSuccess;
-  const Parts pa{part, parts, part_slice};
-  auto kern = part ? silu_mul_kernel<true> : silu_mul_kernel<false>;
-  return launch_k(kern, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, stream,
-                  static_cast<const __nv_bfloat16*>(gu), pa, gu_stride,
+  return launch_k(silu_mul_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0,
+                  stream, static_cast<const __nv_bfloat16*>(gu), gu_stride,
                   static_cast<__nv_bfloat16*>(out), o_stride, static_cast<int>(rows),
                   static_cast<int>(inter));
 }

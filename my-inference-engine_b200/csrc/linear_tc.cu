@@ -24,11 +24,17 @@
 //               D[128, Mpad] += W[128, 16] . x[Mpad, 16]^T, 4 per chunk
 //     warps 2-5 epilogue: warp w reads TMEM lanes 32*(w%4).., i.e. one W row
 //               (one output feature n) per thread, all batch rows as columns
-// Output: either y itself in bf16 (+ bias) when there is one split, or fp32
-// partial sums part[s][m][n] that the consumer kernel adds up in split order
-// (deterministic) before its own epilogue: plain bias + bf16 store here, or
-// the residual add + RMSNorm, SwiGLU and RoPE + K/V append kernels.
+// Epilogue: each CTA moves its fp32 accumulators from TMEM to its own shared
+// memory (over the drained ring).  Split-k: the `splits` CTAs of one W tile
+// form a thread-block cluster (1 x splits) and CTA r adds up batch rows
+// [r*M/splits, ...) of all the cluster's partials through distributed shared
+// memory, in split order (deterministic).  Bias, one bf16 rounding and
+// 8-byte row-contiguous stores of y; nothing else goes to global memory.
 // Every wait is bounded.
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "pkv_device.cuh"
 #include "pkv_kernels.h"
 #include "tc_device.cuh"
@@ -42,19 +48,44 @@ constexpr int kWBytes = kTileN * 128;  // 16 KiB W box per stage
 constexpr int kLinThreads = 192;
 constexpr int kMaxStages = 8;
 constexpr int kSmemCap = 227 * 1024;
+constexpr int kMaxSplits = 16;  // non-portable cluster size limit
 
 __device__ __forceinline__ float bf(__nv_bfloat16 x) { return __bfloat162float(x); }
 
 struct LinParams {
-  void* out;  // bf16 [M][ldo] (direct) or fp32 [splits][M][N] partials
-  int64_t ldo;
-  const __nv_bfloat16* bias;  // direct mode only; nullable
+  __nv_bfloat16* y;  // [M][ldy]
+  int64_t ldy;
+  const __nv_bfloat16* bias;  // nullable
   int32_t M, N, chunks, splits, stages, mpad;
   uint32_t tmem_cols, idesc;
-  int32_t direct;
   int32_t w_tiled;  // W packed as [N/128][K/64][128][64]: one contiguous 16 KiB box per chunk
   int32_t* err;
 };
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cta address -> the same offset in cluster CTA `rank`
+__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_cluster4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
 
 __global__ void __launch_bounds__(kLinThreads, 1)
     linear_tc_kernel(const LinParams p, const __grid_constant__ CUtensorMap wmap,
@@ -143,31 +174,18 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
-    const int n = tile * kTileN + quarter * 32 + lane;
+    const int nl = quarter * 32 + lane;  // W row within the tile == TMEM lane
     const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     if (__all_sync(0xffffffffu, mbar_wait(done, 0, err))) {
       tc_fence_after();
-      if (p.direct) {
-        const float b = p.bias ? bf(p.bias[n]) : 0.f;
-        __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.out) + n;
-        for (int c = 0; c < p.mpad; c += 16) {
-          float v[16];
-          tmem_ld16(taddr + c, v);
-          tmem_wait_ld();
+      // this CTA's accumulators as [mpad][128] fp32 over the drained ring
+      float* red = reinterpret_cast<float*>(smem);
+      for (int c = 0; c < p.mpad; c += 16) {
+        float v[16];
+        tmem_ld16(taddr + c, v);
+        tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            if (c + e < p.M) y[(c + e) * p.ldo] = __float2bfloat16_rn(v[e] + b);
-        }
-      } else {
-        float* y = static_cast<float*>(p.out) + static_cast<int64_t>(split) * p.M * p.N + n;
-        for (int c = 0; c < p.mpad; c += 16) {
-          float v[16];
-          tmem_ld16(taddr + c, v);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 16; ++e)
-            if (c + e < p.M) y[static_cast<int64_t>(c + e) * p.N] = v[e];
-        }
+        for (int e = 0; e < 16; ++e) red[(c + e) * kTileN + nl] = v[e];
       }
     }
   }
@@ -177,33 +195,51 @@ __global__ void __launch_bounds__(kLinThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, p.tmem_cols);
   }
-}
-
-// y[m][n] = bf16(sum_s part[s][m][n] + bias[n]), splits summed in order.
-__global__ void __launch_bounds__(256)
-    splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N,
-                         const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ y,
-                         int64_t ldy) {
-  pdl_trigger();
-  pdl_wait();
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int per_row = N / 4;
-  if (i >= static_cast<int64_t>(M) * per_row) return;
-  const int m = static_cast<int>(i / per_row);
-  const int n = static_cast<int>(i % per_row) * 4;
-  const int64_t slice = static_cast<int64_t>(M) * N;
-  const float4 acc = sum_splits4(part + static_cast<int64_t>(m) * N + n, splits, slice);
-  float4 v = acc;
-  if (bias) {
-    v.x += bf(bias[n + 0]);
-    v.y += bf(bias[n + 1]);
-    v.z += bf(bias[n + 2]);
-    v.w += bf(bias[n + 3]);
+  // Store: thread = 4 consecutive features of one batch row.  With a split,
+  // CTA r of the cluster sums rows [r*per, (r+1)*per) over every split's
+  // shared memory (all loads in flight, adds in split order).
+  const bool clustered = p.splits > 1;
+  if (clustered) cluster_sync_all();  // every split's partial is in shared memory
+  const int per = (p.M + p.splits - 1) / p.splits;
+  const int m0 = clustered ? static_cast<int>(cluster_rank()) * per : 0;
+  const int m1 = min(p.M, m0 + per);
+  const uint32_t base = smem_u32(smem);
+  for (int idx = tid; idx < (m1 - m0) * (kTileN / 4); idx += kLinThreads) {
+    const int m = m0 + idx / (kTileN / 4);
+    const int nl = (idx % (kTileN / 4)) * 4;
+    const uint32_t off = base + static_cast<uint32_t>((m * kTileN + nl) * 4);
+    float4 acc;
+    if (clustered) {
+      float4 v[kMaxSplits];
+#pragma unroll
+      for (int sp = 0; sp < kMaxSplits; ++sp)
+        if (sp < p.splits) v[sp] = ld_cluster4(map_rank(off, sp));
+      acc = v[0];
+#pragma unroll
+      for (int sp = 1; sp < kMaxSplits; ++sp) {
+        if (sp < p.splits) {
+          acc.x += v[sp].x;
+          acc.y += v[sp].y;
+          acc.z += v[sp].z;
+          acc.w += v[sp].w;
+        }
+      }
+    } else {
+      acc = *reinterpret_cast<const float4*>(smem + (m * kTileN + nl) * 4);
+    }
+    const int n = tile * kTileN + nl;
+    if (p.bias) {
+      acc.x += bf(p.bias[n + 0]);
+      acc.y += bf(p.bias[n + 1]);
+      acc.z += bf(p.bias[n + 2]);
+      acc.w += bf(p.bias[n + 3]);
+    }
+    uint2 o;
+    o.x = pack_bf16(acc.x, acc.y);
+    o.y = pack_bf16(acc.z, acc.w);
+    *reinterpret_cast<uint2*>(p.y + m * p.ldy + n) = o;
   }
-  uint2 o;
-  o.x = pack_bf16(v.x, v.y);
-  o.y = pack_bf16(v.z, v.w);
-  *reinterpret_cast<uint2*>(y + static_cast<int64_t>(m) * ldy + n) = o;
+  if (clustered) cluster_sync_all();  // no CTA exits while another reads its shared memory
 }
 
 // w[n][k] (row stride ldw) -> [n/128][k/64][128][64]; one thread per 16 bytes
@@ -236,6 +272,59 @@ int sm_count() {
   return count;
 }
 
+// Per-device one-time function attributes: the full shared-memory opt-in and
+// clusters of up to 16 CTAs.
+cudaError_t configure_kernel() {
+  static int configured_device = -1;
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  if (configured_device == dev) return cudaSuccess;
+  e = cudaFuncSetAttribute(linear_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(linear_tc_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e != cudaSuccess) return e;
+  configured_device = dev;
+  return cudaSuccess;
+}
+
+// Clusters of `splits` CTAs (each with smem_bytes of shared memory) that can
+// be resident at once, from the occupancy API; cached per (device, shape).
+int max_clusters(int splits, int smem_bytes, int tiles) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const auto key = std::make_tuple(dev, splits, smem_bytes);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  if (configure_kernel() != cudaSuccess) return 0;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(tiles, splits);
+  cfg.blockDim = dim3(kLinThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem_bytes);
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 1;
+  attr.val.clusterDim.y = static_cast<unsigned>(splits);
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, linear_tc_kernel, &cfg) != cudaSuccess) {
+    cudaGetLastError();  // a failed query leaves no error behind for the next call
+    n = 0;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache[key] = n;
+  return n;
+}
+
 }  // namespace
 
 LinearPlan plan_linear(int32_t M, int32_t N, int32_t K) {
@@ -251,36 +340,35 @@ LinearPlan plan_linear(int32_t M, int32_t N, int32_t K) {
   pl.stages = budget / stage_bytes;
   if (pl.stages > kMaxStages) pl.stages = kMaxStages;
   pl.smem_bytes = pl.stages * stage_bytes + (2 * pl.stages + 1) * 8 + 16 + 1024;
-  // as many splits as still fit one wave of CTAs (a second wave would run alone)
+  // Split k over a cluster of up to 16 CTAs per W tile: the most splits for
+  // which every tile's cluster is resident in one wave (a second wave would
+  // run alone) and each split keeps >= 2 chunks.  The split partials are
+  // reduced in shared memory, which must hold [mpad][128] fp32.
   const int wave = sm_count() * per_sm;
-  int splits = wave / (pl.tiles > 0 ? pl.tiles : 1);
-  const int max_splits = pl.chunks / 2 > 0 ? pl.chunks / 2 : 1;
-  if (splits > max_splits) splits = max_splits;
-  if (splits < 1) splits = 1;
-  pl.splits = splits;
+  int smax = wave / (pl.tiles > 0 ? pl.tiles : 1);
+  if (smax > kMaxSplits) smax = kMaxSplits;
+  if (smax > pl.chunks / 2) smax = pl.chunks / 2;
+  if (pl.stages * stage_bytes < pl.mpad * kTileN * 4) smax = 1;
+  pl.splits = 1;
+  for (int cand = smax; cand >= 2; --cand) {
+    if (max_clusters(cand, pl.smem_bytes, pl.tiles) >= pl.tiles) {
+      pl.splits = cand;
+      break;
+    }
+  }
   uint32_t cols = 32;
   while (cols < static_cast<uint32_t>(pl.mpad)) cols <<= 1;
   pl.tmem_cols = cols;
-  pl.part_bytes = static_cast<size_t>(splits) * M * N * sizeof(float);
   return pl;
 }
 
 cudaError_t launch_linear(const LinearLaunch& a, const LinearPlan& pl, const CUtensorMap& wmap,
                           const CUtensorMap& xmap, cudaStream_t stream) {
-  static int configured_device = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(linear_tc_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap);
-    if (e != cudaSuccess) return e;
-    configured_device = dev;
-  }
+  cudaError_t e = configure_kernel();
+  if (e != cudaSuccess) return e;
   LinParams p{};
-  p.direct = a.direct;
-  p.w_tiled = a.w_tiled;
-  p.out = a.direct ? a.y : a.part;
-  p.ldo = a.ldy;
+  p.y = static_cast<__nv_bfloat16*>(a.y);
+  p.ldy = a.ldy;
   p.bias = static_cast<const __nv_bfloat16*>(a.bias);
   p.M = a.M;
   p.N = a.N;
@@ -289,13 +377,34 @@ cudaError_t launch_linear(const LinearLaunch& a, const LinearPlan& pl, const CUt
   p.stages = pl.stages;
   p.mpad = pl.mpad;
   p.tmem_cols = pl.tmem_cols;
+  p.w_tiled = a.w_tiled;
   // kind::f16 instruction descriptor: fp32 D, bf16 A and B, both K-major,
   // N = mpad (>> 3 at bit 17), M = 128 (>> 4 at bit 24)
   p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((static_cast<uint32_t>(pl.mpad) >> 3) << 17) |
             ((static_cast<uint32_t>(kTileN) >> 4) << 24);
   p.err = a.err;
-  return launch_k(linear_tc_kernel, dim3(pl.tiles, pl.splits), dim3(kLinThreads),
-                  static_cast<size_t>(pl.smem_bytes), stream, p, wmap, xmap);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(pl.tiles, pl.splits);
+  cfg.blockDim = dim3(kLinThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(pl.smem_bytes);
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2] = {};
+  unsigned n = 0;
+  if (pdl_enabled()) {
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (pl.splits > 1) {
+    attrs[n].id = cudaLaunchAttributeClusterDimension;
+    attrs[n].val.clusterDim.x = 1;
+    attrs[n].val.clusterDim.y = static_cast<unsigned>(pl.splits);
+    attrs[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, linear_tc_kernel, p, wmap, xmap);
 }
 
 cudaError_t launch_pack_weight(const void* w, int64_t ldw, int32_t n, int32_t k, void* out,
@@ -304,15 +413,6 @@ cudaError_t launch_pack_weight(const void* w, int64_t ldw, int32_t n, int32_t k,
   return launch_k(pack_weight_kernel, dim3(static_cast<unsigned>((total16 + 255) / 256)),
                   dim3(256), 0, stream, static_cast<const __nv_bfloat16*>(w), ldw, k / kChunkK,
                   total16, static_cast<__nv_bfloat16*>(out));
-}
-
-cudaError_t launch_splitk_reduce(const float* part, int32_t splits, int32_t M, int32_t N,
-                                 const void* bias, void* y, int64_t ldy, cudaStream_t stream) {
-  const int64_t n = static_cast<int64_t>(M) * (N / 4);
-  if (n == 0) return cudaSuccess;
-  return launch_k(splitk_reduce_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256),
-                  0, stream, part, splits, M, N, static_cast<const __nv_bfloat16*>(bias),
-                  static_cast<__nv_bfloat16*>(y), ldy);
 }
 
 }  // namespace pkv

@@ -192,54 +192,6 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Sum of the fp32 split-k partials p[s * slice] (4 or 2 consecutive floats)
-// over s = 0..n-1, added strictly in split order (so every consumer rounds
-// the same value); loads are issued four splits ahead of the adds.
-__device__ __forceinline__ float4 sum_splits4(const float* p, int n, int64_t slice) {
-  float4 a = *reinterpret_cast<const float4*>(p);
-  int s = 1;
-  for (; s + 4 <= n; s += 4) {
-    float4 v[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const float4*>(p + (s + u) * slice);
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      a.x += v[u].x;
-      a.y += v[u].y;
-      a.z += v[u].z;
-      a.w += v[u].w;
-    }
-  }
-  for (; s < n; ++s) {
-    const float4 v = *reinterpret_cast<const float4*>(p + s * slice);
-    a.x += v.x;
-    a.y += v.y;
-    a.z += v.z;
-    a.w += v.w;
-  }
-  return a;
-}
-__device__ __forceinline__ float2 sum_splits2(const float* p, int n, int64_t slice) {
-  float2 a = *reinterpret_cast<const float2*>(p);
-  int s = 1;
-  for (; s + 4 <= n; s += 4) {
-    float2 v[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const float2*>(p + (s + u) * slice);
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      a.x += v[u].x;
-      a.y += v[u].y;
-    }
-  }
-  for (; s < n; ++s) {
-    const float2 v = *reinterpret_cast<const float2*>(p + s * slice);
-    a.x += v.x;
-    a.y += v.y;
-  }
-  return a;
-}
-
 // Byte offset of 16-byte chunk `chunk` (0..7) of row `row` inside a
 // 128B-swizzled TMA box whose rows are 128 bytes (the hardware XORs the chunk
 // index with the row index modulo 8; the box starts 1024-byte aligned).

@@ -93,14 +93,6 @@ struct AppendLaunch {
   const int32_t* q_lens;  // nullable
   int32_t batch, num_q_heads, num_kv_heads, seq_len_q;
   int32_t* err;
-  // optional: q/k/v read from the fp32 split-k partial sums of the merged
-  // q/k/v GEMM (row b * seq_len_q + t, columns [q heads | k heads | v heads]
-  // x 128) plus qkv_bias, rounded to bf16; q, k, v are then unused
-  const float* part;
-  int32_t parts;
-  int64_t part_slice;
-  int64_t part_ld;
-  const void* qkv_bias;
 };
 cudaError_t launch_append(const AppendLaunch& a, cudaStream_t stream);
 
@@ -116,35 +108,28 @@ struct NormLaunch {
   int64_t o_stride;
   int32_t rows, dim;
   float eps;
-  // optional: read `a` as fp32 split-k partial sums (a_stride = their row
-  // stride) instead of bf16 rows
-  const float* part;
-  int32_t parts;
-  int64_t part_slice;
 };
 cudaError_t launch_add_rmsnorm(const NormLaunch& p, cudaStream_t stream);
 
-// Skinny tcgen05 linear (linear_tc.cu): y[M, N] = x[M, K] . W[N, K]^T, M <= 256.
+// Skinny tcgen05 linear (linear_tc.cu): y[M, N] = x[M, K] . W[N, K]^T (+ bias), M <= 256.
 struct LinearPlan {
-  int32_t mpad;      // M rounded up to a multiple of 16 (the MMA's N)
-  int32_t tiles;     // N / 128
-  int32_t chunks;    // K / 64
-  int32_t splits;    // split-K factor (grid.y)
-  int32_t stages;    // TMA ring depth
+  int32_t mpad;    // M rounded up to a multiple of 16 (the MMA's N)
+  int32_t tiles;   // N / 128
+  int32_t chunks;  // K / 64
+  int32_t splits;  // split-k factor = cluster size (grid.y)
+  int32_t stages;  // TMA ring depth
   int32_t smem_bytes;
   uint32_t tmem_cols;
-  size_t part_bytes;  // fp32 partials: splits * M * N * 4
 };
 struct LinearLaunch {
   int32_t M, N;
-  int32_t direct;    // 1: bf16 y (+ bias) written by the GEMM itself (splits == 1)
-  void* y;           // direct only
+  void* y;  // bf16 [M][ldy]
   int64_t ldy;
-  const void* bias;  // direct only; nullable
-  float* part;       // partial mode: [splits][M][N] fp32
+  const void* bias;  // nullable
   int32_t w_tiled;   // wmap is the 3-D map of a PKV_W_TILED weight
   int32_t* err;
 };
+// Needs a current CUDA device (the split count comes from the occupancy API).
 LinearPlan plan_linear(int32_t M, int32_t N, int32_t K);
 // wmap: 2-D over W [N][K] bf16, box {64, 128} (or 3-D over a PKV_W_TILED W,
 // box {64, 128, 1}); xmap: 2-D over x [M][K], box {64, mpad}
@@ -152,12 +137,7 @@ cudaError_t launch_linear(const LinearLaunch& a, const LinearPlan& pl, const CUt
                           const CUtensorMap& xmap, cudaStream_t stream);
 cudaError_t launch_pack_weight(const void* w, int64_t ldw, int32_t n, int32_t k, void* out,
                                cudaStream_t stream);
-cudaError_t launch_splitk_reduce(const float* part, int32_t splits, int32_t M, int32_t N,
-                                 const void* bias, void* y, int64_t ldy, cudaStream_t stream);
-// part != nullptr: gu is read as fp32 split-k partial sums (gu_stride = their row stride)
 cudaError_t launch_silu_mul(const void* gu, int64_t gu_stride, void* out, int64_t o_stride,
-                            int32_t rows, int32_t inter, cudaStream_t stream,
-                            const float* part = nullptr, int32_t parts = 0,
-                            int64_t part_slice = 0);
+                            int32_t rows, int32_t inter, cudaStream_t stream);
 
 }  // namespace pkv

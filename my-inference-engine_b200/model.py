@@ -222,19 +222,7 @@ class Qwen2ForCausalLM(torch.nn.Module):
         N = B * T
         xs = x.view(N, HIDDEN_SIZE)
         h = pagedkv.add_rmsnorm(xs, None, self.layers[0].input_layernorm.weight, RMS_NORM_EPS)
-        if self.skinny_linears and N <= pagedkv.LINEAR_MAX_ROWS:
-            m = self._skinny_layers(h, xs, B, T, cos, sin, is_causal, kv_lens, cache, step)
-        else:
-            for layer_idx, layer in enumerate(self.layers):
-                a = layer.self_attn(h.view(B, T, HIDDEN_SIZE), cos, sin, None, is_causal, kv_lens,
-                                    cache, layer_idx, step, step)
-                h = pagedkv.add_rmsnorm(a.view(N, HIDDEN_SIZE), xs,
-                                        layer.post_attention_layernorm.weight, RMS_NORM_EPS,
-                                        resid_out=xs)
-                m = layer.mlp(h)
-                if layer_idx + 1 < len(self.layers):
-                    h = pagedkv.add_rmsnorm(m, xs, self.layers[layer_idx + 1].input_layernorm.weight,
-                                            RMS_NORM_EPS, resid_out=xs)
+        m = self._fused_layers(h, xs, B, T, cos, sin, is_causal, kv_lens, cache, step)
         # last position only (model.py:204-206): x + mlp, then the final norm
         if step.q_lens is not None:  # right-padded rows: their last real token
             rows = torch.arange(B, device=x.device)
@@ -247,48 +235,81 @@ class Qwen2ForCausalLM(torch.nn.Module):
         h = pagedkv.add_rmsnorm(m_last, x_last, self.norm.weight, RMS_NORM_EPS)
         return (h @ self.embed_tokens.weight.T)[:, None]
 
-    def _skinny_layers(self, h, xs, B, T, cos, sin, is_causal, kv_lens, cache, step):
-        """The 28 layers for a step of at most 256 rows: every projection is a
-        skinny tensor-core GEMM (weights streamed once) whose split-k partial
-        sums feed the next fused op directly -- q/k/v + bias -> RoPE + K/V
-        append, o_proj -> residual add + RMSNorm, gate/up -> SwiGLU, down_proj
-        -> residual add + the next layer's RMSNorm.  Same op order and bf16
-        rounding points as the cuBLAS branch of forward_step.  Returns the last
-        layer's MLP output (before its residual add)."""
+    def _fused_layers(self, h, xs, B, T, cos, sin, is_causal, kv_lens, cache, step):
+        """The 28 layers on the merged weights, same op order and bf16 rounding
+        points as QwenBlock.forward (model.py:131-138): q/k/v GEMM + bias ->
+        RoPE + K/V append -> paged attention -> o_proj -> residual add + RMSNorm
+        -> gate/up GEMM -> SwiGLU -> down_proj -> residual add + the next
+        layer's RMSNorm.  h: the first layer's normed input [N, 1536]; xs: the
+        residual stream, updated in place.  Each projection runs as a skinny
+        tensor-core GEMM fused with the op after it when the step has at most
+        skinny_rows[op] rows (where it beats cuBLAS), else as cuBLAS + the
+        separate fused kernel.  Returns the last layer's MLP output (before its
+        residual add)."""
         import pagedkv
         from kernels.fa2 import flash_attention
 
         N = B * T
+        use = {op: self.skinny_linears and N <= lim for op, lim in self.skinny_rows.items()}
+        err = cache.err_flag
         m = None
-        for layer_idx, layer in enumerate(self.layers):
+        last = len(self.layers) - 1
+        for li, layer in enumerate(self.layers):
             at, mlp = layer.self_attn, layer.mlp
             q_rot = torch.empty(B, T, NUM_HEADS, HEAD_DIM, device=xs.device, dtype=xs.dtype)
-            pagedkv.linear_rope_append(
-                h, at.qkv_weight, at.qkv_bias, cos, sin, q_rot.transpose(1, 2),
-                cache.buf[layer_idx, 0], cache.buf[layer_idx, 1], cache.block_tables, step.rows,
-                step.starts, NUM_KV_HEADS, err=cache.err_flag, q_lens=step.q_lens)
-            k_blocks, v_blocks = cache.read(layer_idx, step)
+            if use["qkv"]:
+                pagedkv.linear_rope_append(
+                    h, at.qkv_weight, at.qkv_bias, cos, sin, q_rot.transpose(1, 2),
+                    cache.buf[li, 0], cache.buf[li, 1], cache.block_tables, step.rows,
+                    step.starts, NUM_KV_HEADS, err=err, q_lens=step.q_lens)
+            else:
+                qkv = F.linear(h, at.qkv_weight, at.qkv_bias).view(
+                    B, T, NUM_HEADS + 2 * NUM_KV_HEADS, HEAD_DIM)
+                cache.append(li, step, qkv[:, :, :NUM_HEADS].transpose(1, 2),
+                             qkv[:, :, NUM_HEADS:NUM_HEADS + NUM_KV_HEADS].transpose(1, 2),
+                             qkv[:, :, NUM_HEADS + NUM_KV_HEADS:].transpose(1, 2), cos, sin,
+                             q_rot.transpose(1, 2))
+            k_blocks, v_blocks = cache.read(li, step)
             out = torch.empty(B, T, NUM_HEADS, HEAD_DIM, device=xs.device, dtype=xs.dtype)
             flash_attention(q_rot.transpose(1, 2), k_blocks, v_blocks, is_causal, kv_lens,
                             out=out.transpose(1, 2))
-            h = pagedkv.linear_add_rmsnorm(out.view(N, NUM_HEADS * HEAD_DIM), at.o_proj.weight, xs,
-                                           layer.post_attention_layernorm.weight, RMS_NORM_EPS,
-                                           resid_out=xs, err=cache.err_flag)
-            act = pagedkv.linear_silu_mul(h, mlp.gate_up_weight, err=cache.err_flag)
-            if layer_idx + 1 < len(self.layers):
-                h = pagedkv.linear_add_rmsnorm(act, mlp.down_proj.weight, xs,
-                                               self.layers[layer_idx + 1].input_layernorm.weight,
-                                               RMS_NORM_EPS, resid_out=xs, err=cache.err_flag)
+            o_in = out.view(N, NUM_HEADS * HEAD_DIM)
+            post_w = layer.post_attention_layernorm.weight
+            if use["o"]:
+                h = pagedkv.linear_add_rmsnorm(o_in, at.o_proj.weight, xs, post_w, RMS_NORM_EPS,
+                                               resid_out=xs, err=err)
             else:
-                m = pagedkv.linear(act, mlp.down_proj.weight, err=cache.err_flag)
+                h = pagedkv.add_rmsnorm(F.linear(o_in, at.o_proj.weight), xs, post_w, RMS_NORM_EPS,
+                                        resid_out=xs)
+            if use["gate_up"]:
+                act = pagedkv.linear_silu_mul(h, mlp.gate_up_weight, err=err)
+            else:
+                act = pagedkv.silu_mul(F.linear(h, mlp.gate_up_weight))
+            if li < last:
+                nxt = self.layers[li + 1]
+                norm_w = nxt.input_layernorm.weight
+                if use["down"]:
+                    h = pagedkv.linear_add_rmsnorm(act, mlp.down_proj.weight, xs, norm_w,
+                                                   RMS_NORM_EPS, resid_out=xs, err=err)
+                else:
+                    h = pagedkv.add_rmsnorm(F.linear(act, mlp.down_proj.weight), xs, norm_w,
+                                            RMS_NORM_EPS, resid_out=xs)
+            elif use["down"]:
+                m = pagedkv.linear(act, mlp.down_proj.weight, err=err)
+            else:
+                m = F.linear(act, mlp.down_proj.weight)
         return m
 
     @property
     def fused(self):
         return getattr(self, "_fused", False)
 
-    # steps of <= 256 rows use the skinny tensor-core GEMMs (fused path only)
+    # Fused path: a projection of a step with at most skinny_rows[op] rows
+    # runs as the skinny tensor-core GEMM (pkv_linear*), larger ones on
+    # cuBLAS; the limits are where the skinny GEMM stops beating cuBLAS on a
+    # B200 (measured per projection, CUDA-graph replay).
     skinny_linears = True
+    skinny_rows = {"qkv": 32, "o": 32, "gate_up": 32, "down": 128}
 
     def fuse_weights_(self):
         """Merge q/k/v (weights + biases) and gate/up weights into single

@@ -155,8 +155,8 @@ _lin_workspaces: dict[int, torch.Tensor] = {}
 
 
 def linear_workspace(rows: int, n: int, k: int, device: torch.device) -> torch.Tensor:
-    """Grow-only fp32 split-k scratch of the skinny linear entries for `device`
-    (the same retire-but-keep-alive rule as decode_workspace)."""
+    """Grow-only scratch of the fused skinny linear entries for `device` (their
+    bf16 GEMM output; the same retire-but-keep-alive rule as decode_workspace)."""
     need = max(int(lib().pkv_linear_workspace_size(rows, n, k)), 16)
     idx = device.index if device.index is not None else torch.cuda.current_device()
     ws = _lin_workspaces.get(idx)
@@ -293,11 +293,9 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
     n = w.shape[0]
     if out is None:
         out = torch.empty(rows, n, dtype=x.dtype, device=x.device)
-    ws = linear_workspace(rows, n, k, x.device)
     wp, ldw, lay = _w_args(w)
     st = lib().pkv_linear(_ptr(x), x.stride(0), wp, ldw, lay, _ptr(bias), rows, n, k,
-                          _ptr(out), out.stride(0), _ptr(ws), ws.numel(), _ptr(err),
-                          _stream(x.device))
+                          _ptr(out), out.stride(0), None, 0, _ptr(err), _stream(x.device))
     _check(st, "pkv_linear")
     return out
 

@@ -109,13 +109,26 @@ def test_engine_serves_chats_with_eviction(cuda, small_model):
         m._graphs.clear()
 
 
-def test_prefill_graph_matches_eager(cuda, small_model):
+@pytest.mark.parametrize("gemm", ["cublas", "skinny"])
+def test_prefill_graph_matches_eager(cuda, small_model, gemm):
     """One-row prefills replayed from padded-length graphs give the eager
     prefill's logits and K/V (up to GEMM rounding), and only real tokens land
-    in the pool."""
+    in the pool.  A padded graph has more rows than the eager call, so the
+    row-count policy could pick another GEMM for it: each run pins one GEMM
+    family for both arms (cuBLAS, or the skinny GEMMs at every row count)."""
+    m = small_model.fuse_weights_()
+    saved = m.skinny_linears, m.skinny_rows
+    m.skinny_linears = gemm == "skinny"
+    m.skinny_rows = {op: 256 for op in saved[1]}
+    try:
+        _prefill_graph_vs_eager(cuda, m)
+    finally:
+        m.skinny_linears, m.skinny_rows = saved
+
+
+def _prefill_graph_vs_eager(cuda, m):
     from kv_cache import KVCache
 
-    m = small_model.fuse_weights_()
     g = torch.Generator().manual_seed(2)
     prompts = [torch.randint(0, 151936, (n,), generator=g).tolist() for n in (70, 5, 200, 64)]
     res = []

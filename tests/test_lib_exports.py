@@ -78,12 +78,9 @@ def test_linear_workspace_plan_and_validation_without_a_gpu():
     import pagedkv
 
     L = pagedkv.lib()
-    # fp32 partials: splits * rows * n * 4 bytes, at least one split
+    # the fused entries keep the bf16 GEMM output: rows * n * 2 bytes
     for rows, n, k in ((1, 2048, 1536), (16, 1536, 8960), (256, 17920, 1536)):
-        need = L.pkv_linear_workspace_size(rows, n, k)
-        assert need >= rows * n * 4 and need % (rows * n * 4) == 0, (rows, n, k, need)
-    # a long k splits further than a short one for the same output
-    assert L.pkv_linear_workspace_size(16, 1536, 8960) > L.pkv_linear_workspace_size(16, 1536, 128)
+        assert L.pkv_linear_workspace_size(rows, n, k) == rows * n * 2
     for bad in ((0, 2048, 1536), (257, 2048, 1536), (16, 2000, 1536), (16, 2048, 1000)):
         assert L.pkv_linear_workspace_size(*bad) == 0
     # argument checks come before any CUDA call
@@ -95,6 +92,9 @@ def test_linear_workspace_plan_and_validation_without_a_gpu():
     assert st == 3  # PKV_ERR_ALIGN: x not 16-byte aligned
     st = L.pkv_linear_silu_mul(16, 1536, 16, 1536, 0, 16, 100, 1536, 16, 100, None, 0, None, None)
     assert st == 2  # inter not a multiple of 64
+    st = L.pkv_linear_silu_mul(16, 1536, 16, 1536, 0, 16, 8960, 1536, 16, 8960, None, 0, None,
+                               None)
+    assert st == 6  # PKV_ERR_WORKSPACE: the fused entries need their intermediate
     st = L.pkv_linear(16, 1536, 16, 1536, 7, None, 16, 2048, 1536, 16, 2048, None, 0, None, None)
     assert st == 1  # unknown weight layout
     st = L.pkv_linear_pack_weight(16, 1536, 2000, 1536, 16, None)

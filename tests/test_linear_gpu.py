@@ -2,10 +2,10 @@
 
 The plain GEMM is checked against an fp64 product of the same bf16 inputs
 (the nn.Linear the reference runs, model.py:83-86 and :114-116, up to fp32
-summation order and one bf16 rounding).  The fused entries must equal, bit
-for bit, the plain GEMM followed by the separate kernel they fuse
-(add_rmsnorm, silu_mul, append_rope), because they round the same fp32 sums
-at the same point.
+summation order and one bf16 rounding), for row counts that exercise one
+split and cluster split-k reductions of up to 16 CTAs.  The fused entries
+must equal, bit for bit, the plain GEMM followed by the separate kernel they
+fuse (add_rmsnorm, silu_mul, append_rope).
 """
 import ctypes
 import math
@@ -165,15 +165,19 @@ def test_linear_rejections(cuda):
         pagedkv.linear(x, w)
     with pytest.raises(pagedkv.PagedKVError, match="multiple of 128"):
         pagedkv.linear(x[:16], w[:2000])
-    # a workspace smaller than the plan's partials: refused before any launch
-    y = torch.zeros(16, 1536, device=cuda, dtype=torch.bfloat16)
+    # a fused entry with a workspace smaller than its bf16 intermediate:
+    # refused before any launch
     x2, w2, _ = _operands(16, 1536, 8960, cuda, 2, bias=False)
     need = L.pkv_linear_workspace_size(16, 1536, 8960)
-    assert need > 0
+    assert need == 16 * 1536 * 2
     ws = torch.empty(need - 16, dtype=torch.uint8, device=cuda)
-    st = L.pkv_linear(x2.data_ptr(), x2.stride(0), w2.data_ptr(), w2.stride(0), 0, None, 16,
-                      1536, 8960, y.data_ptr(), y.stride(0), ws.data_ptr(), ws.numel(), None,
-                      torch.cuda.current_stream().cuda_stream)
+    resid = torch.zeros(16, 1536, device=cuda, dtype=torch.bfloat16)
+    nw = torch.ones(1536, device=cuda, dtype=torch.bfloat16)
+    out = torch.zeros(16, 1536, device=cuda, dtype=torch.bfloat16)
+    st = L.pkv_linear_add_rmsnorm(
+        x2.data_ptr(), x2.stride(0), w2.data_ptr(), w2.stride(0), 0, 16, 1536, 8960,
+        resid.data_ptr(), 1536, resid.data_ptr(), 1536, nw.data_ptr(), 1e-6, out.data_ptr(), 1536,
+        ws.data_ptr(), ws.numel(), None, torch.cuda.current_stream().cuda_stream)
     assert st == 6  # PKV_ERR_WORKSPACE
     torch.cuda.synchronize()
-    assert int(y.count_nonzero()) == 0
+    assert int(out.count_nonzero()) == 0
