@@ -26,10 +26,11 @@
 //               (one output feature n) per thread, all batch rows as columns
 // Epilogue: each CTA moves its fp32 accumulators from TMEM to its own shared
 // memory (over the drained ring).  Split-k: the `splits` CTAs of one W tile
-// form a thread-block cluster (1 x splits) and CTA r adds up batch rows
-// [r*M/splits, ...) of all the cluster's partials through distributed shared
-// memory, in split order (deterministic).  Bias, one bf16 rounding and
-// 8-byte row-contiguous stores of y; nothing else goes to global memory.
+// form a thread-block cluster (1 x splits); each pushes its partial rows into
+// the receive buffer of the CTA that owns them (distributed shared memory
+// stores + a remote mbarrier arrive), and owner r adds batch rows
+// [r*M/splits, ...) in split order (deterministic).  Bias, one bf16 rounding
+// and 8-byte row-contiguous stores of y; nothing else goes to global memory.
 // Every wait is bounded.
 #include <map>
 #include <mutex>
@@ -58,15 +59,11 @@ struct LinParams {
   const __nv_bfloat16* bias;  // nullable
   int32_t M, N, chunks, splits, stages, mpad;
   uint32_t tmem_cols, idesc;
-  int32_t w_tiled;  // W packed as [N/128][K/64][128][64]: one contiguous 16 KiB box per chunk
+  int32_t recv_off;  // split-k receive buffer: [splits][rows per owner][128] fp32
+  int32_t w_tiled;   // W packed as [N/128][K/64][128][64]: one contiguous 16 KiB box per chunk
   int32_t* err;
 };
 
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile(
-      "barrier.cluster.arrive.release.aligned;\n\t"
-      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -78,13 +75,40 @@ __device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
 }
-__device__ __forceinline__ float4 ld_cluster4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void st_cluster4(uint32_t addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
                : "memory");
-  return v;
+}
+// arrive on an mbarrier of another CTA of the cluster, releasing this
+// thread's earlier (and, through a preceding bar.sync, the CTA's) writes
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile(
+      "fence.acq_rel.cluster;\n\t"
+      "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_wait_acq_cluster(uint64_t* bar, uint32_t parity,
+                                                      const DevErr& err) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  err.raise(PKV_DEVERR_TIMEOUT);
+  return false;
 }
 
 __global__ void __launch_bounds__(kLinThreads, 1)
@@ -97,7 +121,11 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * stage_bytes);
   uint64_t* empty = full + p.stages;
   uint64_t* done = empty + p.stages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* recv_bar = done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
+  float* recv = reinterpret_cast<float*>(smem + p.recv_off);
+  const bool clustered = p.splits > 1;
+  const int per = (p.M + p.splits - 1) / p.splits;  // batch rows each cluster CTA owns
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -113,6 +141,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
       mbar_init(&empty[s], 1);  // tcgen05.commit after the chunk's MMAs
     }
     mbar_init(done, 1);
+    if (clustered) mbar_init(recv_bar, p.splits);  // one arrival per cluster CTA
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, p.tmem_cols);
@@ -120,6 +149,9 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // every CTA's recv_bar is initialised before any CTA arrives on it: the
+  // matching wait sits before the epilogue's remote stores
+  if (clustered) cluster_arrive();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -195,38 +227,10 @@ __global__ void __launch_bounds__(kLinThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, p.tmem_cols);
   }
-  // Store: thread = 4 consecutive features of one batch row.  With a split,
-  // CTA r of the cluster sums rows [r*per, (r+1)*per) over every split's
-  // shared memory (all loads in flight, adds in split order).
-  const bool clustered = p.splits > 1;
-  if (clustered) cluster_sync_all();  // every split's partial is in shared memory
-  const int per = (p.M + p.splits - 1) / p.splits;
-  const int m0 = clustered ? static_cast<int>(cluster_rank()) * per : 0;
-  const int m1 = min(p.M, m0 + per);
-  const uint32_t base = smem_u32(smem);
-  for (int idx = tid; idx < (m1 - m0) * (kTileN / 4); idx += kLinThreads) {
-    const int m = m0 + idx / (kTileN / 4);
-    const int nl = (idx % (kTileN / 4)) * 4;
-    const uint32_t off = base + static_cast<uint32_t>((m * kTileN + nl) * 4);
-    float4 acc;
-    if (clustered) {
-      float4 v[kMaxSplits];
-#pragma unroll
-      for (int sp = 0; sp < kMaxSplits; ++sp)
-        if (sp < p.splits) v[sp] = ld_cluster4(map_rank(off, sp));
-      acc = v[0];
-#pragma unroll
-      for (int sp = 1; sp < kMaxSplits; ++sp) {
-        if (sp < p.splits) {
-          acc.x += v[sp].x;
-          acc.y += v[sp].y;
-          acc.z += v[sp].z;
-          acc.w += v[sp].w;
-        }
-      }
-    } else {
-      acc = *reinterpret_cast<const float4*>(smem + (m * kTileN + nl) * 4);
-    }
+  // Store: thread = 4 consecutive features of one batch row, bias, one bf16
+  // rounding, 8-byte row-contiguous stores of y.
+  const float* red = reinterpret_cast<const float*>(smem);
+  auto store4 = [&](int m, int nl, float4 acc) {
     const int n = tile * kTileN + nl;
     if (p.bias) {
       acc.x += bf(p.bias[n + 0]);
@@ -238,8 +242,48 @@ __global__ void __launch_bounds__(kLinThreads, 1)
     o.x = pack_bf16(acc.x, acc.y);
     o.y = pack_bf16(acc.z, acc.w);
     *reinterpret_cast<uint2*>(p.y + m * p.ldy + n) = o;
+  };
+  if (!clustered) {
+    for (int idx = tid; idx < p.M * (kTileN / 4); idx += kLinThreads) {
+      const int m = idx / (kTileN / 4), nl = (idx % (kTileN / 4)) * 4;
+      store4(m, nl, *reinterpret_cast<const float4*>(red + m * kTileN + nl));
+    }
+    return;
   }
-  if (clustered) cluster_sync_all();  // no CTA exits while another reads its shared memory
+  // Split-k over the cluster: CTA r owns batch rows [r*per, r*per + per).
+  // Push this split's partial rows into their owners' receive buffers (slot
+  // = this CTA's rank), then arrive on each owner's recv_bar; an owner waits
+  // for all `splits` arrivals and adds the slots in split order.  Nothing is
+  // read from another CTA, so no CTA has to wait for the others to exit.
+  cluster_wait();
+  const uint32_t rank = cluster_rank();
+  const uint32_t recv_base = smem_u32(recv);
+  for (int idx = tid; idx < p.M * (kTileN / 4); idx += kLinThreads) {
+    const int m = idx / (kTileN / 4), nl = (idx % (kTileN / 4)) * 4;
+    const int owner = m / per;
+    const uint32_t dst = recv_base + static_cast<uint32_t>(((rank * per + (m - owner * per)) * kTileN + nl) * 4);
+    st_cluster4(map_rank(dst, static_cast<uint32_t>(owner)),
+                *reinterpret_cast<const float4*>(red + m * kTileN + nl));
+  }
+  __syncthreads();
+  if (tid < p.splits && tid * per < p.M)
+    mbar_arrive_remote(map_rank(smem_u32(recv_bar), static_cast<uint32_t>(tid)));
+  const int m0 = static_cast<int>(rank) * per;
+  const int m1 = min(p.M, m0 + per);
+  if (m0 < m1 && mbar_wait_acq_cluster(recv_bar, 0, err)) {
+    for (int idx = tid; idx < (m1 - m0) * (kTileN / 4); idx += kLinThreads) {
+      const int j = idx / (kTileN / 4), nl = (idx % (kTileN / 4)) * 4;
+      float4 acc = *reinterpret_cast<const float4*>(recv + j * kTileN + nl);
+      for (int sp = 1; sp < p.splits; ++sp) {
+        const float4 v = *reinterpret_cast<const float4*>(recv + (sp * per + j) * kTileN + nl);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      store4(m0 + j, nl, acc);
+    }
+  }
 }
 
 // w[n][k] (row stride ldw) -> [n/128][k/64][128][64]; one thread per 16 bytes
@@ -327,6 +371,18 @@ int max_clusters(int splits, int smem_bytes, int tiles) {
 
 }  // namespace
 
+// Shared-memory layout: TMA ring | mbarriers + TMEM slot | split-k receive
+// buffer; the ring doubles as the CTA's [mpad][128] fp32 accumulator copy.
+static void size_smem(LinearPlan& pl, int M, int splits, int stages) {
+  const int stage_bytes = kWBytes + pl.mpad * 128;
+  pl.stages = stages;
+  const int bars = (2 * stages + 2) * 8 + 4;
+  pl.recv_off = (stages * stage_bytes + bars + 15) / 16 * 16;
+  const int per = (M + splits - 1) / splits;
+  const int recv = splits > 1 ? splits * per * kTileN * 4 : 0;
+  pl.smem_bytes = pl.recv_off + recv + 1024;
+}
+
 LinearPlan plan_linear(int32_t M, int32_t N, int32_t K) {
   LinearPlan pl{};
   pl.mpad = (M + 15) / 16 * 16;
@@ -336,22 +392,30 @@ LinearPlan plan_linear(int32_t M, int32_t N, int32_t K) {
   const int stage_bytes = kWBytes + pl.mpad * 128;
   // two CTAs per SM while the ring still holds >= 4 stages, else one
   const int per_sm = (pl.mpad <= 64) ? 2 : 1;
-  const int budget = (per_sm == 2 ? kSmemCap / 2 : kSmemCap) - 1024 - 256;
-  pl.stages = budget / stage_bytes;
-  if (pl.stages > kMaxStages) pl.stages = kMaxStages;
-  pl.smem_bytes = pl.stages * stage_bytes + (2 * pl.stages + 1) * 8 + 16 + 1024;
+  const int cap = (per_sm == 2 ? kSmemCap / 2 : kSmemCap);
+  auto stages_for = [&](int splits) {
+    const int per = (M + splits - 1) / splits;
+    const int recv = splits > 1 ? splits * per * kTileN * 4 : 0;
+    int st = (cap - recv - 1024 - 256) / stage_bytes;
+    return st > kMaxStages ? kMaxStages : st;
+  };
   // Split k over a cluster of up to 16 CTAs per W tile: the most splits for
   // which every tile's cluster is resident in one wave (a second wave would
-  // run alone) and each split keeps >= 2 chunks.  The split partials are
-  // reduced in shared memory, which must hold [mpad][128] fp32.
+  // run alone), each split keeps >= 2 chunks and the ring (>= 3 stages) can
+  // hold the [mpad][128] fp32 accumulator copy.
   const int wave = sm_count() * per_sm;
   int smax = wave / (pl.tiles > 0 ? pl.tiles : 1);
   if (smax > kMaxSplits) smax = kMaxSplits;
   if (smax > pl.chunks / 2) smax = pl.chunks / 2;
-  if (pl.stages * stage_bytes < pl.mpad * kTileN * 4) smax = 1;
+  size_smem(pl, M, 1, stages_for(1));
   pl.splits = 1;
   for (int cand = smax; cand >= 2; --cand) {
-    if (max_clusters(cand, pl.smem_bytes, pl.tiles) >= pl.tiles) {
+    const int st = stages_for(cand);
+    if (st < 3 || st * stage_bytes < pl.mpad * kTileN * 4) continue;
+    LinearPlan trial = pl;
+    size_smem(trial, M, cand, st);
+    if (max_clusters(cand, trial.smem_bytes, pl.tiles) >= pl.tiles) {
+      pl = trial;
       pl.splits = cand;
       break;
     }
@@ -377,6 +441,7 @@ cudaError_t launch_linear(const LinearLaunch& a, const LinearPlan& pl, const CUt
   p.stages = pl.stages;
   p.mpad = pl.mpad;
   p.tmem_cols = pl.tmem_cols;
+  p.recv_off = pl.recv_off;
   p.w_tiled = a.w_tiled;
   // kind::f16 instruction descriptor: fp32 D, bf16 A and B, both K-major,
   // N = mpad (>> 3 at bit 17), M = 128 (>> 4 at bit 24)

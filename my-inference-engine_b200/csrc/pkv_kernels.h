@@ -119,6 +119,7 @@ struct LinearPlan {
   int32_t splits;  // split-k factor = cluster size (grid.y)
   int32_t stages;  // TMA ring depth
   int32_t smem_bytes;
+  int32_t recv_off;  // byte offset of the split-k receive buffer
   uint32_t tmem_cols;
 };
 struct LinearLaunch {
