@@ -71,6 +71,20 @@ def parse():
     ap.add_argument("--engine4-reply", type=int, default=128)
     ap.add_argument("--engine4-pool-gb", type=float, default=120.0)
     ap.add_argument("--prefill-steps", type=int, default=20)
+    # diagnostics (print their own JSON lines and exit; not the bench line)
+    ap.add_argument("--linear-sweep", type=str, default=None, metavar="ROWS",
+                    help="comma-separated row counts: per-projection GEMM + fused-op times, "
+                         "skinny tensor-core GEMMs vs cuBLAS, CUDA-graph replay")
+    ap.add_argument("--decode-step", type=str, default=None, metavar="B:CTX",
+                    help="whole-model decode step time (CUDA graph) at B rows of CTX tokens, "
+                         "skinny-GEMM policy vs cuBLAS")
+    ap.add_argument("--prefill-step", type=int, default=None, metavar="T",
+                    help="whole-model one-row prefill of T tokens (CUDA graph of the padded "
+                         "bucket, as chat.py admits a message)")
+    ap.add_argument("--profile-range", action="store_true",
+                    help="with --decode-step / --prefill-step: one eager step inside "
+                         "cudaProfilerStart/Stop "
+                         "(for ncu --profile-from-start off)")
     return ap.parse_args()
 
 
@@ -555,6 +569,189 @@ def replica_rate(units_per_rank, ms_local, device, world):
 
 
 # ---------------------------------------------------------------- main
+
+
+# ---------------------------------------------------------------- diagnostics
+def _graph_us(fn, calls):
+    """Mean device time per call of `fn` (which makes `calls` calls), replayed
+    from one CUDA graph; median of 10 replays."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(10):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b) * 1e3 / calls)
+    return statistics.median(ts)
+
+
+def linear_sweep(rows_list, device):
+    """Each Qwen2.5-1.5B projection with the op it feeds, as one decode layer
+    runs it: 28 distinct weight copies (weights stream from HBM as in a real
+    step), one CUDA graph of 28 calls.  cuBLAS (F.linear) + the separate fused
+    kernel vs the fused skinny-GEMM entry."""
+    import pagedkv
+
+    peaks, src = measured_peaks()
+    peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
+    nw = torch.ones(1536, device=device, dtype=torch.bfloat16)
+    for n, k, op in ((2048, 1536, "qkv"), (1536, 1536, "o+add_rmsnorm"),
+                     (17920, 1536, "gate_up+silu_mul"), (1536, 8960, "down+add_rmsnorm")):
+        ws = [(0.02 * torch.randn(n, k, device=device)).to(torch.bfloat16) for _ in range(L)]
+        for rows in rows_list:
+            x = torch.randn(rows, k, device=device).to(torch.bfloat16)
+            resid = torch.randn(rows, 1536, device=device).to(torch.bfloat16)
+            outs = [torch.empty(rows, n, device=device, dtype=torch.bfloat16) for _ in range(L)]
+            if op == "qkv":
+                def cub():
+                    for w, o in zip(ws, outs):
+                        torch.matmul(x, w.T, out=o)
+
+                def ours():
+                    for w, o in zip(ws, outs):
+                        pagedkv.linear(x, w, out=o)
+            elif op.startswith("gate_up"):
+                acts = [torch.empty(rows, n // 2, device=device, dtype=torch.bfloat16)
+                        for _ in range(L)]
+
+                def cub():
+                    for w, o, a in zip(ws, outs, acts):
+                        torch.matmul(x, w.T, out=o)
+                        pagedkv.silu_mul(o, out=a)
+
+                def ours():
+                    for w, a in zip(ws, acts):
+                        pagedkv.linear_silu_mul(x, w, out=a)
+            else:
+                hs = [torch.empty(rows, 1536, device=device, dtype=torch.bfloat16)
+                      for _ in range(L)]
+
+                def cub():
+                    for w, o, h in zip(ws, outs, hs):
+                        torch.matmul(x, w.T, out=o)
+                        pagedkv.add_rmsnorm(o, resid, nw, 1e-6, resid_out=resid, out=h)
+
+                def ours():
+                    for w, h in zip(ws, hs):
+                        pagedkv.linear_add_rmsnorm(x, w, resid, nw, 1e-6, resid_out=resid, out=h)
+            t_c, t_o = _graph_us(cub, L), _graph_us(ours, L)
+            wb = n * k * 2
+            print(json.dumps({"diag": "linear_sweep", "op": op, "rows": rows, "n": n, "k": k,
+                              "cublas_us": round(t_c, 2), "skinny_us": round(t_o, 2),
+                              "skinny_weight_gbs": round(wb / t_o / 1e3, 1),
+                              "skinny_frac_of_hbm": round(wb / t_o / 1e3 / peak, 3),
+                              "peak_source": src}), flush=True)
+        del ws
+
+
+def decode_step_diag(spec, device, profile_range=False):
+    """Whole-model decode step (random-init Qwen2.5-1.5B, B rows of CTX
+    tokens of history) replayed from a CUDA graph, under the skinny-GEMM
+    policy and with every projection on cuBLAS."""
+    import model as M
+    from kv_cache import KVCache
+
+    B, ctx = (int(v) for v in spec.split(":"))
+    m = M.Qwen2ForCausalLM().to(device, torch.bfloat16).eval()
+    random_init_(m, 11)
+    m.fuse_weights_()
+    cache = KVCache(B * (ctx // 16 + 8) + 16, 16, device, torch.bfloat16, max_seqs=max(B, 16))
+    seqs = [cache.alloc() for _ in range(B)]
+    for s_ in seqs:  # a history of ctx tokens per row (pool contents irrelevant to timing)
+        cache.ensure_capacity(s_, ctx)
+    cache.advance(seqs, ctx)
+    ids = torch.randint(0, 1000, (B, 1), device=device)
+    res = {}
+    with torch.no_grad():
+        for policy in ("skinny", "cublas"):
+            m.skinny_linears = policy == "skinny"
+            m.enable_decode_graphs(cache, max_batch=max(B, 16))
+            for _ in range(3):
+                m(ids, cache, seqs)
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(10):
+                m(ids, cache, seqs)
+            b.record()
+            b.synchronize()
+            res[policy] = round(a.elapsed_time(b) / 10, 4)
+            m._graphs.clear()
+        m.skinny_linears = True
+        if profile_range:
+            m(ids, cache, seqs)
+            torch.cuda.synchronize()
+            torch.cuda.profiler.start()
+            m(ids, cache, seqs)
+            torch.cuda.synchronize()
+            torch.cuda.profiler.stop()
+    print(json.dumps({"diag": "decode_step", "rows": B, "ctx": ctx,
+                      "graph_ms_skinny_policy": res["skinny"], "graph_ms_cublas": res["cublas"],
+                      "skinny_rows": M.Qwen2ForCausalLM.skinny_rows}), flush=True)
+
+
+def prefill_step_diag(T, device, profile_range=False):
+    """One-row prefill of T tokens from an empty cache (random-init model):
+    CUDA-graph replay of the padded bucket (the engine's path) and eager;
+    model FLOPs/s against the measured bf16 peak."""
+    import model as M
+    from kv_cache import KVCache
+
+    m = M.Qwen2ForCausalLM().to(device, torch.bfloat16).eval()
+    random_init_(m, 11)
+    m.fuse_weights_()
+    cache = KVCache(T // 16 + 64, 16, device, torch.bfloat16, max_seqs=16)
+    ids = torch.randint(0, 1000, (1, T), device=device)
+    nparams = sum(p.numel() for n_, p in m.named_parameters() if "embed" not in n_)
+    flops = 2 * nparams * T + 4 * HQ * D * T * (T + 1) / 2 * L
+    res = {}
+    with torch.no_grad():
+        for mode in ("graph", "eager"):
+            if mode == "graph":
+                m.enable_prefill_graphs(cache, max_len=max(T, 64))
+            else:
+                m._prefill_graphs.clear()
+            ts = []
+            for it in range(4):
+                s_ = cache.alloc()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                m(ids, cache, [s_])
+                b.record()
+                b.synchronize()
+                if it:
+                    ts.append(a.elapsed_time(b))
+                cache.free(s_)
+            res[mode] = round(statistics.median(ts), 3)
+        if profile_range:
+            s_ = cache.alloc()
+            torch.cuda.synchronize()
+            torch.cuda.profiler.start()
+            m(ids, cache, [s_])
+            torch.cuda.synchronize()
+            torch.cuda.profiler.stop()
+            cache.free(s_)
+    peaks, src = measured_peaks()
+    pk = float(peaks.get("bf16_tflops", 1590.0))
+    tf = flops / res["graph"] / 1e9
+    print(json.dumps({"diag": "prefill_step", "T": T, "graph_ms": res["graph"],
+                      "eager_ms": res["eager"], "model_tflops_graph": round(tf, 1),
+                      "frac_of_bf16_peak": round(tf / pk, 3), "peak_source": src}), flush=True)
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -567,6 +764,17 @@ def main():
               "pool_gb": args.pool_gb, "layers": args.layers, "block_size": 16,
               "heads": [HQ, HKV, D], "l2": "inputs larger than L2 (KV read per step >> 126 MB)",
               "parallelism": f"replicas x{args.gpus} (request-sharded, no collective)"}
+
+    if args.linear_sweep or args.decode_step or args.prefill_step:
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        if args.linear_sweep:
+            linear_sweep([int(r) for r in args.linear_sweep.split(",")], dev)
+        if args.decode_step:
+            decode_step_diag(args.decode_step, dev, args.profile_range)
+        if args.prefill_step:
+            prefill_step_diag(args.prefill_step, dev, args.profile_range)
+        return
 
     if args.impl == "reference":
         if rank != 0:
