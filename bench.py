@@ -608,6 +608,7 @@ def linear_sweep(rows_list, device):
     peaks, src = measured_peaks()
     peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
     nw = torch.ones(1536, device=device, dtype=torch.bfloat16)
+    paired = None
     for n, k, op in ((2048, 1536, "qkv"), (1536, 1536, "o+add_rmsnorm"),
                      (17920, 1536, "gate_up+silu_mul"), (1536, 8960, "down+add_rmsnorm")):
         ws = [(0.02 * torch.randn(n, k, device=device)).to(torch.bfloat16) for _ in range(L)]
@@ -626,6 +627,8 @@ def linear_sweep(rows_list, device):
             elif op.startswith("gate_up"):
                 acts = [torch.empty(rows, n // 2, device=device, dtype=torch.bfloat16)
                         for _ in range(L)]
+                if rows == rows_list[0]:  # the model's layout: SwiGLU in the GEMM epilogue
+                    paired = [pagedkv.PairedGateUp(w) for w in ws]
 
                 def cub():
                     for w, o, a in zip(ws, outs, acts):
@@ -633,7 +636,7 @@ def linear_sweep(rows_list, device):
                         pagedkv.silu_mul(o, out=a)
 
                 def ours():
-                    for w, a in zip(ws, acts):
+                    for w, a in zip(paired, acts):
                         pagedkv.linear_silu_mul(x, w, out=a)
             else:
                 hs = [torch.empty(rows, 1536, device=device, dtype=torch.bfloat16)
@@ -655,6 +658,7 @@ def linear_sweep(rows_list, device):
                               "skinny_frac_of_hbm": round(wb / t_o / 1e3 / peak, 3),
                               "peak_source": src}), flush=True)
         del ws
+        paired = None
 
 
 def decode_step_diag(spec, device, profile_range=False):

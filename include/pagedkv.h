@@ -249,7 +249,10 @@ int pkv_paged_decode_static_scratch(const void* q, int64_t q_sb, int64_t q_sh,
  *   pkv_linear_silu_mul     merged gate/up GEMM (w rows [0, inter) gate,
  *                           [inter, 2 inter) up), then pkv_silu_mul
  *   pkv_linear_rope_append  merged q/k/v GEMM + bias, then pkv_append_rope
- *                           (rows = batch * seq_len_q, row b*seq_len_q + t)
+ *                           (rows = batch * seq_len_q, row b*seq_len_q + t);
+ *                           done in the GEMM's epilogue (no workspace) when
+ *                           q_out is 16-byte aligned with strides that are
+ *                           multiples of 8, else as GEMM + append kernel
  * where n is the GEMM's width: dim, 2 * inter, (hq + 2 hkv) * head_dim.
  */
 #define PKV_LINEAR_MAX_ROWS 256
@@ -260,8 +263,20 @@ int pkv_paged_decode_static_scratch(const void* q, int64_t q_sb, int64_t q_sh,
                             128x64 tile one 16 KiB run, so the GEMM streams each
                             CTA's share of w as one contiguous range of HBM;
                             made by pkv_linear_pack_weight                         */
+#define PKV_W_GATE_UP_PAIRED 2 /* pkv_linear_silu_mul only: merged gate/up rows
+                            reordered so rows [128t, 128t+128) are gate rows
+                            [64t, 64t+64) then up rows [64t, 64t+64) (row stride
+                            ldw); the GEMM then finishes SwiGLU in its epilogue
+                            (no workspace, no second kernel); made by
+                            pkv_linear_pair_gate_up                               */
 
 size_t pkv_linear_workspace_size(int32_t rows, int32_t n, int32_t k);
+
+/* Reorder a merged gate/up weight ([2*inter][k], gate rows then up rows, row
+ * stride ldw) into the PKV_W_GATE_UP_PAIRED layout (2*inter rows of k,
+ * contiguous, at w_paired; inter % 64 == 0). */
+int pkv_linear_pair_gate_up(const void* w_gate_up, int64_t ldw, int32_t inter, int32_t k,
+                            void* w_paired, void* stream);
 
 /* Copy a row-major w[n][k] (row stride ldw) into the PKV_W_TILED layout
  * (n * k bf16 elements at w_tiled, 16-byte aligned). */

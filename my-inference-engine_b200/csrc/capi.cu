@@ -170,7 +170,7 @@ int encode_tiled(CUtensorMap* m, const void* base, int32_t n, int32_t k) {
 int check_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, int32_t w_layout,
                  int32_t rows, int32_t n, int32_t k) {
   if (!x || !w) return fail(PKV_ERR_INVALID, "null x or w");
-  if (w_layout != PKV_W_ROWMAJOR && w_layout != PKV_W_TILED)
+  if (w_layout != PKV_W_ROWMAJOR && w_layout != PKV_W_TILED && w_layout != PKV_W_GATE_UP_PAIRED)
     return fail(PKV_ERR_INVALID, "unknown weight layout %d", w_layout);
   if (w_layout == PKV_W_TILED) ldw = k;
   if (rows < 0 || rows > PKV_LINEAR_MAX_ROWS)
@@ -187,7 +187,8 @@ int check_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, int32_t
 // The GEMM half of every pkv_linear* entry: bf16 y (+ bias).
 int run_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, int32_t w_layout,
                int32_t rows, int32_t n, int32_t k, void* y, int64_t ldy, const void* bias,
-               int32_t* err, cudaStream_t stream) {
+               int32_t* err, cudaStream_t stream, bool swiglu = false,
+               const pkv::RopeAppend* rope = nullptr) {
   const pkv::LinearPlan pl = pkv::plan_linear(rows, n, k);
   CUtensorMap wmap, xmap;
   int st = w_layout == PKV_W_TILED ? encode_tiled(&wmap, w, n, k)
@@ -201,6 +202,8 @@ int run_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, int32_t w
   a.ldy = ldy;
   a.bias = bias;
   a.w_tiled = w_layout == PKV_W_TILED ? 1 : 0;
+  a.swiglu = swiglu ? 1 : 0;
+  if (rope) a.rope = *rope;
   a.err = err;
   return launch_status(pkv::launch_linear(a, pl, wmap, xmap, stream), "linear_tc");
 }
@@ -492,6 +495,20 @@ size_t pkv_linear_workspace_size(int32_t rows, int32_t n, int32_t k) {
   return static_cast<size_t>(rows) * n * 2;
 }
 
+int pkv_linear_pair_gate_up(const void* w_gate_up, int64_t ldw, int32_t inter, int32_t k,
+                            void* w_paired, void* stream) {
+  if (!w_gate_up || !w_paired) return fail(PKV_ERR_INVALID, "null w_gate_up or w_paired");
+  if (inter <= 0 || inter % 64 != 0 || k <= 0 || k % 64 != 0)
+    return fail(PKV_ERR_UNSUPPORTED, "inter and k must be positive multiples of 64 (got %d, %d)",
+                inter, k);
+  if (ldw < k) return fail(PKV_ERR_INVALID, "row stride smaller than k");
+  if (!aligned16(w_gate_up) || !aligned16(w_paired) || !mult8(ldw))
+    return fail(PKV_ERR_ALIGN, "weights must be 16-byte aligned, ldw a multiple of 8");
+  return launch_status(pkv::launch_pair_gate_up(w_gate_up, ldw, inter, k, w_paired,
+                                                static_cast<cudaStream_t>(stream)),
+                       "pair_gate_up");
+}
+
 int pkv_linear_pack_weight(const void* w, int64_t ldw, int32_t n, int32_t k, void* w_tiled,
                            void* stream) {
   if (!w || !w_tiled) return fail(PKV_ERR_INVALID, "null w or w_tiled");
@@ -513,6 +530,8 @@ int pkv_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, int32_t w
   (void)workspace_bytes;
   int st = check_linear(x, ldx, w, ldw, w_layout, rows, n, k);
   if (st) return st;
+  if (w_layout == PKV_W_GATE_UP_PAIRED)
+    return fail(PKV_ERR_INVALID, "PKV_W_GATE_UP_PAIRED weights are for pkv_linear_silu_mul only");
   if (!y) return fail(PKV_ERR_INVALID, "null y");
   if (!aligned16(y) || !mult8(ldy) || ldy < n || (bias && !aligned16(bias)))
     return fail(PKV_ERR_ALIGN, "y / bias must be 16-byte aligned, ldy a multiple of 8 >= n");
@@ -559,8 +578,14 @@ int pkv_linear_silu_mul(const void* x, int64_t ldx, const void* w_gate_up, int64
   if (!out) return fail(PKV_ERR_INVALID, "null out");
   if (!aligned16(out) || !mult8(o_stride)) return fail(PKV_ERR_ALIGN, "silu_mul rows must be 16-byte aligned");
   if (rows == 0) return ok();
-  if ((st = check_linear_ws(workspace, workspace_bytes, rows, n))) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (w_layout == PKV_W_GATE_UP_PAIRED) {  // SwiGLU in the GEMM's epilogue
+    if ((st = run_linear(x, ldx, w_gate_up, ldw, w_layout, rows, n, k, out, o_stride, nullptr,
+                         err_flag, s, true)))
+      return st;
+    return ok();
+  }
+  if ((st = check_linear_ws(workspace, workspace_bytes, rows, n))) return st;
   if ((st = run_linear(x, ldx, w_gate_up, ldw, w_layout, rows, n, k, workspace, n, nullptr,
                        err_flag, s)))
     return st;
@@ -597,8 +622,27 @@ int pkv_linear_rope_append(const void* x, int64_t ldx, const void* w_qkv, int64_
     return fail(PKV_ERR_ALIGN, "append pointers must be 4-byte aligned, bias 16-byte aligned");
   if ((qo_sb | qo_sh | qo_st) & 1) return fail(PKV_ERR_ALIGN, "q_out strides must be even");
   if (rows == 0) return ok();
-  if ((st = check_linear_ws(workspace, workspace_bytes, rows, n))) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (aligned16(q_out) && mult8(qo_sb) && mult8(qo_sh) && mult8(qo_st)) {
+    // RoPE + append in the GEMM's epilogue (8-byte stores of q_out rows)
+    pkv::RopeAppend r{};
+    r.q_out = static_cast<__nv_bfloat16*>(q_out);
+    r.qo_sb = qo_sb; r.qo_sh = qo_sh; r.qo_st = qo_st;
+    r.k_pool = static_cast<__nv_bfloat16*>(k_pool);
+    r.v_pool = static_cast<__nv_bfloat16*>(v_pool);
+    r.num_blocks = static_cast<int32_t>(num_slots / 16);
+    r.cos = static_cast<const __nv_bfloat16*>(rope_cos);
+    r.sin = static_cast<const __nv_bfloat16*>(rope_sin);
+    r.rope_rows = rope_rows;
+    r.tables = block_tables; r.pitch = table_pitch; r.rows = seq_rows; r.starts = starts;
+    r.q_lens = q_lens;
+    r.T = seq_len_q; r.hq = num_q_heads; r.hkv = num_kv_heads;
+    if ((st = run_linear(x, ldx, w_qkv, ldw, w_layout, rows, n, k, nullptr, 0, bias, err_flag, s,
+                         false, &r)))
+      return st;
+    return ok();
+  }
+  if ((st = check_linear_ws(workspace, workspace_bytes, rows, n))) return st;
   if ((st = run_linear(x, ldx, w_qkv, ldw, w_layout, rows, n, k, workspace, n, bias, err_flag, s)))
     return st;
   // the GEMM output [batch][seq_len_q][q heads | k heads | v heads][128]

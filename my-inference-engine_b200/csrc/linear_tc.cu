@@ -24,6 +24,14 @@
 //               D[128, Mpad] += W[128, 16] . x[Mpad, 16]^T, 4 per chunk
 //     warps 2-5 epilogue: warp w reads TMEM lanes 32*(w%4).., i.e. one W row
 //               (one output feature n) per thread, all batch rows as columns
+// RoPE + append mode (pkv_linear_rope_append): each 128-row W tile is one
+// head of the merged q/k/v projection, so the epilogue adds the bias, rounds
+// to bf16, rotates q and k (partner dims d and d+64 are both in the tile) and
+// stores q_rot and the new K/V rows into their pool slots: no intermediate,
+// no second kernel.
+// SwiGLU mode (pkv_linear_silu_mul with PKV_W_GATE_UP_PAIRED): every W tile
+// pairs 64 gate rows with the matching 64 up rows, so the epilogue finishes
+// the activation and y is the [M][N/2] SwiGLU output.
 // Epilogue: each CTA moves its fp32 accumulators from TMEM to its own shared
 // memory (over the drained ring).  Split-k: the `splits` CTAs of one W tile
 // form a thread-block cluster (1 x splits); each pushes its partial rows into
@@ -52,6 +60,13 @@ constexpr int kSmemCap = 227 * 1024;
 constexpr int kMaxSplits = 16;  // non-portable cluster size limit
 
 __device__ __forceinline__ float bf(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ __nv_bfloat16 rn(float x) { return __float2bfloat16_rn(x); }
+
+// bf16(bf16(x*c) + bf16(r*s)), each op rounded separately as the reference's
+// three torch ops (model.py:58-65) compute it
+__device__ __forceinline__ float rope1(float x, float c, float r, float sn) {
+  return bf(rn(__fadd_rn(bf(rn(__fmul_rn(x, c))), bf(rn(__fmul_rn(r, sn))))));
+}
 
 struct LinParams {
   __nv_bfloat16* y;  // [M][ldy]
@@ -61,7 +76,11 @@ struct LinParams {
   uint32_t tmem_cols, idesc;
   int32_t recv_off;  // split-k receive buffer: [splits][rows per owner][128] fp32
   int32_t w_tiled;   // W packed as [N/128][K/64][128][64]: one contiguous 16 KiB box per chunk
+  int32_t swiglu;    // W tiles pair 64 gate rows with their 64 up rows: y = SwiGLU, N/2 wide
   int32_t* err;
+  // RoPE + K/V append epilogue (rope.q_out != nullptr): tile = one head of
+  // the merged q/k/v output, row m = batch row m / T, step token m % T
+  RopeAppend rope;
 };
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -227,8 +246,10 @@ __global__ void __launch_bounds__(kLinThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, p.tmem_cols);
   }
-  // Store: thread = 4 consecutive features of one batch row, bias, one bf16
-  // rounding, 8-byte row-contiguous stores of y.
+  // Store: bias, one bf16 rounding (the value F.linear stores), 8-byte
+  // row-contiguous stores of y.  SwiGLU tiles: features i and 64 + i of a
+  // tile are gate and up of output 64*tile + i, combined exactly as
+  // pkv_silu_mul does: bf16(bf16(silu(bf16 g)) * bf16 u).
   const float* red = reinterpret_cast<const float*>(smem);
   auto store4 = [&](int m, int nl, float4 acc) {
     const int n = tile * kTileN + nl;
@@ -243,10 +264,100 @@ __global__ void __launch_bounds__(kLinThreads, 1)
     o.y = pack_bf16(acc.z, acc.w);
     *reinterpret_cast<uint2*>(p.y + m * p.ldy + n) = o;
   };
+  auto store_swiglu4 = [&](int m, int i, float4 g, float4 u) {
+    const float gv[4] = {g.x, g.y, g.z, g.w}, uv[4] = {u.x, u.y, u.z, u.w};
+    float r[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float gb = bf(__float2bfloat16_rn(gv[e]));
+      const float sb = bf(__float2bfloat16_rn(gb / (1.0f + expf(-gb))));
+      r[e] = __fmul_rn(sb, bf(__float2bfloat16_rn(uv[e])));
+    }
+    uint2 o;
+    o.x = pack_bf16(r[0], r[1]);
+    o.y = pack_bf16(r[2], r[3]);
+    *reinterpret_cast<uint2*>(p.y + m * p.ldy + tile * (kTileN / 2) + i) = o;
+  };
+  // RoPE + append (pkv_linear_rope_append): this tile is head `tile` of
+  // [q heads | k heads | v heads]; the thread owns dims d..d+3 and their
+  // rotation partners 64+d..64+d+3 of one token, exactly as append_rope_kernel
+  // treats the bf16 output of the q/k/v GEMM (bias added, one rounding)
+  const RopeAppend& ra = p.rope;
+  auto store_rope8 = [&](int m, int d, float4 lo, float4 hi) {
+    const int b = m / ra.T, tt = m - b * ra.T;
+    const int start = ra.starts[b];
+    if (start < 0) return;                        // inactive (padding) row
+    if (ra.q_lens && tt >= ra.q_lens[b]) return;  // right padding of a shorter row
+    const int pos = start + tt;
+    float xl[4] = {lo.x, lo.y, lo.z, lo.w}, xh[4] = {hi.x, hi.y, hi.z, hi.w};
+    const int n0 = tile * kTileN;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {  // the GEMM output in bf16, as F.linear stores it
+      const float bl = p.bias ? bf(p.bias[n0 + d + e]) : 0.f;
+      const float bh = p.bias ? bf(p.bias[n0 + 64 + d + e]) : 0.f;
+      xl[e] = bf(rn(xl[e] + bl));
+      xh[e] = bf(rn(xh[e] + bh));
+    }
+    const bool is_q = tile < ra.hq;
+    const bool is_v = tile >= ra.hq + ra.hkv;
+    __nv_bfloat16* dst;
+    if (is_q) {
+      dst = ra.q_out + b * ra.qo_sb + tile * ra.qo_sh + tt * ra.qo_st;
+    } else {
+      const int h = is_v ? tile - ra.hq - ra.hkv : tile - ra.hq;
+      const int row = ra.rows ? ra.rows[b] : b;
+      const int64_t bi = pos >> 4;
+      if (pos < 0 || bi >= ra.pitch) {
+        err.raise(PKV_DEVERR_POSITION);
+        return;
+      }
+      const int blk = ra.tables[static_cast<int64_t>(row) * ra.pitch + bi];
+      if (blk < 0 || blk >= ra.num_blocks) {
+        err.raise(PKV_DEVERR_BLOCK_ID);
+        return;
+      }
+      const int64_t slot = static_cast<int64_t>(blk) * kBlockTokens + (pos & 15);
+      dst = (is_v ? ra.v_pool : ra.k_pool) + (slot * ra.hkv + h) * kHeadDim;
+    }
+    float ol[4], oh[4];
+    if (is_v) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) ol[e] = xl[e], oh[e] = xh[e];
+    } else {
+      if (pos < 0 || pos >= ra.rope_rows) {
+        err.raise(PKV_DEVERR_POSITION);
+        return;
+      }
+      const __nv_bfloat16* cr = ra.cos + static_cast<int64_t>(pos) * kHeadDim;
+      const __nv_bfloat16* sr = ra.sin + static_cast<int64_t>(pos) * kHeadDim;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        // first half: x*cos + (-x2)*sin ; second half: x*cos + x1*sin
+        ol[e] = rope1(xl[e], bf(cr[d + e]), -xh[e], bf(sr[d + e]));
+        oh[e] = rope1(xh[e], bf(cr[64 + d + e]), xl[e], bf(sr[64 + d + e]));
+      }
+    }
+    uint2 o;
+    o.x = pack_bf16(ol[0], ol[1]);
+    o.y = pack_bf16(ol[2], ol[3]);
+    *reinterpret_cast<uint2*>(dst + d) = o;
+    o.x = pack_bf16(oh[0], oh[1]);
+    o.y = pack_bf16(oh[2], oh[3]);
+    *reinterpret_cast<uint2*>(dst + 64 + d) = o;
+  };
+  // quads per row: 32 features x 4, or 16 gate/up (or rotation) pairs x 4
+  const bool paired = p.swiglu || ra.q_out;
+  const int quads = paired ? kTileN / 8 : kTileN / 4;
   if (!clustered) {
-    for (int idx = tid; idx < p.M * (kTileN / 4); idx += kLinThreads) {
-      const int m = idx / (kTileN / 4), nl = (idx % (kTileN / 4)) * 4;
-      store4(m, nl, *reinterpret_cast<const float4*>(red + m * kTileN + nl));
+    for (int idx = tid; idx < p.M * quads; idx += kLinThreads) {
+      const int m = idx / quads, nl = (idx % quads) * 4;
+      const float4 a = *reinterpret_cast<const float4*>(red + m * kTileN + nl);
+      if (!paired)
+        store4(m, nl, a);
+      else if (p.swiglu)
+        store_swiglu4(m, nl, a, *reinterpret_cast<const float4*>(red + m * kTileN + 64 + nl));
+      else
+        store_rope8(m, nl, a, *reinterpret_cast<const float4*>(red + m * kTileN + 64 + nl));
     }
     return;
   }
@@ -270,18 +381,26 @@ __global__ void __launch_bounds__(kLinThreads, 1)
     mbar_arrive_remote(map_rank(smem_u32(recv_bar), static_cast<uint32_t>(tid)));
   const int m0 = static_cast<int>(rank) * per;
   const int m1 = min(p.M, m0 + per);
+  auto sum4 = [&](int j, int nl) {
+    float4 acc = *reinterpret_cast<const float4*>(recv + j * kTileN + nl);
+    for (int sp = 1; sp < p.splits; ++sp) {
+      const float4 v = *reinterpret_cast<const float4*>(recv + (sp * per + j) * kTileN + nl);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    return acc;
+  };
   if (m0 < m1 && mbar_wait_acq_cluster(recv_bar, 0, err)) {
-    for (int idx = tid; idx < (m1 - m0) * (kTileN / 4); idx += kLinThreads) {
-      const int j = idx / (kTileN / 4), nl = (idx % (kTileN / 4)) * 4;
-      float4 acc = *reinterpret_cast<const float4*>(recv + j * kTileN + nl);
-      for (int sp = 1; sp < p.splits; ++sp) {
-        const float4 v = *reinterpret_cast<const float4*>(recv + (sp * per + j) * kTileN + nl);
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
-      }
-      store4(m0 + j, nl, acc);
+    for (int idx = tid; idx < (m1 - m0) * quads; idx += kLinThreads) {
+      const int j = idx / quads, nl = (idx % quads) * 4;
+      if (!paired)
+        store4(m0 + j, nl, sum4(j, nl));
+      else if (p.swiglu)
+        store_swiglu4(m0 + j, nl, sum4(j, nl), sum4(j, 64 + nl));
+      else
+        store_rope8(m0 + j, nl, sum4(j, nl), sum4(j, 64 + nl));
     }
   }
 }
@@ -301,6 +420,25 @@ __global__ void __launch_bounds__(256)
   const int64_t t = tc / chunks;
   const uint4 v = *reinterpret_cast<const uint4*>(w + (t * kTileN + r) * ldw + c * kChunkK + j8 * 8);
   *reinterpret_cast<uint4*>(out + i * 8) = v;
+}
+
+// w_gate_up [2*inter][k] (gate rows, then up rows; row stride ldw) ->
+// [2*inter][k] with tile t = rows [128t, 128t+128) holding gate rows
+// [64t, 64t+64) then up rows [64t, 64t+64); one thread per 16 bytes
+__global__ void __launch_bounds__(256)
+    pair_gate_up_kernel(const __nv_bfloat16* __restrict__ w, int64_t ldw, int inter, int k,
+                        int64_t total16, __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total16) return;
+  const int per_row = k / 8;
+  const int64_t r = i / per_row;
+  const int c = static_cast<int>(i % per_row) * 8;
+  const int64_t t = r / kTileN;
+  const int within = static_cast<int>(r % kTileN);
+  const int64_t src = within < 64 ? t * 64 + within : inter + t * 64 + (within - 64);
+  *reinterpret_cast<uint4*>(out + r * k + c) = *reinterpret_cast<const uint4*>(w + src * ldw + c);
 }
 
 int sm_count() {
@@ -399,13 +537,17 @@ LinearPlan plan_linear(int32_t M, int32_t N, int32_t K) {
     int st = (cap - recv - 1024 - 256) / stage_bytes;
     return st > kMaxStages ? kMaxStages : st;
   };
-  // Split k over a cluster of up to 16 CTAs per W tile: the most splits for
-  // which every tile's cluster is resident in one wave (a second wave would
-  // run alone), each split keeps >= 2 chunks and the ring (>= 3 stages) can
-  // hold the [mpad][128] fp32 accumulator copy.
-  const int wave = sm_count() * per_sm;
-  int smax = wave / (pl.tiles > 0 ? pl.tiles : 1);
+  // Split k over a cluster of up to 16 CTAs per W tile.  Each split keeps
+  // >= 3 chunks (fewer makes the cluster epilogue dominate), the ring
+  // (>= 3 stages) must hold the [mpad][128] fp32 accumulator copy, and the
+  // grid must fit one wave: with two CTAs per SM, 90% of the CTA slots
+  // (measured on B200: the occupancy API's cluster count is conservative
+  // there); with one CTA per SM, the occupancy API's count of co-resident
+  // clusters (a cluster too many runs as a second wave at twice the time).
+  const int slots = sm_count() * per_sm;
+  int smax = (per_sm == 2 ? slots * 9 / 10 : slots) / (pl.tiles > 0 ? pl.tiles : 1);
   if (smax > kMaxSplits) smax = kMaxSplits;
+  if (per_sm == 2 && smax > pl.chunks / 3) smax = pl.chunks / 3;
   if (smax > pl.chunks / 2) smax = pl.chunks / 2;
   size_smem(pl, M, 1, stages_for(1));
   pl.splits = 1;
@@ -414,7 +556,7 @@ LinearPlan plan_linear(int32_t M, int32_t N, int32_t K) {
     if (st < 3 || st * stage_bytes < pl.mpad * kTileN * 4) continue;
     LinearPlan trial = pl;
     size_smem(trial, M, cand, st);
-    if (max_clusters(cand, trial.smem_bytes, pl.tiles) >= pl.tiles) {
+    if (per_sm == 2 || max_clusters(cand, trial.smem_bytes, pl.tiles) >= pl.tiles) {
       pl = trial;
       pl.splits = cand;
       break;
@@ -443,6 +585,8 @@ cudaError_t launch_linear(const LinearLaunch& a, const LinearPlan& pl, const CUt
   p.tmem_cols = pl.tmem_cols;
   p.recv_off = pl.recv_off;
   p.w_tiled = a.w_tiled;
+  p.swiglu = a.swiglu;
+  p.rope = a.rope;
   // kind::f16 instruction descriptor: fp32 D, bf16 A and B, both K-major,
   // N = mpad (>> 3 at bit 17), M = 128 (>> 4 at bit 24)
   p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((static_cast<uint32_t>(pl.mpad) >> 3) << 17) |
@@ -470,6 +614,15 @@ cudaError_t launch_linear(const LinearLaunch& a, const LinearPlan& pl, const CUt
   cfg.attrs = attrs;
   cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, linear_tc_kernel, p, wmap, xmap);
+}
+
+cudaError_t launch_pair_gate_up(const void* w, int64_t ldw, int32_t inter, int32_t k, void* out,
+                                cudaStream_t stream) {
+  const int64_t total16 = static_cast<int64_t>(2) * inter * k / 8;
+  return launch_k(pair_gate_up_kernel, dim3(static_cast<unsigned>((total16 + 255) / 256)),
+                  dim3(256), 0, stream, static_cast<const __nv_bfloat16*>(w), ldw,
+                  static_cast<int>(inter), static_cast<int>(k), total16,
+                  static_cast<__nv_bfloat16*>(out));
 }
 
 cudaError_t launch_pack_weight(const void* w, int64_t ldw, int32_t n, int32_t k, void* out,

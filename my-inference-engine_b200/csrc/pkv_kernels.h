@@ -5,6 +5,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <cuda_bf16.h>
 
 namespace pkv {
 
@@ -122,13 +123,32 @@ struct LinearPlan {
   int32_t recv_off;  // byte offset of the split-k receive buffer
   uint32_t tmem_cols;
 };
+// Epilogue of the q/k/v GEMM that does pkv_append_rope's work (linear_tc.cu).
+struct RopeAppend {
+  __nv_bfloat16* q_out;  // nullptr: not this mode
+  int64_t qo_sb, qo_sh, qo_st;
+  __nv_bfloat16* k_pool;
+  __nv_bfloat16* v_pool;
+  int32_t num_blocks;
+  const __nv_bfloat16* cos;
+  const __nv_bfloat16* sin;
+  int64_t rope_rows;
+  const int32_t* tables;
+  int64_t pitch;
+  const int32_t* rows;
+  const int32_t* starts;
+  const int32_t* q_lens;
+  int32_t T, hq, hkv;
+};
 struct LinearLaunch {
   int32_t M, N;
   void* y;  // bf16 [M][ldy]
   int64_t ldy;
   const void* bias;  // nullable
   int32_t w_tiled;   // wmap is the 3-D map of a PKV_W_TILED weight
+  int32_t swiglu;    // W is PKV_W_GATE_UP_PAIRED: y = SwiGLU [M][N/2]
   int32_t* err;
+  RopeAppend rope;   // rope.q_out set: RoPE + K/V append epilogue, y unused
 };
 // Needs a current CUDA device (the split count comes from the occupancy API).
 LinearPlan plan_linear(int32_t M, int32_t N, int32_t K);
@@ -138,6 +158,8 @@ cudaError_t launch_linear(const LinearLaunch& a, const LinearPlan& pl, const CUt
                           const CUtensorMap& xmap, cudaStream_t stream);
 cudaError_t launch_pack_weight(const void* w, int64_t ldw, int32_t n, int32_t k, void* out,
                                cudaStream_t stream);
+cudaError_t launch_pair_gate_up(const void* w, int64_t ldw, int32_t inter, int32_t k, void* out,
+                                cudaStream_t stream);
 cudaError_t launch_silu_mul(const void* gu, int64_t gu_stride, void* out, int64_t o_stride,
                             int32_t rows, int32_t inter, cudaStream_t stream);
 

@@ -281,8 +281,8 @@ class Qwen2ForCausalLM(torch.nn.Module):
             else:
                 h = pagedkv.add_rmsnorm(F.linear(o_in, at.o_proj.weight), xs, post_w, RMS_NORM_EPS,
                                         resid_out=xs)
-            if use["gate_up"]:
-                act = pagedkv.linear_silu_mul(h, mlp.gate_up_weight, err=err)
+            if use["gate_up"]:  # SwiGLU in the GEMM's epilogue (paired gate/up rows)
+                act = pagedkv.linear_silu_mul(h, self._paired_gate_up(mlp), err=err)
             else:
                 act = pagedkv.silu_mul(F.linear(h, mlp.gate_up_weight))
             if li < last:
@@ -299,6 +299,24 @@ class Qwen2ForCausalLM(torch.nn.Module):
             else:
                 m = F.linear(act, mlp.down_proj.weight)
         return m
+
+    @staticmethod
+    def _paired_gate_up(mlp):
+        """The merged gate/up weight in the PKV_W_GATE_UP_PAIRED layout, made
+        on first use on the weight's device and kept (55 MB per layer; not part
+        of the state dict).  refresh_packed_weights() drops it after the
+        weights change."""
+        pw = getattr(mlp, "_gate_up_paired", None)
+        if pw is None:
+            import pagedkv
+
+            pw = pagedkv.PairedGateUp(mlp.gate_up_weight)
+            mlp._gate_up_paired = pw
+        return pw
+
+    def refresh_packed_weights(self):
+        for layer in self.layers:
+            layer.mlp.__dict__.pop("_gate_up_paired", None)
 
     @property
     def fused(self):

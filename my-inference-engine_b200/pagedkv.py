@@ -26,7 +26,7 @@ PKV_DEVERR_TIMEOUT = 4
 HEAD_DIM = 128
 BLOCK_TOKENS = 16
 LINEAR_MAX_ROWS = 256  # PKV_LINEAR_MAX_ROWS
-W_ROWMAJOR, W_TILED = 0, 1  # PKV_W_ROWMAJOR, PKV_W_TILED
+W_ROWMAJOR, W_TILED, W_GATE_UP_PAIRED = 0, 1, 2  # PKV_W_* layouts
 
 _c_i32p = ctypes.POINTER(ctypes.c_int32)
 _vp = ctypes.c_void_p
@@ -57,6 +57,7 @@ _SIGNATURES = {
         [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
          ctypes.c_float, _vp, _i64, _i64, _vp, _vp], ctypes.c_int),
     "pkv_linear_workspace_size": ([_i32, _i32, _i32], ctypes.c_size_t),
+    "pkv_linear_pair_gate_up": ([_vp, _i64, _i32, _i32, _vp, _vp], ctypes.c_int),
     "pkv_linear_pack_weight": ([_vp, _i64, _i32, _i32, _vp, _vp], ctypes.c_int),
     "pkv_linear": (
         [_vp, _i64, _vp, _i64, _i32, _vp, _i32, _i32, _i32, _vp, _i64, _vp, ctypes.c_size_t, _vp,
@@ -279,10 +280,27 @@ class TiledWeight:
         _check(st, "pkv_linear_pack_weight")
 
 
+class PairedGateUp:
+    """A merged gate/up weight [2*inter, k] reordered into the
+    PKV_W_GATE_UP_PAIRED layout (each 128-row tile: 64 gate rows, then their
+    64 up rows), for linear_silu_mul with SwiGLU in the GEMM's epilogue."""
+
+    def __init__(self, w_gate_up: torch.Tensor):
+        n, k = w_gate_up.shape
+        self.shape = torch.Size((n, k))
+        self.data = torch.empty(n, k, dtype=w_gate_up.dtype, device=w_gate_up.device)
+        st = lib().pkv_linear_pair_gate_up(_ptr(w_gate_up), w_gate_up.stride(0), n // 2, k,
+                                           _ptr(self.data), _stream(w_gate_up.device))
+        _check(st, "pkv_linear_pair_gate_up")
+
+
 def _w_args(w) -> tuple[int, int, int]:
-    """(pointer, ldw, layout) of a plain row-major weight or a TiledWeight."""
+    """(pointer, ldw, layout) of a plain row-major weight, a TiledWeight or a
+    PairedGateUp."""
     if isinstance(w, TiledWeight):
         return w.data.data_ptr(), w.shape[1], W_TILED
+    if isinstance(w, PairedGateUp):
+        return w.data.data_ptr(), w.shape[1], W_GATE_UP_PAIRED
     return w.data_ptr(), w.stride(0), W_ROWMAJOR
 
 
@@ -328,11 +346,13 @@ def linear_silu_mul(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor 
     inter = w_gate_up.shape[0] // 2
     if out is None:
         out = torch.empty(rows, inter, dtype=x.dtype, device=x.device)
-    ws = linear_workspace(rows, 2 * inter, k, x.device)
     wp, ldw, lay = _w_args(w_gate_up)
+    # the paired layout finishes SwiGLU in the GEMM: no intermediate
+    ws = linear_workspace(rows, 2 * inter, k, x.device) if lay != W_GATE_UP_PAIRED else None
     st = lib().pkv_linear_silu_mul(_ptr(x), x.stride(0), wp, ldw, lay, rows, inter, k,
                                    _ptr(out), out.stride(0), _ptr(ws),
-                                   ws.numel(), _ptr(err), _stream(x.device))
+                                   ws.numel() if ws is not None else 0, _ptr(err),
+                                   _stream(x.device))
     _check(st, "pkv_linear_silu_mul")
     return out
 

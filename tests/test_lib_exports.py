@@ -99,3 +99,7 @@ def test_linear_workspace_plan_and_validation_without_a_gpu():
     assert st == 1  # unknown weight layout
     st = L.pkv_linear_pack_weight(16, 1536, 2000, 1536, 16, None)
     assert st == 2  # n not a multiple of 128
+    st = L.pkv_linear_pair_gate_up(16, 1536, 100, 1536, 16, None)
+    assert st == 2  # inter not a multiple of 64
+    st = L.pkv_linear(16, 1536, 16, 1536, 2, None, 16, 17920, 1536, 16, 17920, None, 0, None, None)
+    assert st == 1  # the paired gate/up layout is only for pkv_linear_silu_mul

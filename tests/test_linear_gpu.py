@@ -121,8 +121,33 @@ def test_linear_silu_mul_equals_two_step(cuda, rows):
     assert float((got.float() - ref.float()).abs().max()) < 2e-2
 
 
+@pytest.mark.parametrize("rows", [1, 7, 16, 33, 64, 128, 256])
+def test_paired_gate_up_swiglu_epilogue_equals_two_step(cuda, rows):
+    """PKV_W_GATE_UP_PAIRED: SwiGLU finished in the GEMM's epilogue gives the
+    bits of GEMM -> silu_mul on the original weight."""
+    import pagedkv
+
+    x, w, _ = _operands(rows, 17920, 1536, cuda, 40 + rows, bias=False)
+    wp = pagedkv.PairedGateUp(w)
+    gate = w[:8960].view(140, 64, 1536)
+    up = w[8960:].view(140, 64, 1536)
+    assert torch.equal(wp.data.view(140, 128, 1536), torch.cat([gate, up], dim=1))
+    want = pagedkv.silu_mul(pagedkv.linear(x, w))
+    out = torch.full((rows, 8960 + 64), 3.0, device=cuda, dtype=torch.bfloat16)
+    got = pagedkv.linear_silu_mul(x, wp, out=out[:, :8960])
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    assert bool((out[:, 8960:] == 3.0).all())
+    with pytest.raises(pagedkv.PagedKVError, match="silu_mul only"):
+        pagedkv.linear(x, wp)
+
+
+@pytest.mark.parametrize("q_layout", ["dense", "padded"])
 @pytest.mark.parametrize("B,T", [(1, 1), (16, 1), (128, 1), (256, 1), (1, 200), (3, 40)])
-def test_linear_rope_append_equals_two_step(cuda, B, T):
+def test_linear_rope_append_equals_two_step(cuda, B, T, q_layout):
+    """dense q_out: RoPE + append run in the GEMM's epilogue; padded q_out
+    rows (stride 130, not a multiple of 8): GEMM + append kernel.  Both must
+    give the two-step result bit for bit."""
     import model as M
     import pagedkv
 
@@ -139,7 +164,9 @@ def test_linear_rope_append_equals_two_step(cuda, B, T):
         for s, n in zip(seqs, lens):
             cache._lengths[s] = n  # a history of n tokens (contents irrelevant here)
         _, step, _ = cache.prepare(seqs, T)  # reserves blocks for n + T tokens
-        q_rot = torch.full((B, T, 12, 128), float("nan"), device=cuda, dtype=torch.bfloat16)
+        width = 128 if q_layout == "dense" else 130
+        q_rot = torch.full((B, T, 12, width), float("nan"), device=cuda,
+                           dtype=torch.bfloat16)[..., :128]
         if fused:
             pagedkv.linear_rope_append(x, w, b, cos, sin, q_rot.transpose(1, 2),
                                        cache.buf[0, 0], cache.buf[0, 1], cache.block_tables,
