@@ -538,7 +538,9 @@ LinearPlan plan_linear(int32_t M, int32_t N, int32_t K) {
     return st > kMaxStages ? kMaxStages : st;
   };
   // Split k over a cluster of up to 16 CTAs per W tile.  Each split keeps
-  // >= 3 chunks (fewer makes the cluster epilogue dominate), the ring
+  // >= 4 chunks at two CTAs per SM (fewer makes the cluster epilogue
+  // dominate; measured: K = 1536 at <= 16 rows is fastest with 6 splits and
+  // 2x slower with 8), the ring
   // (>= 3 stages) must hold the [mpad][128] fp32 accumulator copy, and the
   // grid must fit one wave: with two CTAs per SM, 90% of the CTA slots
   // (measured on B200: the occupancy API's cluster count is conservative
@@ -547,7 +549,7 @@ LinearPlan plan_linear(int32_t M, int32_t N, int32_t K) {
   const int slots = sm_count() * per_sm;
   int smax = (per_sm == 2 ? slots * 9 / 10 : slots) / (pl.tiles > 0 ? pl.tiles : 1);
   if (smax > kMaxSplits) smax = kMaxSplits;
-  if (per_sm == 2 && smax > pl.chunks / 3) smax = pl.chunks / 3;
+  if (per_sm == 2 && smax > pl.chunks / 4) smax = pl.chunks / 4;
   if (smax > pl.chunks / 2) smax = pl.chunks / 2;
   size_smem(pl, M, 1, stages_for(1));
   pl.splits = 1;

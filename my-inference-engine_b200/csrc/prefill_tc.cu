@@ -307,20 +307,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&s_free[sb]);
 
       const int key0 = j * kKeys;
-      float mx = -INFINITY;
+      // Row max of the raw scores (scale_log2 > 0 commutes with max), as 8
+      // independent partial maxima instead of one 128-long dependency chain.
+      float pm[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) pm[u] = -INFINITY;
       if (key0 + kKeys <= lim) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          s[i] *= p.scale_log2;
-          mx = fmaxf(mx, s[i]);
-        }
+        for (int i = 0; i < 128; ++i) pm[i & 7] = fmaxf(pm[i & 7], s[i]);
       } else {
 #pragma unroll
         for (int i = 0; i < 128; ++i) {
-          s[i] = (key0 + i < lim) ? s[i] * p.scale_log2 : -INFINITY;
-          mx = fmaxf(mx, s[i]);
+          if (key0 + i >= lim) s[i] = -INFINITY;
+          pm[i & 7] = fmaxf(pm[i & 7], s[i]);
         }
       }
+      const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                             fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) *
+                       p.scale_log2;
       // Lazy rescaling: keep the running max unless this tile raises it by
       // more than 2^8 (P <= 256 then, exact in fp32 and bf16-representable);
       // O is rescaled in TMEM only when some row of the warp moved its max.
@@ -328,12 +332,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (mx > m + kRescaleThreshold || m == -INFINITY) mn = mx;
       const float base = mn == -INFINITY ? 0.f : mn;
       const float alpha = (mn == m) ? 1.f : ex2(m - base);
-      float rs = 0.f;
+      // p = 2^(s*scale - base): scale and shift in one FMA; the row sum as 8
+      // partial sums
+      float ps[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) ps[u] = 0.f;
 #pragma unroll
       for (int i = 0; i < 128; ++i) {
-        s[i] = ex2(s[i] - base);
-        rs += s[i];
+        s[i] = ex2(fmaf(s[i], p.scale_log2, -base));
+        ps[i & 7] += s[i];
       }
+      const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       l = l * alpha + rs;
       m = mn;
       const bool rescale = __any_sync(0xffffffffu, alpha != 1.f);
