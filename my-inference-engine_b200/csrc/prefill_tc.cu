@@ -10,9 +10,11 @@
 //   grid  = (Hq, B, ceil(T/128)): one CTA per 128 query rows of one head,
 //           heaviest (last) q-tiles first
 //   block = 6 warps
-//     warp 0    TMA producer (one thread): Q tile once, then 128-key K/V
+//     warp 0    TMA producer (one thread): Q tile once, then 128-key K and V
 //               tiles (eight 16-token blocks each, through the block table)
-//               into a 2-deep ring; a tile's block ids are read one tile ahead
+//               into separate 2-deep rings, K one tile ahead of V: a K stage
+//               is refilled as soon as its Q.K^T retired, so the next K tile
+//               loads during the current softmax; block ids read one tile ahead
 //     warp 1    owns TMEM (512 columns: S0, S1, O) and issues tcgen05.mma:
 //               S[b] = Q.K^T (M=128, N=128, K=128 in 8 steps), then
 //               O += P.V (K = 16 keys per step, only the loaded blocks)
@@ -49,7 +51,7 @@ constexpr int kOffQ = 0;
 constexpr int kOffKV = kOffQ + kOperand;  // stage s: K at +s*64K, V at +32K
 constexpr int kOffP = kOffKV + kStages * 2 * kOperand;
 constexpr int kOffBar = kOffP + kOperand;
-constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 1 + 1 + 1;
+constexpr int kNumBars = 1 + 4 * kStages + 2 + 2 + 1 + 1 + 1;
 constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
 
 // instruction descriptors (kind::f16): fp32 accumulate, bf16 A/B, M=128, N=128
@@ -90,9 +92,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = kv_full + kStages;
-  uint64_t* s_full = kv_empty + kStages;
+  // K and V have separate rings: a K stage is free once Q.K^T retired, a V
+  // stage once P.V retired, so K(j+2) streams in during tile j's softmax
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + kStages;
+  uint64_t* v_full = k_empty + kStages;
+  uint64_t* v_empty = v_full + kStages;
+  uint64_t* s_full = v_empty + kStages;
   uint64_t* s_free = s_full + 2;
   uint64_t* p_full = s_free + 2;
   uint64_t* pv_done = p_full + 1;
@@ -148,8 +154,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&kv_full[s], 1);   // producer's arrive.expect_tx
-      mbar_init(&kv_empty[s], 1);  // tcgen05.commit after the tile's PV
+      mbar_init(&k_full[s], 1);   // producer's arrive.expect_tx
+      mbar_init(&k_empty[s], 1);  // tcgen05.commit after the tile's Q.K^T
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);  // tcgen05.commit after the tile's P.V
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);  // tcgen05.commit after Q.K^T
@@ -200,35 +208,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&kmap);
       prefetch_tmap(&vmap);
       const uint64_t keep = policy_evict_last();
-      int cur[kTileBlocks] = {}, nxt[kTileBlocks] = {};
-      fetch(0, nxt);
-      mbar_arrive_expect_tx(q_full, kOperand);
-      tma_load_4d(smem + kOffQ, &qmap, q_full, 0, q0, hq, b, keep);
-      tma_load_4d(smem + kOffQ + kRegion, &qmap, q_full, 64, q0, hq, b, keep);
-      for (int j = 0; j < ntiles; ++j) {
-#pragma unroll
-        for (int jb = 0; jb < kTileBlocks; ++jb) cur[jb] = nxt[jb];
-        if (j + 1 < ntiles) fetch(j + 1, nxt);
+      // K runs one tile ahead of V: issue K(j+1), then V(j)
+      auto issue = [&](int j, const int (&ids)[kTileBlocks], bool is_v) -> bool {
         const int st = j % kStages;
-        if (j >= kStages && !mbar_wait(&kv_empty[st], ((j / kStages) - 1) & 1, err)) break;
-        uint8_t* kt = smem + kOffKV + st * 2 * kOperand;
-        uint8_t* vt = kt + kOperand;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * kOperand);
+        uint64_t* full = is_v ? &v_full[st] : &k_full[st];
+        uint64_t* empty = is_v ? &v_empty[st] : &k_empty[st];
+        if (j >= kStages && !mbar_wait(empty, ((j / kStages) - 1) & 1, err)) return false;
+        uint8_t* dst = smem + kOffKV + st * 2 * kOperand + (is_v ? kOperand : 0);
+        const CUtensorMap* map = is_v ? &vmap : &kmap;
+        mbar_arrive_expect_tx(full, kOperand);
 #pragma unroll
         for (int jb = 0; jb < kTileBlocks; ++jb) {
           if constexpr (kPaged) {
-            const int slot = cur[jb] * kBlockTokens;
-            tma_load_3d(kt + jb * 2048, &kmap, &kv_full[st], 0, kvh, slot, keep);
-            tma_load_3d(kt + kRegion + jb * 2048, &kmap, &kv_full[st], 64, kvh, slot, keep);
-            tma_load_3d(vt + jb * 2048, &vmap, &kv_full[st], 0, kvh, slot, keep);
-            tma_load_3d(vt + kRegion + jb * 2048, &vmap, &kv_full[st], 64, kvh, slot, keep);
+            const int slot = ids[jb] * kBlockTokens;
+            tma_load_3d(dst + jb * 2048, map, full, 0, kvh, slot, keep);
+            tma_load_3d(dst + kRegion + jb * 2048, map, full, 64, kvh, slot, keep);
           } else {
             const int tok = (j * kTileBlocks + jb) * kBlockTokens;
-            tma_load_4d(kt + jb * 2048, &kmap, &kv_full[st], 0, tok, kvh, b, keep);
-            tma_load_4d(kt + kRegion + jb * 2048, &kmap, &kv_full[st], 64, tok, kvh, b, keep);
-            tma_load_4d(vt + jb * 2048, &vmap, &kv_full[st], 0, tok, kvh, b, keep);
-            tma_load_4d(vt + kRegion + jb * 2048, &vmap, &kv_full[st], 64, tok, kvh, b, keep);
+            tma_load_4d(dst + jb * 2048, map, full, 0, tok, kvh, b, keep);
+            tma_load_4d(dst + kRegion + jb * 2048, map, full, 64, tok, kvh, b, keep);
           }
+        }
+        return true;
+      };
+      int idk[kTileBlocks] = {}, idv[kTileBlocks] = {};
+      fetch(0, idk);
+      mbar_arrive_expect_tx(q_full, kOperand);
+      tma_load_4d(smem + kOffQ, &qmap, q_full, 0, q0, hq, b, keep);
+      tma_load_4d(smem + kOffQ + kRegion, &qmap, q_full, 64, q0, hq, b, keep);
+      if (issue(0, idk, false)) {
+        for (int j = 0; j < ntiles; ++j) {
+#pragma unroll
+          for (int jb = 0; jb < kTileBlocks; ++jb) idv[jb] = idk[jb];
+          if (j + 1 < ntiles) {
+            fetch(j + 1, idk);
+            if (!issue(j + 1, idk, false)) break;
+          }
+          if (!issue(j, idv, true)) break;
         }
       }
     }
@@ -238,8 +254,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool dead = !mbar_wait(q_full, 0, err);
       auto issue_pv = [&](int i) -> bool {
         if (!mbar_wait(p_full, i & 1, err)) return false;
-        tc_fence_after();
         const int st = i % kStages;
+        if (!mbar_wait(&v_full[st], (i / kStages) & 1, err)) return false;
+        tc_fence_after();
         const uint32_t sV = smem_u32(smem + kOffKV + st * 2 * kOperand + kOperand);
         const int nb = min(kTileBlocks, nblk - i * kTileBlocks);
         for (int kb = 0; kb < nb; ++kb) {
@@ -247,13 +264,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                (i > 0 || kb > 0) ? 1u : 0u);
         }
         umma_commit(pv_done);
-        umma_commit(&kv_empty[st]);
+        umma_commit(&v_empty[st]);
         return true;
       };
       for (int j = 0; j < ntiles && !dead; ++j) {
         const int st = j % kStages;
         const int sb = j & 1;
-        if (!mbar_wait(&kv_full[st], (j / kStages) & 1, err)) {
+        if (!mbar_wait(&k_full[st], (j / kStages) & 1, err)) {
           dead = true;
           break;
         }
@@ -268,6 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma(tmem + (sb ? kColS1 : kColS0), kmajor_desc(sQ, kk), kmajor_desc(sK, kk), kIdescQK,
                kk > 0 ? 1u : 0u);
         umma_commit(&s_full[sb]);
+        umma_commit(&k_empty[st]);
         if (j >= 1 && !issue_pv(j - 1)) {
           dead = true;
           break;
