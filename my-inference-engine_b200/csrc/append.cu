@@ -113,9 +113,127 @@ __global__ void __launch_bounds__(256) append_rope_kernel(const AppendLaunch a, 
   *reinterpret_cast<__nv_bfloat162*>(dst + 64 + d) = ohi;
 }
 
+// One warp per (row, step token): 16 lanes per head, two heads per pass;
+// lane l owns dims 4l..4l+3 and their rotation partners 64+4l..64+4l+3
+// (8-byte accesses).  The token's cos/sin and pool slot are looked up once
+// for all its heads.  Same arithmetic per element as append_rope_kernel.
+__global__ void __launch_bounds__(256) append_rope_vec_kernel(const AppendLaunch a,
+                                                              int32_t num_blocks) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t tok = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (tok >= static_cast<int64_t>(a.batch) * a.seq_len_q) return;
+  const int tt = static_cast<int>(tok % a.seq_len_q);
+  const int b = static_cast<int>(tok / a.seq_len_q);
+  const DevErr err{a.err};
+  const int start = a.starts[b];
+  if (start < 0) return;                      // inactive (padding) row
+  if (a.q_lens && tt >= a.q_lens[b]) return;  // right padding of a shorter row
+  const int pos = start + tt;
+  const bool rope = a.rope_cos != nullptr;
+  const int nq = a.q_out ? a.num_q_heads : 0;
+  const int per_tok = nq + 2 * a.num_kv_heads;
+  const int d = 4 * (lane & 15);
+
+  // pool slot of this token (k and v heads), checked once
+  int64_t slot = -1;
+  {
+    const int row = a.rows ? a.rows[b] : b;
+    const int64_t bi = pos >> 4;
+    if (pos < 0 || bi >= a.pitch) {
+      if (lane == 0) err.raise(PKV_DEVERR_POSITION);
+    } else {
+      const int blk = a.tables[static_cast<int64_t>(row) * a.pitch + bi];
+      if (blk < 0 || blk >= num_blocks) {
+        if (lane == 0) err.raise(PKV_DEVERR_BLOCK_ID);
+      } else {
+        slot = static_cast<int64_t>(blk) * kBlockTokens + (pos & 15);
+      }
+    }
+  }
+  // cos/sin of this position (dims d..d+3 and 64+d..64+d+3)
+  bool rope_ok = rope;
+  __nv_bfloat16 c[8], sn[8];
+  if (rope) {
+    if (pos < 0 || pos >= a.rope_rows) {
+      if (lane == 0) err.raise(PKV_DEVERR_POSITION);
+      rope_ok = false;
+    } else {
+      const __nv_bfloat16* cr = static_cast<const __nv_bfloat16*>(a.rope_cos) + static_cast<int64_t>(pos) * kHeadDim;
+      const __nv_bfloat16* sr = static_cast<const __nv_bfloat16*>(a.rope_sin) + static_cast<int64_t>(pos) * kHeadDim;
+      *reinterpret_cast<uint2*>(c) = *reinterpret_cast<const uint2*>(cr + d);
+      *reinterpret_cast<uint2*>(c + 4) = *reinterpret_cast<const uint2*>(cr + 64 + d);
+      *reinterpret_cast<uint2*>(sn) = *reinterpret_cast<const uint2*>(sr + d);
+      *reinterpret_cast<uint2*>(sn + 4) = *reinterpret_cast<const uint2*>(sr + 64 + d);
+    }
+  }
+
+  for (int which = lane >> 4; which < per_tok; which += 2) {
+    const __nv_bfloat16* src;
+    __nv_bfloat16* dst;
+    bool do_rope = rope;
+    if (which < nq) {
+      if (!rope_ok) continue;  // q needs its rotation
+      src = static_cast<const __nv_bfloat16*>(a.q) + b * a.q_sb + which * a.q_sh + tt * a.q_st;
+      dst = static_cast<__nv_bfloat16*>(a.q_out) + b * a.qo_sb + which * a.qo_sh + tt * a.qo_st;
+    } else {
+      const bool is_k = which < nq + a.num_kv_heads;
+      const int h = is_k ? which - nq : which - nq - a.num_kv_heads;
+      if (slot < 0) continue;
+      if (is_k) {
+        if (rope && !rope_ok) continue;
+        src = static_cast<const __nv_bfloat16*>(a.k) + b * a.k_sb + h * a.k_sh + tt * a.k_st;
+        dst = static_cast<__nv_bfloat16*>(a.k_pool) + (slot * a.num_kv_heads + h) * kHeadDim;
+      } else {
+        src = static_cast<const __nv_bfloat16*>(a.v) + b * a.v_sb + h * a.v_sh + tt * a.v_st;
+        dst = static_cast<__nv_bfloat16*>(a.v_pool) + (slot * a.num_kv_heads + h) * kHeadDim;
+        do_rope = false;
+      }
+    }
+    __nv_bfloat16 x[8];
+    *reinterpret_cast<uint2*>(x) = *reinterpret_cast<const uint2*>(src + d);
+    *reinterpret_cast<uint2*>(x + 4) = *reinterpret_cast<const uint2*>(src + 64 + d);
+    if (do_rope) {
+      __nv_bfloat16 o[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        // first half: x*cos + (-x2)*sin ; second half: x*cos + x1*sin
+        o[e] = rope1(x[e], c[e], __hneg(x[4 + e]), sn[e]);
+        o[4 + e] = rope1(x[4 + e], c[4 + e], x[e], sn[4 + e]);
+      }
+      *reinterpret_cast<uint2*>(dst + d) = *reinterpret_cast<const uint2*>(o);
+      *reinterpret_cast<uint2*>(dst + 64 + d) = *reinterpret_cast<const uint2*>(o + 4);
+    } else {
+      *reinterpret_cast<uint2*>(dst + d) = *reinterpret_cast<const uint2*>(x);
+      *reinterpret_cast<uint2*>(dst + 64 + d) = *reinterpret_cast<const uint2*>(x + 4);
+    }
+  }
+}
+
+bool vec8_ok(const AppendLaunch& a) {
+  auto al8 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; };
+  auto m4 = [](int64_t v) { return (v & 3) == 0; };
+  if (!al8(a.k) || !al8(a.v) || !m4(a.k_sb) || !m4(a.k_sh) || !m4(a.k_st) || !m4(a.v_sb) ||
+      !m4(a.v_sh) || !m4(a.v_st))
+    return false;
+  if (a.q_out && (!al8(a.q) || !al8(a.q_out) || !m4(a.q_sb) || !m4(a.q_sh) || !m4(a.q_st) ||
+                  !m4(a.qo_sb) || !m4(a.qo_sh) || !m4(a.qo_st)))
+    return false;
+  if (a.rope_cos && (!al8(a.rope_cos) || !al8(a.rope_sin))) return false;
+  return true;
+}
+
 }  // namespace
 
 cudaError_t launch_append(const AppendLaunch& a, cudaStream_t stream) {
+  const int32_t num_blocks_vec = static_cast<int32_t>(a.num_slots / kBlockTokens);
+  if (vec8_ok(a)) {
+    const int64_t warps = static_cast<int64_t>(a.batch) * a.seq_len_q;
+    if (warps == 0) return cudaSuccess;
+    return launch_k(append_rope_vec_kernel, dim3(static_cast<unsigned>((warps * 32 + 255) / 256)),
+                    dim3(256), 0, stream, a, num_blocks_vec);
+  }
   const int per_tok = (a.q_out ? a.num_q_heads : 0) + 2 * a.num_kv_heads;
   const int64_t warps = static_cast<int64_t>(a.batch) * a.seq_len_q * per_tok;
   if (warps == 0) return cudaSuccess;

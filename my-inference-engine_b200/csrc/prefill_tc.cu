@@ -27,6 +27,7 @@
 // the start address by 32 B), V MN-major (64-dim groups 16 KB apart, 8-key
 // groups 1024 B apart).  Every wait is bounded.
 #include <math.h>
+#include <stdlib.h>
 
 #include "pkv_device.cuh"
 #include "pkv_kernels.h"
@@ -442,20 +443,394 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------- head pairs
+// Two query heads of one KV group per CTA (GQA groups of even size): the K/V
+// tiles are loaded once for both, halving the L2 -> SM traffic per head-tile
+// that sets the tile period of the one-head kernel.  10 warps: warp 0 TMA,
+// warp 1 MMA, warps 2-5 softmax of head A, warps 6-9 softmax of head B (each
+// warpgroup covers the four TMEM lane quarters).  TMEM: S_A, S_B, O_A, O_B.
+// One shared P buffer is filled in a fixed order (P_A(j), then P_B(j) once
+// P.V_A(j) retired, then P_A(j+1) once P.V_B(j) retired), so shared memory
+// holds both Q tiles, two K and two V stages and P (224 KiB); Q.K^T of the
+// next tile is issued before the current tile's two P.V products, so the
+// exponentials of tile j+1 overlap the P.V chain of tile j.
+constexpr int kPairThreads = 320;
+constexpr uint32_t kPColSA = 0, kPColSB = 128, kPColOA = 256, kPColOB = 384;
+constexpr int kPOffQ = 0;                          // Q_A, Q_B: 2 x 32 KiB
+constexpr int kPOffK = kPOffQ + 2 * kOperand;      // K stage s at +s*32 KiB
+constexpr int kPOffV = kPOffK + kStages * kOperand;
+constexpr int kPOffP = kPOffV + kStages * kOperand;
+constexpr int kPOffBar = kPOffP + kOperand;
+constexpr int kPNumBars = 1 + 4 * kStages + 2 * 5 + 1;
+constexpr int kPSmemBytes = kPOffBar + kPNumBars * 8 + 16 + 1024;
+static_assert(kPSmemBytes <= 227 * 1024, "paired prefill shared memory exceeds the per-CTA limit");
+
 template <bool kPaged>
+__global__ void __launch_bounds__(kPairThreads, 1)
+    prefill_tc_pair_kernel(const TcParams p, const __grid_constant__ CUtensorMap qmap,
+                           const __grid_constant__ CUtensorMap kmap,
+                           const __grid_constant__ CUtensorMap vmap) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPOffBar);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + kStages;
+  uint64_t* v_full = k_empty + kStages;
+  uint64_t* v_empty = v_full + kStages;
+  uint64_t* s_full = v_empty + kStages;  // [head]
+  uint64_t* s_free = s_full + 2;         // [head], one arrival per softmax warp
+  uint64_t* p_full = s_free + 2;         // [head], one arrival per softmax warp
+  uint64_t* pv_done = p_full + 2;        // [head]
+  uint64_t* mma_done = pv_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kPNumBars);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int hq0 = 2 * blockIdx.x;  // heads hq0 (A) and hq0 + 1 (B), same KV head
+  const int b = blockIdx.y;
+  const int kvh = hq0 / p.group;
+  const int q0 = (gridDim.z - 1 - blockIdx.z) * kRows;  // heaviest q-tiles first
+  pdl_trigger();
+  pdl_wait();
+  const int T = p.q_lens ? min(max(p.q_lens[b], 0), p.T) : p.T;
+  const DevErr err{p.err};
+
+  int kv_len = max(p.kv_lens[b], 0);
+  const int32_t* trow = nullptr;
+  if constexpr (kPaged) {
+    const int row = p.rows ? p.rows[b] : b;
+    trow = p.tables + static_cast<int64_t>(row) * p.pitch;
+    if (kv_len > p.pitch * kBlockTokens) {
+      if (tid == 0 && q0 == 0 && hq0 == 0) err.raise(PKV_DEVERR_POSITION);
+      kv_len = static_cast<int>(p.pitch) * kBlockTokens;
+    }
+  }
+  const int offset = kv_len - T;
+  int kv_end = kv_len;
+  if (p.causal) kv_end = min(kv_len, min(q0 + kRows, T) + offset);
+  kv_end = max(kv_end, 0);
+  const int nblk = (kv_end + kBlockTokens - 1) / kBlockTokens;
+  const int ntiles = (nblk + kTileBlocks - 1) / kTileBlocks;
+
+  if (ntiles == 0) {
+    // no visible key for any row of this tile: 0/0 rows, as the reference
+    const uint32_t nan2 = 0x7fc07fc0u;
+    const uint4 nv = make_uint4(nan2, nan2, nan2, nan2);
+    for (int i = tid; i < 2 * kRows * 16; i += kPairThreads) {
+      const int hh = i / (kRows * 16), r = (i / 16) % kRows, c = i % 16;
+      const int qi = q0 + r;
+      if (qi < T)
+        *reinterpret_cast<uint4*>(p.out + b * p.o_sb + (hq0 + hh) * p.o_sh +
+                                  static_cast<int64_t>(qi) * p.o_st + c * 8) = nv;
+    }
+    return;
+  }
+
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&s_full[h], 1);
+      mbar_init(&s_free[h], 4);
+      mbar_init(&p_full[h], 4);
+      mbar_init(&pv_done[h], 1);
+    }
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sP = smem_u32(smem + kPOffP);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      auto fetch = [&](int j, int (&ids)[kTileBlocks]) {
+        if constexpr (kPaged) {
+#pragma unroll
+          for (int jb = 0; jb < kTileBlocks; ++jb) {
+            const int lb = j * kTileBlocks + jb;
+            ids[jb] = trow[lb < nblk ? lb : 0];  // past the end: finite, masked
+          }
+#pragma unroll
+          for (int jb = 0; jb < kTileBlocks; ++jb) {
+            if (ids[jb] < 0 || ids[jb] >= p.num_blocks) {
+              err.raise(PKV_DEVERR_BLOCK_ID);
+              ids[jb] = 0;
+            }
+          }
+        }
+      };
+      prefetch_tmap(&qmap);
+      prefetch_tmap(&kmap);
+      prefetch_tmap(&vmap);
+      const uint64_t keep = policy_evict_last();
+      auto issue = [&](int j, const int (&ids)[kTileBlocks], bool is_v) -> bool {
+        const int st = j % kStages;
+        uint64_t* full = is_v ? &v_full[st] : &k_full[st];
+        uint64_t* empty = is_v ? &v_empty[st] : &k_empty[st];
+        if (j >= kStages && !mbar_wait(empty, ((j / kStages) - 1) & 1, err)) return false;
+        uint8_t* dst = smem + (is_v ? kPOffV : kPOffK) + st * kOperand;
+        const CUtensorMap* map = is_v ? &vmap : &kmap;
+        mbar_arrive_expect_tx(full, kOperand);
+#pragma unroll
+        for (int jb = 0; jb < kTileBlocks; ++jb) {
+          if constexpr (kPaged) {
+            const int slot = ids[jb] * kBlockTokens;
+            tma_load_3d(dst + jb * 2048, map, full, 0, kvh, slot, keep);
+            tma_load_3d(dst + kRegion + jb * 2048, map, full, 64, kvh, slot, keep);
+          } else {
+            const int tok = (j * kTileBlocks + jb) * kBlockTokens;
+            tma_load_4d(dst + jb * 2048, map, full, 0, tok, kvh, b, keep);
+            tma_load_4d(dst + kRegion + jb * 2048, map, full, 64, tok, kvh, b, keep);
+          }
+        }
+        return true;
+      };
+      int idk[kTileBlocks] = {}, idv[kTileBlocks] = {};
+      fetch(0, idk);
+      mbar_arrive_expect_tx(q_full, 2 * kOperand);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint8_t* qd = smem + kPOffQ + h * kOperand;
+        tma_load_4d(qd, &qmap, q_full, 0, q0, hq0 + h, b, keep);
+        tma_load_4d(qd + kRegion, &qmap, q_full, 64, q0, hq0 + h, b, keep);
+      }
+      if (issue(0, idk, false)) {
+        for (int j = 0; j < ntiles; ++j) {
+#pragma unroll
+          for (int jb = 0; jb < kTileBlocks; ++jb) idv[jb] = idk[jb];
+          if (j + 1 < ntiles) {
+            fetch(j + 1, idk);
+            if (!issue(j + 1, idk, false)) break;
+          }
+          if (!issue(j, idv, true)) break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool dead = !mbar_wait(q_full, 0, err);
+      const uint32_t sQA = smem_u32(smem + kPOffQ), sQB = sQA + kOperand;
+      auto issue_qk = [&](int j) -> bool {
+        const int st = j % kStages;
+        if (!mbar_wait(&k_full[st], (j / kStages) & 1, err)) return false;
+        const uint32_t sK = smem_u32(smem + kPOffK + st * kOperand);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          // S_h is free once softmax h read tile j-1's scores
+          if (j >= 1 && !mbar_wait(&s_free[h], (j - 1) & 1, err)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma(tmem + (h ? kPColSB : kPColSA), kmajor_desc(h ? sQB : sQA, kk),
+                 kmajor_desc(sK, kk), kIdescQK, kk > 0 ? 1u : 0u);
+          umma_commit(&s_full[h]);
+        }
+        umma_commit(&k_empty[st]);
+        return true;
+      };
+      auto issue_pv = [&](int j, int h) -> bool {
+        if (!mbar_wait(&p_full[h], j & 1, err)) return false;
+        const int st = j % kStages;
+        if (h == 0 && !mbar_wait(&v_full[st], (j / kStages) & 1, err)) return false;
+        tc_fence_after();
+        const uint32_t sV = smem_u32(smem + kPOffV + st * kOperand);
+        const int nb = min(kTileBlocks, nblk - j * kTileBlocks);
+        for (int kb = 0; kb < nb; ++kb)
+          umma(tmem + (h ? kPColOB : kPColOA), kmajor_desc(sP, kb),
+               sdesc(sV + kb * 2048, kRegion, 1024), kIdescPV, (j > 0 || kb > 0) ? 1u : 0u);
+        umma_commit(&pv_done[h]);
+        if (h == 1) umma_commit(&v_empty[st]);
+        return true;
+      };
+      if (!dead) dead = !issue_qk(0);
+      for (int j = 0; j < ntiles && !dead; ++j) {
+        if (j + 1 < ntiles && !issue_qk(j + 1)) {
+          dead = true;
+          break;
+        }
+        if (!issue_pv(j, 0) || !issue_pv(j, 1)) {
+          dead = true;
+          break;
+        }
+      }
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, err);  // every MMA retired before TMEM is freed
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int h = warp >= 6 ? 1 : 0;  // warps 2-5: head A, 6-9: head B
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // query row within the tile == TMEM lane
+    const int qi = q0 + r;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t colS = h ? kPColSB : kPColSA, colO = h ? kPColOB : kPColOA;
+    const int lim = p.causal ? min(kv_len, qi + offset + 1) : kv_len;  // keys < lim visible
+    float m = -INFINITY, l = 0.f;
+    bool dead = false;
+    for (int j = 0; j < ntiles && !dead; ++j) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[h], j & 1, err))) {
+        dead = true;
+        break;
+      }
+      tc_fence_after();
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(lane_addr + colS + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = v[i];
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[h]);
+
+      const int key0 = j * kKeys;
+      float pm[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) pm[u] = -INFINITY;
+      if (key0 + kKeys <= lim) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) pm[i & 7] = fmaxf(pm[i & 7], s[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) {
+          if (key0 + i >= lim) s[i] = -INFINITY;
+          pm[i & 7] = fmaxf(pm[i & 7], s[i]);
+        }
+      }
+      const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                             fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) *
+                       p.scale_log2;
+      float mn = m;
+      if (mx > m + kRescaleThreshold || m == -INFINITY) mn = mx;
+      const float base = mn == -INFINITY ? 0.f : mn;
+      const float alpha = (mn == m) ? 1.f : ex2(m - base);
+      float ps[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) ps[u] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        s[i] = ex2(fmaf(s[i], p.scale_log2, -base));
+        ps[i & 7] += s[i];
+      }
+      const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      l = l * alpha + rs;
+      m = mn;
+      const bool rescale = __any_sync(0xffffffffu, alpha != 1.f);
+      // The shared P buffer is free (and O_h stable) once the product
+      // before this one in the order P_A(j), P_B(j), P_A(j+1) retired:
+      // head A waits P.V_B(j-1), head B waits P.V_A(j)
+      bool ok = true;
+      if (h == 0) {
+        if (j >= 1) ok = mbar_wait(&pv_done[1], (j - 1) & 1, err);
+      } else {
+        ok = mbar_wait(&pv_done[0], j & 1, err);
+      }
+      if (!__all_sync(0xffffffffu, ok)) {
+        dead = true;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int reg = 0; reg < 2; ++reg) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const int k = reg * 64 + c * 8;
+          uint4 pk;
+          pk.x = pack_bf16(s[k + 0], s[k + 1]);
+          pk.y = pack_bf16(s[k + 2], s[k + 3]);
+          pk.z = pack_bf16(s[k + 4], s[k + 5]);
+          pk.w = pack_bf16(s[k + 6], s[k + 7]);
+          *reinterpret_cast<uint4*>(smem + kPOffP + reg * kRegion + swz128(r, c)) = pk;
+        }
+      }
+      fence_async_smem();
+      if (j >= 1 && rescale) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld32(lane_addr + colO + c * 32, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= alpha;
+          tmem_st32(lane_addr + colO + c * 32, v);
+        }
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[h]);
+    }
+    // ------------------------------------------------------------ epilogue
+    bool have = !dead;
+    if (have) have = __all_sync(0xffffffffu, mbar_wait(&pv_done[h], (ntiles - 1) & 1, err));
+    __nv_bfloat16* orow = p.out + b * p.o_sb + (hq0 + h) * p.o_sh +
+                          static_cast<int64_t>(min(qi, T - 1)) * p.o_st;
+    if (have) {
+      tc_fence_after();
+      const float inv = 1.f / l;  // 0/0 -> NaN for a row with no visible key
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(lane_addr + colO + c * 32, v);
+        tmem_wait_ld();
+        if (qi < T) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            uint4 pk;
+            pk.x = pack_bf16(v[e + 0] * inv, v[e + 1] * inv);
+            pk.y = pack_bf16(v[e + 2] * inv, v[e + 3] * inv);
+            pk.z = pack_bf16(v[e + 4] * inv, v[e + 5] * inv);
+            pk.w = pack_bf16(v[e + 6] * inv, v[e + 7] * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + e) = pk;
+          }
+        }
+      }
+    } else if (qi < T) {
+      const uint32_t nan2 = 0x7fc07fc0u;  // a timed-out wait: NaN rows, not stale data
+      const uint4 nv = make_uint4(nan2, nan2, nan2, nan2);
+#pragma unroll
+      for (int e = 0; e < 128; e += 8) *reinterpret_cast<uint4*>(orow + e) = nv;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <bool kPaged, bool kPair>
 cudaError_t launch_tc_t(const TcParams& prm, const CUtensorMap& qmap, const KVSource& src,
                         dim3 grid, cudaStream_t stream) {
-  auto kern = prefill_tc_kernel<kPaged>;
+  auto kern = kPair ? prefill_tc_pair_kernel<kPaged> : prefill_tc_kernel<kPaged>;
+  const int smem = kPair ? kPSmemBytes : kSmemBytes;
   static int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     configured_device = dev;
   }
-  return launch_k(kern, grid, dim3(kThreads), static_cast<size_t>(kSmemBytes), stream, prm, qmap,
-                  src.kmap, src.vmap);
+  return launch_k(kern, grid, dim3(kPair ? kPairThreads : kThreads), static_cast<size_t>(smem),
+                  stream, prm, qmap, src.kmap, src.vmap);
 }
 
 }  // namespace
@@ -478,9 +853,30 @@ cudaError_t launch_prefill_tc(const PrefillLaunch& a, const CUtensorMap& qmap, c
   prm.causal = a.causal;
   prm.scale_log2 = a.sm_scale * 1.4426950408889634f;
   prm.err = a.err;
-  dim3 grid(a.num_q_heads, a.batch, (a.seq_len_q + kRows - 1) / kRows);
-  return src.paged ? launch_tc_t<true>(prm, qmap, src, grid, stream)
-                   : launch_tc_t<false>(prm, qmap, src, grid, stream);
+  const unsigned qtiles = (a.seq_len_q + kRows - 1) / kRows;
+  // Head pairs share their K/V tiles but halve the CTA count: use them when
+  // the paired grid still gives every SM two CTAs (measured: 8 rows x 1024
+  // or 2048 tokens and config 1 gain 10-15%, one 2048-token row loses 10%).
+  int sms = 148;
+  {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  const int64_t pair_ctas = static_cast<int64_t>(a.num_q_heads / 2) * a.batch * qtiles;
+  bool pair = pair_ctas >= 2 * sms;
+  if (const char* force = getenv("PKV_PREFILL_PAIR")) {  // "0" / "1": pin the kernel
+    if (force[0] == '0') pair = false;
+    if (force[0] == '1') pair = true;
+  }
+  if (prm.group % 2 == 0 && pair) {  // head pairs share their K/V tiles
+    dim3 grid(a.num_q_heads / 2, a.batch, qtiles);
+    return src.paged ? launch_tc_t<true, true>(prm, qmap, src, grid, stream)
+                     : launch_tc_t<false, true>(prm, qmap, src, grid, stream);
+  }
+  dim3 grid(a.num_q_heads, a.batch, qtiles);
+  return src.paged ? launch_tc_t<true, false>(prm, qmap, src, grid, stream)
+                   : launch_tc_t<false, false>(prm, qmap, src, grid, stream);
 }
 
 }  // namespace pkv

@@ -41,10 +41,13 @@ def test_append_rope_matches_reference_bits(cuda, golden):
         assert cache.block_tables[cache.table_row(s), :len(t)].tolist() == t
 
 
+@pytest.mark.parametrize("width", [128, 130])
 @pytest.mark.parametrize("T,B", [(1, 7), (16, 3), (37, 2), (300, 1)])
-def test_append_random_strided_inputs_vs_oracle(cuda, T, B):
+def test_append_random_strided_inputs_vs_oracle(cuda, T, B, width):
     """Non-contiguous q/k/v (the projections' transposed views) and a table
-    that crosses block boundaries mid-step; every pool byte is checked."""
+    that crosses block boundaries mid-step; every pool byte is checked.
+    width 128: 8-byte aligned rows (the one-warp-per-token kernel); width
+    130: head rows 260 bytes apart (the one-warp-per-head kernel)."""
     import model
 
     g = torch.Generator().manual_seed(100 + T)
@@ -61,13 +64,14 @@ def test_append_random_strided_inputs_vs_oracle(cuda, T, B):
         cache._lengths[s] = n
         ref.ensure_capacity(r, n)
         ref.lengths[r] = n
-    x = (torch.randn(B, T, 12 + 2 + 2, 128, generator=g) * 3).to(torch.bfloat16)
+    x_full = (torch.randn(B, T, 12 + 2 + 2, width, generator=g) * 3).to(torch.bfloat16)
+    x = x_full[..., :128]
     q, k, v = (t.transpose(1, 2) for t in x.split([12, 2, 2], dim=2))  # strided views
     st, step, _ = cache.prepare(seqs, T)
     rst, slot, _ = ref.prepare(rseqs, T)
     cos, sin = model.rope_table(cache.table_pitch * 16, torch.bfloat16, cuda)
     q_out = torch.empty(B, T, 12, 128, dtype=torch.bfloat16, device=cuda).transpose(1, 2)
-    xd = x.to(cuda)
+    xd = x_full.to(cuda)[..., :128]  # keeps the padded row stride on the device
     qd, kd, vd = (t.transpose(1, 2) for t in xd.split([12, 2, 2], dim=2))
     cache.append(5, step, qd, kd, vd, cos, sin, q_out)
     torch.cuda.synchronize()

@@ -188,3 +188,33 @@ def test_right_padded_rows_with_q_lens(cuda):
     changed = (cache.buf[0] != pool_before).any(-1).any(-1).any(0)  # [slots]
     expect = sum(qlen)
     assert int(changed.sum()) <= expect
+
+
+@pytest.mark.parametrize("hq,hkv,B,T,causal", [(12, 2, 3, 700, True), (32, 2, 2, 300, True),
+                                               (4, 2, 5, 129, True), (12, 2, 2, 256, False)])
+def test_head_pair_kernel_matches_one_head_kernel(cuda, monkeypatch, hq, hkv, B, T, causal):
+    """Even GQA groups may run two q-heads per CTA over shared K/V tiles; the
+    per-head arithmetic is the one-head kernel's, so both give the same bits
+    (and match the oracle).  PKV_PREFILL_PAIR pins the kernel."""
+    import pagedkv
+
+    g = torch.Generator().manual_seed(hq * 100 + T)
+    S = T + 37
+    q = torch.randn(B, hq, T, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, hkv, S, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, hkv, S, 128, generator=g).to(torch.bfloat16)
+    kv_lens = [S - (b * 13) % 29 for b in range(B)]
+    outs = []
+    for force in ("1", "0"):
+        monkeypatch.setenv("PKV_PREFILL_PAIR", force)
+        out = torch.full((B, hq, T, 128), 5.0, dtype=torch.bfloat16, device=cuda)
+        pagedkv.dense_attention(q.to(cuda), k.to(cuda), v.to(cuda),
+                                torch.tensor(kv_lens, dtype=torch.int32, device=cuda), out,
+                                causal, 1 / math.sqrt(128))
+        torch.cuda.synchronize()
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1])
+    for b in range(B):
+        want = attention_ref.attention_np(q[b:b + 1].float().numpy(), k[b:b + 1].float().numpy(),
+                                          v[b:b + 1].float().numpy(), [kv_lens[b]], causal)
+        assert max_err(outs[0][b:b + 1], want) < TOL, b
