@@ -22,6 +22,68 @@ constexpr int kNormThreads = 256;
 
 // One CTA per row: thread i owns elements [8i, 8i+8) (+ 2048 for dim > 2048).
 // h = a (+ resid) in bf16; resid_out = h; out = weight * bf16(h * rsqrt(mean(h^2) + eps))
+// One warp per row (dim % 256 == 0, dim <= 2048): lane l owns the 16-byte
+// chunks l, l+32, ... of the row; the sum of squares is a shuffle tree, no
+// shared memory or block barrier, so every row of a prefill is in flight at
+// once.  Same arithmetic per element as add_rmsnorm_kernel.
+constexpr int kNormRowsPerCta = 8;
+template <int kChunks>
+__global__ void __launch_bounds__(32 * kNormRowsPerCta)
+    add_rmsnorm_warp_kernel(const __nv_bfloat16* __restrict__ a, int64_t a_stride,
+                            const __nv_bfloat16* resid, int64_t r_stride,
+                            __nv_bfloat16* resid_out, int64_t ro_stride,
+                            const __nv_bfloat16* __restrict__ weight,
+                            __nv_bfloat16* __restrict__ out, int64_t o_stride, int rows, int dim,
+                            float eps) {
+  pdl_trigger();
+  pdl_wait();
+  const int row = blockIdx.x * kNormRowsPerCta + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  uint4 av[kChunks], rv[kChunks];
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    av[c] = *reinterpret_cast<const uint4*>(a + row * a_stride + (c * 32 + lane) * 8);
+    if (resid) rv[c] = *reinterpret_cast<const uint4*>(resid + row * r_stride + (c * 32 + lane) * 8);
+  }
+  float h[kChunks][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const __nv_bfloat16* ap = reinterpret_cast<const __nv_bfloat16*>(&av[c]);
+    uint4 hv;
+    __nv_bfloat16* hp = reinterpret_cast<__nv_bfloat16*>(&hv);
+    if (resid) {
+      const __nv_bfloat16* rp = reinterpret_cast<const __nv_bfloat16*>(&rv[c]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) hp[e] = rn(__fadd_rn(bf(rp[e]), bf(ap[e])));
+    } else {
+      hv = av[c];
+    }
+    if (resid_out)
+      *reinterpret_cast<uint4*>(resid_out + row * ro_stride + (c * 32 + lane) * 8) = hv;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      h[c][e] = bf(hp[e]);
+      ss = __fadd_rn(ss, __fmul_rn(h[c][e], h[c][e]));
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float r = rsqrtf(__fadd_rn(ss * (1.0f / static_cast<float>(dim)), eps));
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    const uint4 wv = *reinterpret_cast<const uint4*>(weight + col);
+    const __nv_bfloat16* wp = reinterpret_cast<const __nv_bfloat16*>(&wv);
+    uint4 ov;
+    __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(&ov);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) op[e] = rn(__fmul_rn(bf(wp[e]), bf(rn(__fmul_rn(h[c][e], r)))));
+    *reinterpret_cast<uint4*>(out + row * o_stride + col) = ov;
+  }
+}
+
 __global__ void __launch_bounds__(kNormThreads)
     add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ a, int64_t a_stride,
                        const __nv_bfloat16* resid, int64_t r_stride, __nv_bfloat16* resid_out,
@@ -110,6 +172,27 @@ __global__ void __launch_bounds__(256)
 }  // namespace
 
 cudaError_t launch_add_rmsnorm(const NormLaunch& p, cudaStream_t stream) {
+  if (p.dim % 256 == 0 && p.dim <= 2048) {
+    const dim3 grid((p.rows + kNormRowsPerCta - 1) / kNormRowsPerCta), block(32 * kNormRowsPerCta);
+    auto args = [&](auto kern) {
+      return launch_k(kern, grid, block, 0, stream, static_cast<const __nv_bfloat16*>(p.a),
+                      p.a_stride, static_cast<const __nv_bfloat16*>(p.resid), p.r_stride,
+                      static_cast<__nv_bfloat16*>(p.resid_out), p.ro_stride,
+                      static_cast<const __nv_bfloat16*>(p.weight),
+                      static_cast<__nv_bfloat16*>(p.out), p.o_stride, static_cast<int>(p.rows),
+                      static_cast<int>(p.dim), p.eps);
+    };
+    switch (p.dim / 256) {
+      case 1: return args(add_rmsnorm_warp_kernel<1>);
+      case 2: return args(add_rmsnorm_warp_kernel<2>);
+      case 3: return args(add_rmsnorm_warp_kernel<3>);
+      case 4: return args(add_rmsnorm_warp_kernel<4>);
+      case 5: return args(add_rmsnorm_warp_kernel<5>);
+      case 6: return args(add_rmsnorm_warp_kernel<6>);
+      case 7: return args(add_rmsnorm_warp_kernel<7>);
+      default: return args(add_rmsnorm_warp_kernel<8>);
+    }
+  }
   return launch_k(add_rmsnorm_kernel, dim3(p.rows), dim3(kNormThreads), 0, stream,
                   static_cast<const __nv_bfloat16*>(p.a), p.a_stride,
                   static_cast<const __nv_bfloat16*>(p.resid), p.r_stride,
