@@ -158,13 +158,17 @@ __global__ void __launch_bounds__(256)
   const uint4 uv = *reinterpret_cast<const uint4*>(gu + row * gu_stride + inter + col);
   const __nv_bfloat16* gp = reinterpret_cast<const __nv_bfloat16*>(&gv);
   const __nv_bfloat16* up = reinterpret_cast<const __nv_bfloat16*>(&uv);
+  // F.silu in fp32, rounded to bf16, times up, rounded to bf16; the roundings
+  // go two values per cvt.rn.bf16x2 (the conversions share the MUFU/XU pipe
+  // with expf and the division, which bounds this kernel)
   uint4 ov;
-  __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(&ov);
+  __nv_bfloat162* op = reinterpret_cast<__nv_bfloat162*>(&ov);
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const float g = bf(gp[e]);
-    const __nv_bfloat16 s = rn(g / (1.0f + expf(-g)));  // F.silu in fp32, then bf16
-    op[e] = rn(__fmul_rn(bf(s), bf(up[e])));
+  for (int e = 0; e < 8; e += 2) {
+    const float g0 = bf(gp[e]), g1 = bf(gp[e + 1]);
+    const __nv_bfloat162 s = __floats2bfloat162_rn(g0 / (1.0f + expf(-g0)), g1 / (1.0f + expf(-g1)));
+    op[e / 2] = __floats2bfloat162_rn(__fmul_rn(__low2float(s), bf(up[e])),
+                                      __fmul_rn(__high2float(s), bf(up[e + 1])));
   }
   *reinterpret_cast<uint4*>(out + row * o_stride + col) = ov;
 }
