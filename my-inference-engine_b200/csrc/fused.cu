@@ -22,10 +22,11 @@ constexpr int kNormThreads = 256;
 
 // One CTA per row: thread i owns elements [8i, 8i+8) (+ 2048 for dim > 2048).
 // h = a (+ resid) in bf16; resid_out = h; out = weight * bf16(h * rsqrt(mean(h^2) + eps))
-// One warp per row (dim % 256 == 0, dim <= 2048): lane l owns the 16-byte
-// chunks l, l+32, ... of the row; the sum of squares is a shuffle tree, no
-// shared memory or block barrier, so every row of a prefill is in flight at
-// once.  Same arithmetic per element as add_rmsnorm_kernel.
+// One warp per row (dim % 256 == 0, dim <= 2048, >= 1024 rows): lane l owns
+// the 16-byte chunks l, l+32, ... of the row; the sum of squares is a
+// shuffle tree, no shared memory or block barrier, so every row of a
+// prefill is in flight at once.  Same arithmetic per element as
+// add_rmsnorm_kernel.
 constexpr int kNormRowsPerCta = 8;
 template <int kChunks>
 __global__ void __launch_bounds__(32 * kNormRowsPerCta)
@@ -176,7 +177,9 @@ __global__ void __launch_bounds__(256)
 }  // namespace
 
 cudaError_t launch_add_rmsnorm(const NormLaunch& p, cudaStream_t stream) {
-  if (p.dim % 256 == 0 && p.dim <= 2048) {
+  // warp per row for prefill-sized launches (all rows in flight at once);
+  // a decode step's few rows keep one CTA each, i.e. one SM each
+  if (p.dim % 256 == 0 && p.dim <= 2048 && p.rows >= 1024) {
     const dim3 grid((p.rows + kNormRowsPerCta - 1) / kNormRowsPerCta), block(32 * kNormRowsPerCta);
     auto args = [&](auto kern) {
       return launch_k(kern, grid, block, 0, stream, static_cast<const __nv_bfloat16*>(p.a),
