@@ -20,6 +20,7 @@ e2e    : the same bytes over the time of the public API driven from pinned
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import math
 import os
@@ -70,6 +71,9 @@ def parse():
     ap.add_argument("--engine4-prompt", type=int, nargs=2, default=[32, 4096])
     ap.add_argument("--engine4-reply", type=int, default=128)
     ap.add_argument("--engine4-pool-gb", type=float, default=120.0)
+    ap.add_argument("--engine4-mixed", type=int, default=None, metavar="MIN_TOKENS",
+                    help="also serve config 4 with chat.MIXED_PREFILL_MIN_TOKENS=MIN_TOKENS "
+                         "(prompts of at least MIN_TOKENS share the tick's decode forward)")
     ap.add_argument("--prefill-steps", type=int, default=20)
     # diagnostics (print their own JSON lines and exit; not the bench line)
     ap.add_argument("--linear-sweep", type=str, default=None, metavar="ROWS",
@@ -427,18 +431,30 @@ class _CountingModel:
         e0.record()
         out = self.model(input_ids, cache, seqs)
         e1.record()
-        self.calls.append((B, T, kv, e0, e1))
+        self.calls.append(("decode" if T == 1 else "prefill", B * T, kv, e0, e1))
+        return out
+
+    def forward_mixed(self, prefill_ids, prefill_seq, decode_ids, decode_seqs, cache):
+        T, B = prefill_ids.shape[1], len(decode_seqs)
+        kv = sum(cache.length(s) for s in decode_seqs) + B + cache.length(prefill_seq) + T
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        out = self.model.forward_mixed(prefill_ids, prefill_seq, decode_ids, decode_seqs, cache)
+        e1.record()
+        self.calls.append(("mixed", T + B, kv, e0, e1))
         return out
 
 
 def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_batch,
-               rank=0, world=1, seed=0):
+               rank=0, world=1, seed=0, mixed_min=None):
     """Serve `chats_total` chats through chat.py (uniform random token-id prompts
     in `prompt_range`, `reply`-token replies with EOS and stop sequences off as
     metrics/benchmark_concurrency.py:122,143 does, temperature-1 sampling, one
     prefill per tick).  Rank r serves chats i with i % world == r from one
     seeded prompt set, on its own model replica and `blocks`-block pool.
-    Returns this rank's tokens, wall time and a roofline."""
+    mixed_min: chat.MIXED_PREFILL_MIN_TOKENS for this run (None: the
+    reference's scheduling).  Returns this rank's tokens, wall time and a
+    roofline."""
     import chat
     import model as M
     from kv_cache import KVCache
@@ -449,6 +465,7 @@ def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_b
     cache = KVCache(blocks, 16, device, torch.bfloat16)
     chat.init(kv_cache=cache, start_worker=False)
     chat.STOP_SEQUENCES = []
+    chat.MIXED_PREFILL_MIN_TOKENS = mixed_min
     lo, hi = prompt_range
     runner = m.enable_decode_graphs(cache, max_batch=max_batch)
     for b in runner.buckets:  # capture outside the timed region
@@ -491,24 +508,34 @@ def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_b
     flops_peak = float(peaks.get("bf16_tflops", 1590.0)) * 1e12
     kv_tok = L * 2 * HKV * D * 2
     t_roof = 0.0
-    decode_steps = prefills = 0
-    gpu_decode = gpu_prefill = 0.0
-    for B, T, kv, e0, e1 in cm.calls:
+    decode_steps = prefills = mixed = 0
+    gpu_decode = gpu_prefill = gpu_mixed = 0.0
+    for kind, rows, kv, e0, e1 in cm.calls:
         ms = e0.elapsed_time(e1)
-        if T == 1:
+        if kind == "decode":
             decode_steps += 1
             gpu_decode += ms
             t_roof += (wbytes + kv * kv_tok) / bw
         else:
-            prefills += 1
-            gpu_prefill += ms
-            t_roof += max(2 * nparams * B * T / flops_peak, (wbytes + kv * kv_tok) / bw)
+            if kind == "mixed":
+                mixed += 1
+                gpu_mixed += ms
+            else:
+                prefills += 1
+                gpu_prefill += ms
+            t_roof += max(2 * nparams * rows / flops_peak, (wbytes + kv * kv_tok) / bw)
     chat._kv_cache = None
-    del runner, prunner, m, cache
+    chat.MIXED_PREFILL_MIN_TOKENS = None
+    m._graphs.clear()  # the graph runners and the model refer to each other
+    m._prefill_graphs.clear()
+    del runner, prunner, m, cache, cm
+    gc.collect()
     torch.cuda.empty_cache()
     return {"tok_s": round(toks / el, 1), "tokens": toks, "wall_s": round(el, 4),
             "decode_steps": decode_steps, "prefills": prefills,
+            **({"mixed_steps": mixed, "mixed_min_tokens": mixed_min} if mixed_min is not None else {}),
             "model_ms": {"decode_total": round(gpu_decode, 2), "prefill_total": round(gpu_prefill, 2),
+                         **({"mixed_total": round(gpu_mixed, 2)} if mixed_min is not None else {}),
                          "decode_per_step": round(gpu_decode / max(decode_steps, 1), 3),
                          "note": "CUDA events around each model call on the stream"},
             "roofline_tok_s": round(toks / t_roof, 1), "frac": round(t_roof / el, 4),
@@ -517,7 +544,9 @@ def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_b
             "config": f"{label}: {chats_total} chats ({len(mine)} on this GPU), prompts "
                       f"U[{lo},{hi}] random ids, {reply}-token replies, {blocks}-block pool, "
                       f"random-init bf16 Qwen2.5-1.5B (std 0.02), temperature-1 sampling, "
-                      f"one prefill per tick (chat.py), CUDA-graph decode and prefill"}
+                      f"one prefill per tick (chat.py), CUDA-graph decode and prefill"
+                      + (f"; prompts >= {mixed_min} tokens admitted while others decode share "
+                         f"their forward (eager mixed step)" if mixed_min is not None else "")}
 
 
 def engine_cpu_sample(seconds_budget=60.0):
@@ -850,7 +879,7 @@ def main():
     del w
     torch.cuda.empty_cache()
     prefill = None if args.no_prefill else prefill_run(args, dev, seed=args.seed)
-    engine = engine4 = None
+    engine = engine4 = engine4_mixed = None
     if not args.no_engine:
         # config 2 on every GPU (weak scaling: 16 chats per GPU)
         engine = engine_run(dev, label="config2", chats_total=args.engine_chats,
@@ -868,18 +897,23 @@ def main():
         per_gpu = -(-args.engine4_chats // world)
         need = per_gpu * -(-(args.engine4_prompt[1] + args.engine4_reply + 1) // 16) + 64
         blocks = int(min(need, args.engine4_pool_gb * 1e9 // block_bytes))
-        engine4 = engine_run(dev, label="config4", chats_total=args.engine4_chats,
-                             prompt_range=args.engine4_prompt, reply=args.engine4_reply,
-                             blocks=blocks, max_batch=256, rank=rank, world=world,
-                             seed=args.seed)
-        toks_all = cross_rank(engine4["tokens"], torch.distributed.ReduceOp.SUM if world > 1 else None,
-                              dev, world)
-        wall_max = cross_rank(engine4["wall_s"], torch.distributed.ReduceOp.MAX if world > 1 else None,
-                              dev, world)
-        engine4.update({"tok_s_all_gpus": round(toks_all / wall_max, 1),
-                        "tokens_all_gpus": int(toks_all), "wall_s_max_over_gpus": round(wall_max, 4),
-                        "n_gpus": world, "scaling": "strong (1024 chats split over the GPUs)"})
-        if rank == 0 and world == 1 and not args.no_engine_cpu:
+        runs = {}
+        for mixed_min in [None] + ([args.engine4_mixed] if args.engine4_mixed is not None else []):
+            r = engine_run(dev, label="config4", chats_total=args.engine4_chats,
+                           prompt_range=args.engine4_prompt, reply=args.engine4_reply,
+                           blocks=blocks, max_batch=256, rank=rank, world=world,
+                           seed=args.seed, mixed_min=mixed_min)
+            toks_all = cross_rank(r["tokens"], torch.distributed.ReduceOp.SUM if world > 1 else None,
+                                  dev, world)
+            wall_max = cross_rank(r["wall_s"], torch.distributed.ReduceOp.MAX if world > 1 else None,
+                                  dev, world)
+            r.update({"tok_s_all_gpus": round(toks_all / wall_max, 1),
+                      "tokens_all_gpus": int(toks_all), "wall_s_max_over_gpus": round(wall_max, 4),
+                      "n_gpus": world, "scaling": "strong (1024 chats split over the GPUs)"})
+            runs[mixed_min] = r
+        engine4 = runs[None]
+        engine4_mixed = runs.get(args.engine4_mixed) if args.engine4_mixed is not None else None
+        if engine is not None and rank == 0 and world == 1 and not args.no_engine_cpu:
             torch.set_num_threads(os.cpu_count() or 1)
             engine["cpu_baseline"] = engine_cpu_sample()
 
@@ -916,7 +950,8 @@ def main():
                 "data": "synthetic", "config": config, "roofline": roofline,
                 "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
                 "gpu_launches": args.steps * layers * 2,
-                "kv_bytes_per_step": step_bytes, "prefill": prefill, "engine": engine, "engine_config4": engine4}
+                "kv_bytes_per_step": step_bytes, "prefill": prefill, "engine": engine, "engine_config4": engine4,
+                **({"engine_config4_mixed": engine4_mixed} if engine4_mixed is not None else {})}
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()

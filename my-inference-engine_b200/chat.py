@@ -19,6 +19,14 @@ decode step can replay a captured CUDA graph (model.DecodeGraphs), and
 nothing is allocated or started at import -- `KV_CACHE` is created on first
 use and the worker thread on the first message (`init()` sets both up
 explicitly).
+
+One opt-in departure (off by default, so the decisions above stay the
+reference's): with MIXED_PREFILL_MIN_TOKENS set, a tick that admits a prompt
+of at least that many tokens while other jobs are decoding runs the prompt
+and their decode rows as ONE forward (model.forward_mixed: one pass over the
+weights, one sampling sync).  The admitted job then takes its first decode
+step in the next tick instead of this one; every other decision (admission,
+eviction, deferral, trimming, FIFO order) is unchanged.
 """
 from __future__ import annotations
 
@@ -39,6 +47,9 @@ TEMPERATURE = 1
 BLOCK_SIZE = 16
 KV_CACHE_TOKENS = 8 * 2048  # the reference's 448 MB budget (1024 blocks)
 MAX_SEQ_LEN = 2048
+
+# opt-in mixed prefill + decode ticks (see the module docstring); None = off
+MIXED_PREFILL_MIN_TOKENS = None
 
 DEVICE = torch.device("cuda")
 DTYPE = torch.bfloat16
@@ -61,9 +72,17 @@ def __getattr__(name):  # module attribute KV_CACHE, created on first access
 
 def init(kv_cache=None, start_worker=True):
     """Install a cache (default: the reference's 1024-block budget) and start
-    the worker thread now instead of on the first message."""
+    the worker thread now instead of on the first message.  Installing a new
+    cache forgets every resident chat's sequence (its K/V lived in the old
+    pool; its next message prefills the whole history again) and is refused
+    while a message is in flight."""
     global _kv_cache
-    if kv_cache is not None:
+    if kv_cache is not None and kv_cache is not _kv_cache:
+        if active or _deferred or _mixed:
+            raise RuntimeError("cannot replace the KV cache while messages are in flight")
+        for c in _resident:
+            c.seq = None
+        _resident.clear()
         _kv_cache = kv_cache
     _kv()
     if start_worker:
@@ -148,6 +167,7 @@ _resident = []
 _cache_lock = threading.Lock()
 _worker_thread = None
 _worker_lock = threading.Lock()
+_mixed = []  # at most one (job, prompt ids) whose prefill joins this tick's decode step
 
 
 def _reserve_len(job):
@@ -166,7 +186,7 @@ def _evict(chat):
 
 
 def _make_room(job):
-    busy = {j.chat for j in active} | {job.chat}
+    busy = {j.chat for j in active} | {j.chat for j, _ in _mixed} | {job.chat}
     with _cache_lock:
         while _blocks_needed(job) > _kv().free_block_count():
             idle = [c for c in _resident if c not in busy]
@@ -198,9 +218,17 @@ def _admit(job):
     prefill_ids = chat.ids[cache.length(chat.seq):]
     cache.ensure_capacity(chat.seq, reserve_len)
     _touch(chat)
+    if (MIXED_PREFILL_MIN_TOKENS is not None and active and not _mixed
+            and len(prefill_ids) >= MIXED_PREFILL_MIN_TOKENS and hasattr(model, "forward_mixed")):
+        _mixed.append((job, prefill_ids))  # runs inside this tick's decode step
+        return
+    _prefill(job, prefill_ids)
+
+
+def _prefill(job, prefill_ids):
     input_ids = torch.tensor([prefill_ids], device=DEVICE)
     with torch.no_grad():
-        logits = model(input_ids, cache, [chat.seq])
+        logits = job.model(input_ids, _kv(), [job.chat.seq])
     job.next_token = _sample(logits[:, -1])[0]
     active.append(job)
 
@@ -315,11 +343,28 @@ def _process(active):
 
         continuing.append(job)
 
+    mixed = _mixed.pop() if _mixed else None
+    if mixed is not None and not continuing:  # nothing left to share the forward with
+        _prefill(*mixed)
+        return
     if not continuing:
         return
 
     model = continuing[0].model
     seqs = [job.chat.seq for job in continuing]
+    if mixed is not None:
+        new_job, prefill_ids = mixed
+        with torch.no_grad():
+            logits = model.forward_mixed(
+                torch.tensor([prefill_ids], device=DEVICE), new_job.chat.seq,
+                torch.tensor([[job.next_token] for job in continuing], device=DEVICE), seqs, _kv())
+        tokens = _sample(logits)
+        new_job.next_token = tokens[0]
+        for job, token_id in zip(continuing, tokens[1:]):
+            job.next_token = token_id
+        active.append(new_job)
+        return
+
     # host tensor: the decode graph copies ids with the step's other inputs
     input_ids = torch.tensor([[job.next_token] for job in continuing])
     if not getattr(model, "_graphs", None):

@@ -235,7 +235,7 @@ class Qwen2ForCausalLM(torch.nn.Module):
         h = pagedkv.add_rmsnorm(m_last, x_last, self.norm.weight, RMS_NORM_EPS)
         return (h @ self.embed_tokens.weight.T)[:, None]
 
-    def _fused_layers(self, h, xs, B, T, cos, sin, is_causal, kv_lens, cache, step):
+    def _fused_layers(self, h, xs, B, T, cos, sin, is_causal, kv_lens, cache, step, segs=None):
         """The 28 layers on the merged weights, same op order and bf16 rounding
         points as QwenBlock.forward (model.py:131-138): q/k/v GEMM + bias ->
         RoPE + K/V append -> paged attention -> o_proj -> residual add + RMSNorm
@@ -245,34 +245,48 @@ class Qwen2ForCausalLM(torch.nn.Module):
         tensor-core GEMM fused with the op after it when the step has at most
         skinny_rows[op] rows (where it beats cuBLAS), else as cuBLAS + the
         separate fused kernel.  Returns the last layer's MLP output (before its
-        residual add)."""
+        residual add).
+
+        segs: row segments [(first row, B, T, PagedStep, causal)] that share
+        the GEMMs but append and attend separately (a mixed prefill + decode
+        step); default one segment (0, B, T, step, is_causal)."""
         import pagedkv
         from kernels.fa2 import flash_attention
 
-        N = B * T
+        N = xs.shape[0]
+        if segs is None:
+            segs = [(0, B, T, step, is_causal)]
         use = {op: self.skinny_linears and N <= lim for op, lim in self.skinny_rows.items()}
+        fused_qkv = use["qkv"] and len(segs) == 1
         err = cache.err_flag
         m = None
         last = len(self.layers) - 1
         for li, layer in enumerate(self.layers):
             at, mlp = layer.self_attn, layer.mlp
-            q_rot = torch.empty(B, T, NUM_HEADS, HEAD_DIM, device=xs.device, dtype=xs.dtype)
-            if use["qkv"]:
+            q_rot = torch.empty(N, NUM_HEADS, HEAD_DIM, device=xs.device, dtype=xs.dtype)
+            if fused_qkv:
                 pagedkv.linear_rope_append(
-                    h, at.qkv_weight, at.qkv_bias, cos, sin, q_rot.transpose(1, 2),
-                    cache.buf[li, 0], cache.buf[li, 1], cache.block_tables, step.rows,
-                    step.starts, NUM_KV_HEADS, err=err, q_lens=step.q_lens)
+                    h, at.qkv_weight, at.qkv_bias, cos, sin,
+                    q_rot.view(B, T, NUM_HEADS, HEAD_DIM).transpose(1, 2), cache.buf[li, 0],
+                    cache.buf[li, 1], cache.block_tables, step.rows, step.starts, NUM_KV_HEADS,
+                    err=err, q_lens=step.q_lens)
             else:
-                qkv = F.linear(h, at.qkv_weight, at.qkv_bias).view(
-                    B, T, NUM_HEADS + 2 * NUM_KV_HEADS, HEAD_DIM)
-                cache.append(li, step, qkv[:, :, :NUM_HEADS].transpose(1, 2),
-                             qkv[:, :, NUM_HEADS:NUM_HEADS + NUM_KV_HEADS].transpose(1, 2),
-                             qkv[:, :, NUM_HEADS + NUM_KV_HEADS:].transpose(1, 2), cos, sin,
-                             q_rot.transpose(1, 2))
-            k_blocks, v_blocks = cache.read(li, step)
-            out = torch.empty(B, T, NUM_HEADS, HEAD_DIM, device=xs.device, dtype=xs.dtype)
-            flash_attention(q_rot.transpose(1, 2), k_blocks, v_blocks, is_causal, kv_lens,
-                            out=out.transpose(1, 2))
+                qkv = (pagedkv.linear(h, at.qkv_weight, at.qkv_bias, err=err) if use["qkv"]
+                       else F.linear(h, at.qkv_weight, at.qkv_bias))
+                qkv = qkv.view(N, NUM_HEADS + 2 * NUM_KV_HEADS, HEAD_DIM)
+                for r0, Bs, Ts, st, _ in segs:
+                    part = qkv[r0:r0 + Bs * Ts].view(Bs, Ts, NUM_HEADS + 2 * NUM_KV_HEADS, HEAD_DIM)
+                    cache.append(li, st, part[:, :, :NUM_HEADS].transpose(1, 2),
+                                 part[:, :, NUM_HEADS:NUM_HEADS + NUM_KV_HEADS].transpose(1, 2),
+                                 part[:, :, NUM_HEADS + NUM_KV_HEADS:].transpose(1, 2), cos, sin,
+                                 q_rot[r0:r0 + Bs * Ts].view(Bs, Ts, NUM_HEADS, HEAD_DIM)
+                                 .transpose(1, 2))
+            out = torch.empty(N, NUM_HEADS, HEAD_DIM, device=xs.device, dtype=xs.dtype)
+            for r0, Bs, Ts, st, causal in segs:
+                k_blocks, v_blocks = cache.read(li, st)
+                qs = q_rot[r0:r0 + Bs * Ts].view(Bs, Ts, NUM_HEADS, HEAD_DIM).transpose(1, 2)
+                os_ = out[r0:r0 + Bs * Ts].view(Bs, Ts, NUM_HEADS, HEAD_DIM).transpose(1, 2)
+                flash_attention(qs, k_blocks, v_blocks, causal, st.kv_lens, out=os_)
             o_in = out.view(N, NUM_HEADS * HEAD_DIM)
             post_w = layer.post_attention_layernorm.weight
             if use["o"]:
@@ -299,6 +313,36 @@ class Qwen2ForCausalLM(torch.nn.Module):
             else:
                 m = F.linear(act, mlp.down_proj.weight)
         return m
+
+    def forward_mixed(self, prefill_ids, prefill_seq, decode_ids, decode_seqs, cache):
+        """One forward over a prompt and a batch of decode rows (a mixed
+        prefill + decode step): prefill_ids [1, T] for sequence prefill_seq,
+        decode_ids [B, 1] for decode_seqs.  The projections, norms and SwiGLU
+        run once over all T + B rows (one pass over the weights); RoPE + K/V
+        append and attention run per part (the causal prefill kernel for the
+        prompt, the decode kernel for the rest).  Returns logits
+        [1 + B, vocab]: the prompt's last token, then each decode row.  Eager
+        (not graph-captured): meant for prompts long enough that the GPU work
+        hides the launches.  Needs the fused weights (fuse_weights_)."""
+        import pagedkv
+
+        self.fuse_weights_()
+        dev = cache.device
+        T, B = prefill_ids.shape[1], len(decode_seqs)
+        _, step_p, _ = cache.prepare([prefill_seq], T)
+        _, step_d, _ = cache.prepare(decode_seqs, 1)
+        ids = torch.cat([prefill_ids.reshape(-1), decode_ids.reshape(-1)]).to(dev, non_blocking=True)
+        x = self.embed_tokens(ids)
+        cos, sin = self.rope_tables(cache.table_pitch * cache.block_size, x.dtype, dev)
+        xs = x.view(T + B, HIDDEN_SIZE)
+        h = pagedkv.add_rmsnorm(xs, None, self.layers[0].input_layernorm.weight, RMS_NORM_EPS)
+        segs = [(0, 1, T, step_p, True), (T, B, 1, step_d, False)]
+        m = self._fused_layers(h, xs, 0, 0, cos, sin, None, None, cache, None, segs=segs)
+        last = torch.cat([torch.tensor([T - 1]), torch.arange(T, T + B)]).to(dev, non_blocking=True)
+        hl = pagedkv.add_rmsnorm(m[last], xs[last], self.norm.weight, RMS_NORM_EPS)
+        cache.advance([prefill_seq], T)
+        cache.advance(decode_seqs, 1)
+        return hl @ self.embed_tokens.weight.T
 
     @staticmethod
     def _paired_gate_up(mlp):

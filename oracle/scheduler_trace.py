@@ -43,13 +43,33 @@ class FakeModel:
         for s in seqs:
             cache.ensure_capacity(s, cache.length(s) + T)
         cache.advance(seqs, T)
-        logits = torch.full((B, 1, VOCAB), -1e9)
+        return self._logits(cache, seqs)[:, None]
+
+    def forward_mixed(self, prefill_ids, prefill_seq, decode_ids, decode_seqs, cache):
+        """The product's optional mixed step: a prompt and decode rows in one
+        call; logits [1 + B, vocab] (the prompt's last token first)."""
+        T = prefill_ids.shape[1]
+        self.log.append({"mixed": True, "prefill_seq": prefill_seq, "T": T,
+                         "ids": prefill_ids.cpu().tolist(), "seqs": list(decode_seqs),
+                         "decode_ids": decode_ids.cpu().tolist()})
+        cache.ensure_capacity(prefill_seq, cache.length(prefill_seq) + T)
+        for s in decode_seqs:
+            cache.ensure_capacity(s, cache.length(s) + 1)
+        cache.advance([prefill_seq], T)
+        cache.advance(decode_seqs, 1)
+        return self._logits(cache, [prefill_seq] + list(decode_seqs))
+
+    @staticmethod
+    def _logits(cache, seqs):
+        """One-hot [len(seqs), VOCAB]: the next token is a function of the
+        sequence id and its length only."""
+        logits = torch.full((len(seqs), VOCAB), -1e9)
         for b, s in enumerate(seqs):
             n = cache.length(s)
             tok = 10 + (s * 13 + n * 5) % 50
             if n % 23 == 0:
                 tok = EOS
-            logits[b, 0, tok] = 0.0
+            logits[b, tok] = 0.0
         return logits
 
 
@@ -74,10 +94,10 @@ def run_trace(chat_mod, install_cache, num_blocks=14, max_reply=12, ticks=90):
     """Drive `chat_mod` for `ticks` worker ticks; returns the recorded trace."""
     calls = []
     model = FakeModel(calls)
-    cache = install_cache(num_blocks)
     chat_mod._job_queue = queue.Queue()  # a private queue: no worker thread can take jobs
     chat_mod.active.clear()
     chat_mod._deferred.clear()
+    cache = install_cache(num_blocks)
     chat_mod._resident.clear()
     chat_mod.MAX_REPLY_TOKENS = max_reply
     chat_mod.STOP_SEQUENCES = ["\nUser:", "\nUser"]

@@ -62,7 +62,10 @@ def test_decode_graph_matches_eager(cuda, small_model):
     assert int(view[:, :, unused].count_nonzero()) == 0
 
 
-def test_engine_serves_chats_with_eviction(cuda, small_model):
+@pytest.mark.parametrize("mixed", [None, 1])
+def test_engine_serves_chats_with_eviction(cuda, small_model, mixed):
+    """mixed=1: every prompt admitted while others decode joins their step
+    (chat.MIXED_PREFILL_MIN_TOKENS, model.forward_mixed)."""
     import chat
     from kv_cache import KVCache
 
@@ -82,9 +85,10 @@ def test_engine_serves_chats_with_eviction(cuda, small_model):
     cache = KVCache(40, 16, cuda, torch.bfloat16)
     chat.init(kv_cache=cache, start_worker=False)
     m.enable_decode_graphs(cache, max_batch=8)
-    saved = (chat.MAX_REPLY_TOKENS, chat.STOP_SEQUENCES)
+    saved = (chat.MAX_REPLY_TOKENS, chat.STOP_SEQUENCES, chat.MIXED_PREFILL_MIN_TOKENS)
     chat.MAX_REPLY_TOKENS = 24
     chat.STOP_SEQUENCES = []
+    chat.MIXED_PREFILL_MIN_TOKENS = mixed
     try:
         tok = Tok()
         chats = [chat.Chat(tok) for _ in range(6)]
@@ -104,7 +108,8 @@ def test_engine_serves_chats_with_eviction(cuda, small_model):
         for c in chats:
             assert len(c.messages) == 4
     finally:
-        chat.MAX_REPLY_TOKENS, chat.STOP_SEQUENCES = saved
+        chat.MAX_REPLY_TOKENS, chat.STOP_SEQUENCES, chat.MIXED_PREFILL_MIN_TOKENS = saved
+        chat._mixed.clear()
         chat._kv_cache = None
         m._graphs.clear()
 
@@ -151,6 +156,62 @@ def _prefill_graph_vs_eager(cuda, m):
         assert float((a - b).abs().max()) < 0.05
         assert torch.equal(a.argmax(-1), b.argmax(-1))
     assert float((ca.buf.float() - cb.buf.float()).abs().max()) < 0.05
+    used = {x for t in cb._block_tables.values() for x in t}
+    unused = [x for x in range(cb.num_blocks) if x not in used]
+    view = cb.buf.view(cb.buf.shape[0], 2, cb.num_blocks, 16, -1)
+    assert int(view[:, :, unused].count_nonzero()) == 0
+
+
+@pytest.mark.parametrize("gemm", ["cublas", "skinny"])
+def test_mixed_forward_matches_separate_calls(cuda, small_model, gemm):
+    """forward_mixed (a prompt + decode rows through shared GEMMs) gives the
+    logits and K/V of a prefill call followed by a decode call, up to GEMM
+    rounding (the shared GEMMs have more rows, so cuBLAS may tile them
+    differently), and advances every sequence the same way."""
+    from kv_cache import KVCache
+
+    m = small_model.fuse_weights_()
+    saved = m.skinny_linears, m.skinny_rows
+    m.skinny_linears = gemm == "skinny"
+    m.skinny_rows = {op: 256 for op in saved[1]}
+    g = torch.Generator().manual_seed(4)
+    hist = [torch.randint(0, 151936, (n,), generator=g).tolist() for n in (33, 7, 130)]
+    prompt = torch.randint(0, 151936, (1, 90), generator=g)
+    dec = torch.tensor([[5], [6], [7]])
+    res = []
+    try:
+        for mixed in (False, True):
+            c = KVCache(64, 16, cuda, torch.bfloat16)
+            seqs = [c.alloc() for _ in hist]
+            new = c.alloc()
+            with torch.no_grad():
+                for s, p in zip(seqs, hist):
+                    m(torch.tensor([p], device=cuda), c, [s])
+                if mixed:
+                    lg = m.forward_mixed(prompt.to(cuda), new, dec.to(cuda), seqs, c).float()
+                else:
+                    lp = m(prompt.to(cuda), c, [new])[:, -1]
+                    ld = m(dec.to(cuda), c, seqs)[:, -1]
+                    lg = torch.cat([lp, ld]).float()
+            torch.cuda.synchronize()
+            c.check_errors()
+            res.append((lg, c, [c.length(s) for s in seqs + [new]]))
+    finally:
+        m.skinny_linears, m.skinny_rows = saved
+    (la, ca, na), (lb, cb, nb) = res
+    assert na == nb == [34, 8, 131, 90]
+    assert lb.shape == (4, 151936)
+    # the decode rows' GEMMs run with 3 rows in one arm and 93 in the other,
+    # so their split-k summation order differs; the bf16 rounding differences
+    # compound over 28 layers (a few ulps of logits near 1)
+    d = (la - lb).abs()
+    assert float(d.max()) < 0.1 and float(d.mean()) < 0.01
+    assert torch.equal(la.argmax(-1), lb.argmax(-1))
+    live = (ca.buf != 0) | (cb.buf != 0)
+    d = (ca.buf.float() - cb.buf.float()).abs()
+    assert float(d.max()) < 0.1 and float(d[live].mean()) < 0.005
+    # same block ownership, and blocks no sequence owns stay zero
+    assert ca._block_tables == cb._block_tables
     used = {x for t in cb._block_tables.values() for x in t}
     unused = [x for x in range(cb.num_blocks) if x not in used]
     view = cb.buf.view(cb.buf.shape[0], 2, cb.num_blocks, 16, -1)
