@@ -152,7 +152,6 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   const int c0 = static_cast<int>(static_cast<int64_t>(split) * p.chunks / p.splits);
   const int nc = static_cast<int>(static_cast<int64_t>(split + 1) * p.chunks / p.splits) - c0;
   const DevErr err{p.err};
-  pdl_trigger();
 
   if (tid == 0) {
     for (int s = 0; s < p.stages; ++s) {
@@ -167,6 +166,10 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Dependents launch only once every CTA of this grid holds its TMEM, so a
+  // dependent that allocates before its griddepcontrol.wait cannot take
+  // columns this grid still needs.
+  pdl_trigger();
   const uint32_t tmem = *tmem_slot;
   // every CTA's recv_bar is initialised before any CTA arrives on it: the
   // matching wait sits before the epilogue's remote stores

@@ -20,14 +20,16 @@
 //               O += P.V (K = 16 keys per step, only the loaded blocks)
 //     warps 2-5 softmax: warp w owns TMEM lanes 32*(w%4).., i.e. one query
 //               row per thread, so row max / sum need no shuffles; writes P
-//               (bf16) to shared memory, rescales O in TMEM when a row's max
-//               moved, epilogue
-// Shared-memory operands use the canonical 128B-swizzled layouts: Q, K, P
+//               (bf16 pairs) over the first 64 columns of its S buffer, which
+//               P.V reads as its A operand from tensor memory; rescales O in
+//               TMEM when a row's max moved; epilogue
+// Shared-memory operands use the canonical 128B-swizzled layouts: Q, K
 // K-major (rows of 64 elements, 8-row groups 1024 B apart, k-steps advance
 // the start address by 32 B), V MN-major (64-dim groups 16 KB apart, 8-key
 // groups 1024 B apart).  Every wait is bounded.
 #include <math.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include "pkv_device.cuh"
 #include "pkv_kernels.h"
@@ -50,9 +52,8 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // smem map (offsets from the 1024-aligned base)
 constexpr int kOffQ = 0;
 constexpr int kOffKV = kOffQ + kOperand;  // stage s: K at +s*64K, V at +32K
-constexpr int kOffP = kOffKV + kStages * 2 * kOperand;
-constexpr int kOffBar = kOffP + kOperand;
-constexpr int kNumBars = 1 + 4 * kStages + 2 + 2 + 1 + 1 + 1;
+constexpr int kOffBar = kOffKV + kStages * 2 * kOperand;
+constexpr int kNumBars = 1 + 4 * kStages + 2 + 1 + 1 + 1;
 constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
 
 // instruction descriptors (kind::f16): fp32 accumulate, bf16 A/B, M=128, N=128
@@ -99,9 +100,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* k_empty = k_full + kStages;
   uint64_t* v_full = k_empty + kStages;
   uint64_t* v_empty = v_full + kStages;
+  // S[b] is rewritten by Q.K^T(j+2) only after P.V(j) (issue order), which
+  // waited for P(j): that also means the softmax has read S(j)
   uint64_t* s_full = v_empty + kStages;
-  uint64_t* s_free = s_full + 2;
-  uint64_t* p_full = s_free + 2;
+  uint64_t* p_full = s_full + 2;
   uint64_t* pv_done = p_full + 1;
   uint64_t* mma_done = pv_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
@@ -116,7 +118,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kvh = hq / p.group;
   const int q0 = (gridDim.z - 1 - blockIdx.z) * kRows;
   // this row's real query count (right padding beyond it is not written)
-  pdl_trigger();
   pdl_wait();
   const int T = p.q_lens ? min(max(p.q_lens[b], 0), p.T) : p.T;
   const DevErr err{p.err};
@@ -160,10 +161,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);  // tcgen05.commit after the tile's P.V
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&s_full[s], 1);  // tcgen05.commit after Q.K^T
-      mbar_init(&s_free[s], 4);  // one arrival per softmax warp
-    }
+    for (int s = 0; s < 2; ++s) mbar_init(&s_full[s], 1);  // tcgen05.commit after Q.K^T
     mbar_init(p_full, 4);
     mbar_init(pv_done, 1);
     mbar_init(mma_done, 1);
@@ -178,9 +176,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_trigger();  // dependents launch once this CTA holds its TMEM
   const uint32_t tmem = *tmem_slot;
   const uint32_t sQ = smem_u32(smem + kOffQ);
-  const uint32_t sP = smem_u32(smem + kOffP);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -259,10 +257,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&v_full[st], (i / kStages) & 1, err)) return false;
         tc_fence_after();
         const uint32_t sV = smem_u32(smem + kOffKV + st * 2 * kOperand + kOperand);
+        const uint32_t pS = tmem + ((i & 1) ? kColS1 : kColS0);  // P(i): 8 columns per 16 keys
         const int nb = min(kTileBlocks, nblk - i * kTileBlocks);
         for (int kb = 0; kb < nb; ++kb) {
-          umma(tmem + kColO, kmajor_desc(sP, kb), sdesc(sV + kb * 2048, kRegion, 1024), kIdescPV,
-               (i > 0 || kb > 0) ? 1u : 0u);
+          umma_ts(tmem + kColO, pS + kb * 8, sdesc(sV + kb * 2048, kRegion, 1024), kIdescPV,
+                  (i > 0 || kb > 0) ? 1u : 0u);
         }
         umma_commit(pv_done);
         umma_commit(&v_empty[st]);
@@ -272,10 +271,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = j % kStages;
         const int sb = j & 1;
         if (!mbar_wait(&k_full[st], (j / kStages) & 1, err)) {
-          dead = true;
-          break;
-        }
-        if (j >= 2 && !mbar_wait(&s_free[sb], ((j >> 1) - 1) & 1, err)) {
           dead = true;
           break;
         }
@@ -321,9 +316,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 32; ++i) s[c * 32 + i] = v[i];
       }
       tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[sb]);
 
       const int key0 = j * kKeys;
       // Row max of the raw scores (scale_log2 > 0 commutes with max), as 8
@@ -365,27 +357,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       l = l * alpha + rs;
       m = mn;
       const bool rescale = __any_sync(0xffffffffu, alpha != 1.f);
-      // P and O are free once the previous tile's PV product retired
-      if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, err))) {
-        dead = true;
-        break;
-      }
-      tc_fence_after();
-#pragma unroll
-      for (int reg = 0; reg < 2; ++reg) {
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const int k = reg * 64 + c * 8;
-          uint4 pk;
-          pk.x = pack_bf16(s[k + 0], s[k + 1]);
-          pk.y = pack_bf16(s[k + 2], s[k + 3]);
-          pk.z = pack_bf16(s[k + 4], s[k + 5]);
-          pk.w = pack_bf16(s[k + 6], s[k + 7]);
-          *reinterpret_cast<uint4*>(smem + kOffP + reg * kRegion + swz128(r, c)) = pk;
-        }
-      }
-      fence_async_smem();
+      // O is stable once the previous tile's P.V retired
       if (j >= 1 && rescale) {
+        if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, err))) {
+          dead = true;
+          break;
+        }
+        tc_fence_after();
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           float v[32];
@@ -395,16 +373,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i) v[i] *= alpha;
           tmem_st32(lane_addr + kColO + c * 32, v);
         }
-        tmem_wait_st();
       }
+      // P(j) as bf16 pairs over columns [0, 64) of S[sb] (already read)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1]);
+        tmem_st16u(lane_addr + (sb ? kColS1 : kColS0) + c * 16, pk);
+      }
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
     // ------------------------------------------------------------ epilogue
     // tcgen05.ld is warp-collective: every lane loads, only rows < T store
+    // every product retired: the softmax skips P.V waits on tiles without a
+    // rescale, so pv_done may be two phases behind here; mma_done is
+    // committed once, after the last P.V
     bool have = !dead;
-    if (have) have = __all_sync(0xffffffffu, mbar_wait(pv_done, (ntiles - 1) & 1, err));
+    if (have) have = __all_sync(0xffffffffu, mbar_wait(mma_done, 0, err));
     __nv_bfloat16* orow =
         p.out + b * p.o_sb + hq * p.o_sh + static_cast<int64_t>(min(qi, T - 1)) * p.o_st;
     if (have) {
@@ -492,7 +481,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   const int b = blockIdx.y;
   const int kvh = hq0 / p.group;
   const int q0 = (gridDim.z - 1 - blockIdx.z) * kRows;  // heaviest q-tiles first
-  pdl_trigger();
   pdl_wait();
   const int T = p.q_lens ? min(max(p.q_lens[b], 0), p.T) : p.T;
   const DevErr err{p.err};
@@ -549,6 +537,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_trigger();  // dependents launch once this CTA holds its TMEM
   const uint32_t tmem = *tmem_slot;
   const uint32_t sP = smem_u32(smem + kPOffP);
 
@@ -816,9 +805,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   }
 }
 
-template <bool kPaged, bool kPair>
+enum class TcKernel { kOneHead, kHeadPair };
+
+template <bool kPaged, TcKernel kKind>
 cudaError_t launch_tc_t(const TcParams& prm, const CUtensorMap& qmap, const KVSource& src,
                         dim3 grid, cudaStream_t stream) {
+  constexpr bool kPair = kKind == TcKernel::kHeadPair;
   auto kern = kPair ? prefill_tc_pair_kernel<kPaged> : prefill_tc_kernel<kPaged>;
   const int smem = kPair ? kPSmemBytes : kSmemBytes;
   static int configured_device = -1;
@@ -831,6 +823,13 @@ cudaError_t launch_tc_t(const TcParams& prm, const CUtensorMap& qmap, const KVSo
   }
   return launch_k(kern, grid, dim3(kPair ? kPairThreads : kThreads), static_cast<size_t>(smem),
                   stream, prm, qmap, src.kmap, src.vmap);
+}
+
+template <TcKernel kKind>
+cudaError_t launch_tc_kind(const TcParams& prm, const CUtensorMap& qmap, const KVSource& src,
+                           dim3 grid, cudaStream_t stream) {
+  return src.paged ? launch_tc_t<true, kKind>(prm, qmap, src, grid, stream)
+                   : launch_tc_t<false, kKind>(prm, qmap, src, grid, stream);
 }
 
 }  // namespace
@@ -854,9 +853,14 @@ cudaError_t launch_prefill_tc(const PrefillLaunch& a, const CUtensorMap& qmap, c
   prm.scale_log2 = a.sm_scale * 1.4426950408889634f;
   prm.err = a.err;
   const unsigned qtiles = (a.seq_len_q + kRows - 1) / kRows;
-  // Head pairs share their K/V tiles but halve the CTA count: use them when
-  // the paired grid still gives every SM two CTAs (measured: 8 rows x 1024
-  // or 2048 tokens and config 1 gain 10-15%, one 2048-token row loses 10%).
+  // Head pairs share their K/V tiles and overlap one head's exponentials
+  // with the other's products, but stage P through shared memory and keep
+  // one S buffer per head; the one-head kernel double-buffers S and keeps P
+  // in tensor memory.  Measured: pairs are 1-4% faster while every row is
+  // at most 1024 tokens (8 q-tiles) and the paired grid covers the SMs
+  // (config 1, 8 x 768, 8 x 1024); one head per CTA is 7-20% faster on
+  // longer rows (8 x 2048, 2 x 4096, 1 x 16384).  PKV_PREFILL_KERNEL=one|pair
+  // pins a kernel (pair needs an even GQA group).
   int sms = 148;
   {
     int dev = 0;
@@ -864,19 +868,17 @@ cudaError_t launch_prefill_tc(const PrefillLaunch& a, const CUtensorMap& qmap, c
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   }
   const int64_t pair_ctas = static_cast<int64_t>(a.num_q_heads / 2) * a.batch * qtiles;
-  bool pair = pair_ctas >= 2 * sms;
-  if (const char* force = getenv("PKV_PREFILL_PAIR")) {  // "0" / "1": pin the kernel
-    if (force[0] == '0') pair = false;
-    if (force[0] == '1') pair = true;
+  TcKernel kind = (prm.group % 2 == 0 && qtiles <= 8 && pair_ctas >= sms) ? TcKernel::kHeadPair
+                                                                          : TcKernel::kOneHead;
+  if (const char* force = getenv("PKV_PREFILL_KERNEL")) {
+    if (!strcmp(force, "one")) kind = TcKernel::kOneHead;
+    if (!strcmp(force, "pair") && prm.group % 2 == 0) kind = TcKernel::kHeadPair;
   }
-  if (prm.group % 2 == 0 && pair) {  // head pairs share their K/V tiles
-    dim3 grid(a.num_q_heads / 2, a.batch, qtiles);
-    return src.paged ? launch_tc_t<true, true>(prm, qmap, src, grid, stream)
-                     : launch_tc_t<false, true>(prm, qmap, src, grid, stream);
-  }
-  dim3 grid(a.num_q_heads, a.batch, qtiles);
-  return src.paged ? launch_tc_t<true, false>(prm, qmap, src, grid, stream)
-                   : launch_tc_t<false, false>(prm, qmap, src, grid, stream);
+  if (kind == TcKernel::kHeadPair)
+    return launch_tc_kind<TcKernel::kHeadPair>(prm, qmap, src,
+                                               dim3(a.num_q_heads / 2, a.batch, qtiles), stream);
+  return launch_tc_kind<TcKernel::kOneHead>(prm, qmap, src,
+                                            dim3(a.num_q_heads, a.batch, qtiles), stream);
 }
 
 }  // namespace pkv

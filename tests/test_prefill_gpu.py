@@ -191,11 +191,14 @@ def test_right_padded_rows_with_q_lens(cuda):
 
 
 @pytest.mark.parametrize("hq,hkv,B,T,causal", [(12, 2, 3, 700, True), (32, 2, 2, 300, True),
-                                               (4, 2, 5, 129, True), (12, 2, 2, 256, False)])
-def test_head_pair_kernel_matches_one_head_kernel(cuda, monkeypatch, hq, hkv, B, T, causal):
-    """Even GQA groups may run two q-heads per CTA over shared K/V tiles; the
-    per-head arithmetic is the one-head kernel's, so both give the same bits
-    (and match the oracle).  PKV_PREFILL_PAIR pins the kernel."""
+                                               (4, 2, 5, 129, True), (12, 2, 2, 256, False),
+                                               (12, 4, 2, 200, True)])
+def test_prefill_kernels_give_identical_bits(cuda, monkeypatch, hq, hkv, B, T, causal):
+    """Two tensor-core prefill kernels: one head per CTA (P in tensor memory)
+    and two q-heads of an even GQA group per CTA over shared K/V tiles (P
+    staged in shared memory).  The per-head arithmetic is the same, so both
+    give the same bits (and match the oracle).  PKV_PREFILL_KERNEL pins the
+    kernel."""
     import pagedkv
 
     g = torch.Generator().manual_seed(hq * 100 + T)
@@ -205,16 +208,53 @@ def test_head_pair_kernel_matches_one_head_kernel(cuda, monkeypatch, hq, hkv, B,
     v = torch.randn(B, hkv, S, 128, generator=g).to(torch.bfloat16)
     kv_lens = [S - (b * 13) % 29 for b in range(B)]
     outs = []
-    for force in ("1", "0"):
-        monkeypatch.setenv("PKV_PREFILL_PAIR", force)
+    kernels = ("one", "pair") if (hq // hkv) % 2 == 0 else ("one",)
+    for force in kernels:
+        monkeypatch.setenv("PKV_PREFILL_KERNEL", force)
         out = torch.full((B, hq, T, 128), 5.0, dtype=torch.bfloat16, device=cuda)
         pagedkv.dense_attention(q.to(cuda), k.to(cuda), v.to(cuda),
                                 torch.tensor(kv_lens, dtype=torch.int32, device=cuda), out,
                                 causal, 1 / math.sqrt(128))
         torch.cuda.synchronize()
         outs.append(out)
-    assert torch.equal(outs[0], outs[1])
+    for o in outs[1:]:
+        assert torch.equal(outs[0], o)
     for b in range(B):
         want = attention_ref.attention_np(q[b:b + 1].float().numpy(), k[b:b + 1].float().numpy(),
                                           v[b:b + 1].float().numpy(), [kv_lens[b]], causal)
         assert max_err(outs[0][b:b + 1], want) < TOL, b
+
+
+@pytest.mark.parametrize("prior,T", [([0, 0, 7], 300), ([1000, 3], 129)])
+def test_paged_prefill_kernels_give_identical_bits(cuda, monkeypatch, prior, T):
+    """Both prefill kernels on block-table K/V (shuffled, poisoned pool)."""
+    from kernels.fa2 import flash_attention
+
+    g = torch.Generator().manual_seed(sum(prior) * 3 + T)
+    B = len(prior)
+    N = sum(math.ceil((n + T) / 16) for n in prior) + 8
+    cache = build_cache(N, torch.randperm(N, generator=g).tolist(), cuda)
+    cache.buf.fill_(cases.PAD_VALUE)
+    seqs = [cache.alloc() for _ in prior]
+    hk = [torch.randn(1, 2, n, 128, generator=g).to(torch.bfloat16) for n in prior]
+    hv = [torch.randn(1, 2, n, 128, generator=g).to(torch.bfloat16) for n in prior]
+    write_history(cache, seqs, hk, hv)
+    q = torch.randn(B, 12, T, 128, generator=g).to(torch.bfloat16)
+    kn = torch.randn(B, 2, T, 128, generator=g).to(torch.bfloat16)
+    vn = torch.randn(B, 2, T, 128, generator=g).to(torch.bfloat16)
+    _, step, gidx = cache.prepare(seqs, T)
+    cache.write(0, step, kn.to(cuda), vn.to(cuda))
+    kh, vh = cache.read(0, gidx)
+    outs = []
+    for force in ("one", "pair"):
+        monkeypatch.setenv("PKV_PREFILL_KERNEL", force)
+        outs.append(flash_attention(q.to(cuda), kh, vh, True, step.kv_lens))
+    torch.cuda.synchronize()
+    cache.check_errors()
+    for o in outs[1:]:
+        assert torch.equal(outs[0], o)
+    kd = torch.cat([hk[0], kn[0:1]], 2)
+    vd = torch.cat([hv[0], vn[0:1]], 2)
+    want = attention_ref.attention_np(q[0:1].float().numpy(), kd.float().numpy(),
+                                      vd.float().numpy(), [prior[0] + T], True)
+    assert max_err(outs[1][0:1], want) < TOL
