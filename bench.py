@@ -85,6 +85,10 @@ def parse():
     ap.add_argument("--prefill-step", type=int, default=None, metavar="T",
                     help="whole-model one-row prefill of T tokens (CUDA graph of the padded "
                          "bucket, as chat.py admits a message)")
+    ap.add_argument("--prefill-sweep", type=str, default=None, metavar="BxT,...",
+                    help="causal prefill attention on dense K/V (12 q / 2 kv heads, d 128) "
+                         "per shape and per kernel (PKV_PREFILL_KERNEL one, pair), 20 "
+                         "launches per CUDA graph")
     ap.add_argument("--profile-range", action="store_true",
                     help="with --decode-step / --prefill-step: one eager step inside "
                          "cudaProfilerStart/Stop "
@@ -747,6 +751,53 @@ def decode_step_diag(spec, device, profile_range=False):
                       "skinny_rows": M.Qwen2ForCausalLM.skinny_rows}), flush=True)
 
 
+def prefill_sweep(shapes, device):
+    """Causal prefill attention per (B, T) on dense K/V, each kernel pinned by
+    PKV_PREFILL_KERNEL: 20 launches captured in a CUDA graph, CUDA events
+    around two replays.  Useful FLOPs = B * 4 * Hq * D * T(T+1)/2."""
+    from kernels.fa2 import flash_attention
+
+    peaks, src = measured_peaks()
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    saved = os.environ.get("PKV_PREFILL_KERNEL")
+    try:
+        for kern in ("one", "pair"):
+            os.environ["PKV_PREFILL_KERNEL"] = kern
+            for B, T in shapes:
+                g = torch.Generator(device=device).manual_seed(B * 100000 + T)
+                q = torch.randn(B, HQ, T, D, device=device, generator=g).to(torch.bfloat16)
+                k = torch.randn(B, HKV, T, D, device=device, generator=g).to(torch.bfloat16)
+                v = torch.randn(B, HKV, T, D, device=device, generator=g).to(torch.bfloat16)
+                out = torch.empty_like(q)
+                for _ in range(3):
+                    flash_attention(q, k, v, True, None, out=out)
+                torch.cuda.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    for _ in range(20):
+                        flash_attention(q, k, v, True, None, out=out)
+                graph.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                graph.replay()
+                graph.replay()
+                e1.record()
+                e1.synchronize()
+                us = e0.elapsed_time(e1) / 40 * 1e3
+                tf = B * 4 * HQ * D * T * (T + 1) / 2 / (us * 1e-6) / 1e12
+                print(json.dumps({"diag": "prefill_sweep", "kernel": kern, "B": B, "T": T,
+                                  "us_per_launch": round(us, 1), "tflops": round(tf, 1),
+                                  "frac_of_bf16_peak": round(tf / peak, 3), "peak_source": src}),
+                      flush=True)
+                del graph, q, k, v, out
+    finally:
+        if saved is None:
+            os.environ.pop("PKV_PREFILL_KERNEL", None)
+        else:
+            os.environ["PKV_PREFILL_KERNEL"] = saved
+
+
 def prefill_step_diag(T, device, profile_range=False):
     """One-row prefill of T tokens from an empty cache (random-init model):
     CUDA-graph replay of the padded bucket (the engine's path) and eager;
@@ -809,9 +860,12 @@ def main():
               "heads": [HQ, HKV, D], "l2": "inputs larger than L2 (KV read per step >> 126 MB)",
               "parallelism": f"replicas x{args.gpus} (request-sharded, no collective)"}
 
-    if args.linear_sweep or args.decode_step or args.prefill_step:
+    if args.linear_sweep or args.decode_step or args.prefill_step or args.prefill_sweep:
         dev = torch.device("cuda", local)
         torch.cuda.set_device(dev)
+        if args.prefill_sweep:
+            prefill_sweep([tuple(int(v) for v in x.split("x")) for x in args.prefill_sweep.split(",")],
+                          dev)
         if args.linear_sweep:
             linear_sweep([int(r) for r in args.linear_sweep.split(",")], dev)
         if args.decode_step:
