@@ -153,6 +153,54 @@ __global__ void __launch_bounds__(kThreads, 1)
     return;
   }
 
+  // ---- producer helpers (used by thread 0 only: warp 0 lane 0 issues every
+  // TMA load).  A tile's eight block ids are loaded together one tile ahead,
+  // so table reads never serialise the issue.
+  const uint64_t keep = policy_evict_last();
+  auto fetch = [&](int j, int (&ids)[kTileBlocks]) {
+    if constexpr (kPaged) {
+#pragma unroll
+      for (int jb = 0; jb < kTileBlocks; ++jb) {
+        const int lb = j * kTileBlocks + jb;
+        // blocks past the row's end load the row's first block: finite
+        // data, masked out of S and never multiplied into O
+        ids[jb] = trow[lb < nblk ? lb : 0];
+      }
+#pragma unroll
+      for (int jb = 0; jb < kTileBlocks; ++jb) {
+        if (ids[jb] < 0 || ids[jb] >= p.num_blocks) {
+          err.raise(PKV_DEVERR_BLOCK_ID);
+          ids[jb] = 0;
+        }
+      }
+    }
+  };
+  // K runs one tile ahead of V: issue K(j+1), then V(j)
+  auto issue = [&](int j, const int (&ids)[kTileBlocks], bool is_v) -> bool {
+    const int st = j % kStages;
+    uint64_t* full = is_v ? &v_full[st] : &k_full[st];
+    uint64_t* empty = is_v ? &v_empty[st] : &k_empty[st];
+    if (j >= kStages && !mbar_wait(empty, ((j / kStages) - 1) & 1, err)) return false;
+    uint8_t* dst = smem + kOffKV + st * 2 * kOperand + (is_v ? kOperand : 0);
+    const CUtensorMap* map = is_v ? &vmap : &kmap;
+    mbar_arrive_expect_tx(full, kOperand);
+#pragma unroll
+    for (int jb = 0; jb < kTileBlocks; ++jb) {
+      if constexpr (kPaged) {
+        const int slot = ids[jb] * kBlockTokens;
+        tma_load_3d(dst + jb * 2048, map, full, 0, kvh, slot, keep);
+        tma_load_3d(dst + kRegion + jb * 2048, map, full, 64, kvh, slot, keep);
+      } else {
+        const int tok = (j * kTileBlocks + jb) * kBlockTokens;
+        tma_load_4d(dst + jb * 2048, map, full, 0, tok, kvh, b, keep);
+        tma_load_4d(dst + kRegion + jb * 2048, map, full, 64, tok, kvh, b, keep);
+      }
+    }
+    return true;
+  };
+  int idk[kTileBlocks] = {}, idv[kTileBlocks] = {};
+  bool first_ok = false;
+
   if (tid == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < kStages; ++s) {
@@ -166,6 +214,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(pv_done, 1);
     mbar_init(mma_done, 1);
     fence_mbar_init();
+    // Q and the first K tile are requested before the TMEM allocation and
+    // the CTA barrier, so their latency overlaps the set-up
+    prefetch_tmap(&qmap);
+    prefetch_tmap(&kmap);
+    prefetch_tmap(&vmap);
+    fetch(0, idk);
+    mbar_arrive_expect_tx(q_full, kOperand);
+    tma_load_4d(smem + kOffQ, &qmap, q_full, 0, q0, hq, b, keep);
+    tma_load_4d(smem + kOffQ + kRegion, &qmap, q_full, 64, q0, hq, b, keep);
+    first_ok = issue(0, idk, false);
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -182,60 +240,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    // One thread issues every TMA load.  A tile's eight block ids are loaded
-    // together one tile ahead, so table reads never serialise the issue.
     if (lane == 0) {
-      auto fetch = [&](int j, int (&ids)[kTileBlocks]) {
-        if constexpr (kPaged) {
-#pragma unroll
-          for (int jb = 0; jb < kTileBlocks; ++jb) {
-            const int lb = j * kTileBlocks + jb;
-            // blocks past the row's end load the row's first block: finite
-            // data, masked out of S and never multiplied into O
-            ids[jb] = trow[lb < nblk ? lb : 0];
-          }
-#pragma unroll
-          for (int jb = 0; jb < kTileBlocks; ++jb) {
-            if (ids[jb] < 0 || ids[jb] >= p.num_blocks) {
-              err.raise(PKV_DEVERR_BLOCK_ID);
-              ids[jb] = 0;
-            }
-          }
-        }
-      };
-      prefetch_tmap(&qmap);
-      prefetch_tmap(&kmap);
-      prefetch_tmap(&vmap);
-      const uint64_t keep = policy_evict_last();
-      // K runs one tile ahead of V: issue K(j+1), then V(j)
-      auto issue = [&](int j, const int (&ids)[kTileBlocks], bool is_v) -> bool {
-        const int st = j % kStages;
-        uint64_t* full = is_v ? &v_full[st] : &k_full[st];
-        uint64_t* empty = is_v ? &v_empty[st] : &k_empty[st];
-        if (j >= kStages && !mbar_wait(empty, ((j / kStages) - 1) & 1, err)) return false;
-        uint8_t* dst = smem + kOffKV + st * 2 * kOperand + (is_v ? kOperand : 0);
-        const CUtensorMap* map = is_v ? &vmap : &kmap;
-        mbar_arrive_expect_tx(full, kOperand);
-#pragma unroll
-        for (int jb = 0; jb < kTileBlocks; ++jb) {
-          if constexpr (kPaged) {
-            const int slot = ids[jb] * kBlockTokens;
-            tma_load_3d(dst + jb * 2048, map, full, 0, kvh, slot, keep);
-            tma_load_3d(dst + kRegion + jb * 2048, map, full, 64, kvh, slot, keep);
-          } else {
-            const int tok = (j * kTileBlocks + jb) * kBlockTokens;
-            tma_load_4d(dst + jb * 2048, map, full, 0, tok, kvh, b, keep);
-            tma_load_4d(dst + kRegion + jb * 2048, map, full, 64, tok, kvh, b, keep);
-          }
-        }
-        return true;
-      };
-      int idk[kTileBlocks] = {}, idv[kTileBlocks] = {};
-      fetch(0, idk);
-      mbar_arrive_expect_tx(q_full, kOperand);
-      tma_load_4d(smem + kOffQ, &qmap, q_full, 0, q0, hq, b, keep);
-      tma_load_4d(smem + kOffQ + kRegion, &qmap, q_full, 64, q0, hq, b, keep);
-      if (issue(0, idk, false)) {
+      if (first_ok) {
         for (int j = 0; j < ntiles; ++j) {
 #pragma unroll
           for (int jb = 0; jb < kTileBlocks; ++jb) idv[jb] = idk[jb];
@@ -399,19 +405,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (have) {
       tc_fence_after();
       const float inv = 1.f / l;  // 0/0 -> NaN for a row with no visible key
+      float v[4][32];  // all of O's row, one wait
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(lane_addr + kColO + c * 32, v);
-        tmem_wait_ld();
-        if (qi < T) {
+      for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + kColO + c * 32, v[c]);
+      tmem_wait_ld();
+      if (qi < T) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
 #pragma unroll
           for (int e = 0; e < 32; e += 8) {
             uint4 pk;
-            pk.x = pack_bf16(v[e + 0] * inv, v[e + 1] * inv);
-            pk.y = pack_bf16(v[e + 2] * inv, v[e + 3] * inv);
-            pk.z = pack_bf16(v[e + 4] * inv, v[e + 5] * inv);
-            pk.w = pack_bf16(v[e + 6] * inv, v[e + 7] * inv);
+            pk.x = pack_bf16(v[c][e + 0] * inv, v[c][e + 1] * inv);
+            pk.y = pack_bf16(v[c][e + 2] * inv, v[c][e + 3] * inv);
+            pk.z = pack_bf16(v[c][e + 4] * inv, v[c][e + 5] * inv);
+            pk.w = pack_bf16(v[c][e + 6] * inv, v[c][e + 7] * inv);
             *reinterpret_cast<uint4*>(orow + c * 32 + e) = pk;
           }
         }
@@ -516,6 +523,49 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     return;
   }
 
+  // ---- producer helpers (thread 0, warp 0 lane 0, issues every TMA load)
+  const uint64_t keep = policy_evict_last();
+  auto fetch = [&](int j, int (&ids)[kTileBlocks]) {
+    if constexpr (kPaged) {
+#pragma unroll
+      for (int jb = 0; jb < kTileBlocks; ++jb) {
+        const int lb = j * kTileBlocks + jb;
+        ids[jb] = trow[lb < nblk ? lb : 0];  // past the end: finite, masked
+      }
+#pragma unroll
+      for (int jb = 0; jb < kTileBlocks; ++jb) {
+        if (ids[jb] < 0 || ids[jb] >= p.num_blocks) {
+          err.raise(PKV_DEVERR_BLOCK_ID);
+          ids[jb] = 0;
+        }
+      }
+    }
+  };
+  auto issue = [&](int j, const int (&ids)[kTileBlocks], bool is_v) -> bool {
+    const int st = j % kStages;
+    uint64_t* full = is_v ? &v_full[st] : &k_full[st];
+    uint64_t* empty = is_v ? &v_empty[st] : &k_empty[st];
+    if (j >= kStages && !mbar_wait(empty, ((j / kStages) - 1) & 1, err)) return false;
+    uint8_t* dst = smem + (is_v ? kPOffV : kPOffK) + st * kOperand;
+    const CUtensorMap* map = is_v ? &vmap : &kmap;
+    mbar_arrive_expect_tx(full, kOperand);
+#pragma unroll
+    for (int jb = 0; jb < kTileBlocks; ++jb) {
+      if constexpr (kPaged) {
+        const int slot = ids[jb] * kBlockTokens;
+        tma_load_3d(dst + jb * 2048, map, full, 0, kvh, slot, keep);
+        tma_load_3d(dst + kRegion + jb * 2048, map, full, 64, kvh, slot, keep);
+      } else {
+        const int tok = (j * kTileBlocks + jb) * kBlockTokens;
+        tma_load_4d(dst + jb * 2048, map, full, 0, tok, kvh, b, keep);
+        tma_load_4d(dst + kRegion + jb * 2048, map, full, 64, tok, kvh, b, keep);
+      }
+    }
+    return true;
+  };
+  int idk[kTileBlocks] = {}, idv[kTileBlocks] = {};
+  bool first_ok = false;
+
   if (tid == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < kStages; ++s) {
@@ -532,6 +582,20 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     }
     mbar_init(mma_done, 1);
     fence_mbar_init();
+    // both Q tiles and the first K tile are requested before the TMEM
+    // allocation and the CTA barrier, so their latency overlaps the set-up
+    prefetch_tmap(&qmap);
+    prefetch_tmap(&kmap);
+    prefetch_tmap(&vmap);
+    fetch(0, idk);
+    mbar_arrive_expect_tx(q_full, 2 * kOperand);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint8_t* qd = smem + kPOffQ + h * kOperand;
+      tma_load_4d(qd, &qmap, q_full, 0, q0, hq0 + h, b, keep);
+      tma_load_4d(qd + kRegion, &qmap, q_full, 64, q0, hq0 + h, b, keep);
+    }
+    first_ok = issue(0, idk, false);
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before();
@@ -544,58 +608,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      auto fetch = [&](int j, int (&ids)[kTileBlocks]) {
-        if constexpr (kPaged) {
-#pragma unroll
-          for (int jb = 0; jb < kTileBlocks; ++jb) {
-            const int lb = j * kTileBlocks + jb;
-            ids[jb] = trow[lb < nblk ? lb : 0];  // past the end: finite, masked
-          }
-#pragma unroll
-          for (int jb = 0; jb < kTileBlocks; ++jb) {
-            if (ids[jb] < 0 || ids[jb] >= p.num_blocks) {
-              err.raise(PKV_DEVERR_BLOCK_ID);
-              ids[jb] = 0;
-            }
-          }
-        }
-      };
-      prefetch_tmap(&qmap);
-      prefetch_tmap(&kmap);
-      prefetch_tmap(&vmap);
-      const uint64_t keep = policy_evict_last();
-      auto issue = [&](int j, const int (&ids)[kTileBlocks], bool is_v) -> bool {
-        const int st = j % kStages;
-        uint64_t* full = is_v ? &v_full[st] : &k_full[st];
-        uint64_t* empty = is_v ? &v_empty[st] : &k_empty[st];
-        if (j >= kStages && !mbar_wait(empty, ((j / kStages) - 1) & 1, err)) return false;
-        uint8_t* dst = smem + (is_v ? kPOffV : kPOffK) + st * kOperand;
-        const CUtensorMap* map = is_v ? &vmap : &kmap;
-        mbar_arrive_expect_tx(full, kOperand);
-#pragma unroll
-        for (int jb = 0; jb < kTileBlocks; ++jb) {
-          if constexpr (kPaged) {
-            const int slot = ids[jb] * kBlockTokens;
-            tma_load_3d(dst + jb * 2048, map, full, 0, kvh, slot, keep);
-            tma_load_3d(dst + kRegion + jb * 2048, map, full, 64, kvh, slot, keep);
-          } else {
-            const int tok = (j * kTileBlocks + jb) * kBlockTokens;
-            tma_load_4d(dst + jb * 2048, map, full, 0, tok, kvh, b, keep);
-            tma_load_4d(dst + kRegion + jb * 2048, map, full, 64, tok, kvh, b, keep);
-          }
-        }
-        return true;
-      };
-      int idk[kTileBlocks] = {}, idv[kTileBlocks] = {};
-      fetch(0, idk);
-      mbar_arrive_expect_tx(q_full, 2 * kOperand);
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint8_t* qd = smem + kPOffQ + h * kOperand;
-        tma_load_4d(qd, &qmap, q_full, 0, q0, hq0 + h, b, keep);
-        tma_load_4d(qd + kRegion, &qmap, q_full, 64, q0, hq0 + h, b, keep);
-      }
-      if (issue(0, idk, false)) {
+      if (first_ok) {
         for (int j = 0; j < ntiles; ++j) {
 #pragma unroll
           for (int jb = 0; jb < kTileBlocks; ++jb) idv[jb] = idk[jb];
@@ -773,19 +786,20 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     if (have) {
       tc_fence_after();
       const float inv = 1.f / l;  // 0/0 -> NaN for a row with no visible key
+      float v[4][32];  // all of O's row, one wait
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(lane_addr + colO + c * 32, v);
-        tmem_wait_ld();
-        if (qi < T) {
+      for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + colO + c * 32, v[c]);
+      tmem_wait_ld();
+      if (qi < T) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
 #pragma unroll
           for (int e = 0; e < 32; e += 8) {
             uint4 pk;
-            pk.x = pack_bf16(v[e + 0] * inv, v[e + 1] * inv);
-            pk.y = pack_bf16(v[e + 2] * inv, v[e + 3] * inv);
-            pk.z = pack_bf16(v[e + 4] * inv, v[e + 5] * inv);
-            pk.w = pack_bf16(v[e + 6] * inv, v[e + 7] * inv);
+            pk.x = pack_bf16(v[c][e + 0] * inv, v[c][e + 1] * inv);
+            pk.y = pack_bf16(v[c][e + 2] * inv, v[c][e + 3] * inv);
+            pk.z = pack_bf16(v[c][e + 4] * inv, v[c][e + 5] * inv);
+            pk.w = pack_bf16(v[c][e + 6] * inv, v[c][e + 7] * inv);
             *reinterpret_cast<uint4*>(orow + c * 32 + e) = pk;
           }
         }
