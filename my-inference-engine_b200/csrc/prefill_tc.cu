@@ -84,6 +84,42 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk) {
   return sdesc(base + (kk >> 2) * kRegion + (kk & 3) * 32, 16, 1024);
 }
 
+// Epilogue store of one softmax warp's 32 output rows.  Lane i holds row i
+// of O (fp32, from TMEM); a direct store would have every lane write its own
+// 256-byte row, 32 lines per instruction.  Instead the rows go through an
+// 8 KiB shared-memory stage (16-byte chunk c of row i at slot c ^ (i & 15):
+// conflict-free both ways) and come back out two whole rows per instruction.
+// `obase` is the warp's first row; rows at or past `rows_valid` are not
+// written.
+__device__ __forceinline__ void store_o_rows(uint8_t* stage, const float (&v)[4][32], float inv,
+                                             int lane, __nv_bfloat16* obase, int64_t o_st,
+                                             int rows_valid) {
+  uint8_t* mine = stage + lane * 256;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+#pragma unroll
+    for (int e = 0; e < 32; e += 8) {
+      uint4 pk;
+      pk.x = pack_bf16(v[c][e + 0] * inv, v[c][e + 1] * inv);
+      pk.y = pack_bf16(v[c][e + 2] * inv, v[c][e + 3] * inv);
+      pk.z = pack_bf16(v[c][e + 4] * inv, v[c][e + 5] * inv);
+      pk.w = pack_bf16(v[c][e + 6] * inv, v[c][e + 7] * inv);
+      const int chunk = c * 4 + e / 8;
+      *reinterpret_cast<uint4*>(mine + ((chunk ^ (lane & 15)) << 4)) = pk;
+    }
+  }
+  __syncwarp();
+  const int ch = lane & 15;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int row = 2 * i + (lane >> 4);
+    const uint4 val =
+        *reinterpret_cast<const uint4*>(stage + row * 256 + ((ch ^ (row & 15)) << 4));
+    if (row < rows_valid)
+      *reinterpret_cast<uint4*>(obase + static_cast<int64_t>(row) * o_st + ch * 8) = val;
+  }
+}
+
 template <bool kPaged>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap qmap,
@@ -117,6 +153,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int b = blockIdx.y;
   const int kvh = hq / p.group;
   const int q0 = (gridDim.z - 1 - blockIdx.z) * kRows;
+  // the tensor maps are launch parameters: fetch them while the predecessor
+  // grid drains
+  if (tid == 0) {
+    prefetch_tmap(&qmap);
+    prefetch_tmap(&kmap);
+    prefetch_tmap(&vmap);
+  }
   // this row's real query count (right padding beyond it is not written)
   pdl_wait();
   const int T = p.q_lens ? min(max(p.q_lens[b], 0), p.T) : p.T;
@@ -215,14 +258,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(mma_done, 1);
     fence_mbar_init();
     // Q and the first K tile are requested before the TMEM allocation and
-    // the CTA barrier, so their latency overlaps the set-up
-    prefetch_tmap(&qmap);
-    prefetch_tmap(&kmap);
-    prefetch_tmap(&vmap);
-    fetch(0, idk);
+    // the CTA barrier, so their latency overlaps the set-up; Q goes first,
+    // so its load overlaps the block-table read that K(0) depends on
     mbar_arrive_expect_tx(q_full, kOperand);
     tma_load_4d(smem + kOffQ, &qmap, q_full, 0, q0, hq, b, keep);
     tma_load_4d(smem + kOffQ + kRegion, &qmap, q_full, 64, q0, hq, b, keep);
+    fetch(0, idk);
     first_ok = issue(0, idk, false);
   }
   if (warp == 1) {
@@ -409,6 +450,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + kColO + c * 32, v[c]);
       tmem_wait_ld();
+      // direct row stores: staging through shared memory (store_o_rows, as
+      // the head-pair kernel does) cost this kernel two registers and ~5%
+      // of its main-loop speed on every measured shape
       if (qi < T) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -488,6 +532,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   const int b = blockIdx.y;
   const int kvh = hq0 / p.group;
   const int q0 = (gridDim.z - 1 - blockIdx.z) * kRows;  // heaviest q-tiles first
+  if (tid == 0) {  // launch parameters: fetched while the predecessor drains
+    prefetch_tmap(&qmap);
+    prefetch_tmap(&kmap);
+    prefetch_tmap(&vmap);
+  }
   pdl_wait();
   const int T = p.q_lens ? min(max(p.q_lens[b], 0), p.T) : p.T;
   const DevErr err{p.err};
@@ -583,11 +632,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     mbar_init(mma_done, 1);
     fence_mbar_init();
     // both Q tiles and the first K tile are requested before the TMEM
-    // allocation and the CTA barrier, so their latency overlaps the set-up
-    prefetch_tmap(&qmap);
-    prefetch_tmap(&kmap);
-    prefetch_tmap(&vmap);
-    fetch(0, idk);
+    // allocation and the CTA barrier, so their latency overlaps the set-up;
+    // Q goes first, overlapping the block-table read that K(0) depends on
     mbar_arrive_expect_tx(q_full, 2 * kOperand);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -595,6 +641,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       tma_load_4d(qd, &qmap, q_full, 0, q0, hq0 + h, b, keep);
       tma_load_4d(qd + kRegion, &qmap, q_full, 64, q0, hq0 + h, b, keep);
     }
+    fetch(0, idk);
     first_ok = issue(0, idk, false);
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
@@ -790,20 +837,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + colO + c * 32, v[c]);
       tmem_wait_ld();
-      if (qi < T) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            uint4 pk;
-            pk.x = pack_bf16(v[c][e + 0] * inv, v[c][e + 1] * inv);
-            pk.y = pack_bf16(v[c][e + 2] * inv, v[c][e + 3] * inv);
-            pk.z = pack_bf16(v[c][e + 4] * inv, v[c][e + 5] * inv);
-            pk.w = pack_bf16(v[c][e + 6] * inv, v[c][e + 7] * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + e) = pk;
-          }
-        }
-      }
+      // Q_h is free: pv_done[h] of the last tile retired every earlier MMA,
+      // this head's Q.K^T products included
+      const int w0 = q0 + quarter * 32;
+      store_o_rows(smem + kPOffQ + h * kOperand + quarter * 8192, v, inv, lane,
+                   p.out + b * p.o_sb + (hq0 + h) * p.o_sh + static_cast<int64_t>(w0) * p.o_st,
+                   p.o_st, T - w0);
     } else if (qi < T) {
       const uint32_t nan2 = 0x7fc07fc0u;  // a timed-out wait: NaN rows, not stale data
       const uint4 nv = make_uint4(nan2, nan2, nan2, nan2);
