@@ -25,6 +25,7 @@ metrics/benchmark_concurrency.py:25-26) and the CPU oracle read it unchanged.
 """
 from __future__ import annotations
 
+import itertools
 import math
 from dataclasses import dataclass
 
@@ -155,11 +156,16 @@ class BlockTables:
             raise RuntimeError(
                 f"KV cache exhausted: seq {seq} would hold {len(table) + need} blocks, "
                 f"the device table holds {self.table_pitch} per sequence")
+        if need == 0:
+            return
         row = self._row_of[seq]
-        for _ in range(need):
-            blk = self._free_blocks.pop()
-            self._pending[(row, len(table))] = blk
-            table.append(blk)
+        # the blocks `need` pops from the tail of the free list would return,
+        # in pop order, taken as one slice
+        blks = self._free_blocks[-need:][::-1]
+        del self._free_blocks[-need:]
+        col0 = len(table)
+        self._pending.update(zip(zip(itertools.repeat(row, need), range(col0, col0 + need)), blks))
+        table.extend(blks)
 
     def trim(self, seq):
         """Give back any blocks past the one holding seq's last written token."""
@@ -188,8 +194,10 @@ class BlockTables:
     def step_rows(self, seqs, T):
         """Host part of prepare(): reserve blocks, return (starts, rows)."""
         starts = [self._lengths[s] for s in seqs]
+        bs, tables = self.block_size, self._block_tables
         for s, start in zip(seqs, starts):
-            self.ensure_capacity(s, start + T)
+            if start + T > len(tables[s]) * bs:  # otherwise ensure_capacity adds nothing
+                self.ensure_capacity(s, start + T)
         return starts, [self._row_of[s] for s in seqs]
 
 

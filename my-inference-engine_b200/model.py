@@ -18,6 +18,7 @@ Changed (the hot path):
 """
 from __future__ import annotations
 
+import numpy as np
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
@@ -482,17 +483,17 @@ class DecodeGraphs:
         g, ins, host, logits = self.graphs.get(Bp) or self._capture(Bp)
         starts, rows = self.cache.step_rows(seqs, 1)
         self.cache.flush_tables()
+        h = host.numpy()  # the pinned buffer, filled in place (no per-row torch ops)
         if not input_ids.is_cuda:
-            host[0, :B] = input_ids.view(-1).to(torch.int32)
-        st = torch.tensor(starts, dtype=torch.int32)
-        host[1, :B] = torch.tensor(rows, dtype=torch.int32)
-        host[2, :B] = st
-        host[3, :B] = st + 1
+            h[0, :B] = input_ids.view(-1).numpy()
+        h[1, :B] = rows
+        h[2, :B] = starts
+        np.add(h[2, :B], 1, out=h[3, :B])
         if Bp > B:
-            host[0, B:] = 0
-            host[1, B:] = 0
-            host[2, B:] = -1
-            host[3, B:] = 0
+            h[0, B:] = 0
+            h[1, B:] = 0
+            h[2, B:] = -1
+            h[3, B:] = 0
         ins.copy_(host, non_blocking=True)
         if input_ids.is_cuda:  # device ids: a device-side copy, no host sync
             ins[0, :B].copy_(input_ids.view(-1))
@@ -557,9 +558,10 @@ class PrefillGraphs:
         g, ids, meta, host, logits = self.graphs.get(Tp) or self._capture(Tp)
         starts, rows = self.cache.step_rows(seqs, T)
         self.cache.flush_tables()
-        host[0], host[1], host[2], host[3] = rows[0], starts[0], starts[0] + T, T
+        h = host.numpy()
+        h[:4] = (rows[0], starts[0], starts[0] + T, T)
         if not input_ids.is_cuda:
-            host[4:4 + T] = input_ids.view(-1).to(torch.int32)
+            h[4:4 + T] = input_ids.view(-1).numpy()
         meta.view(-1).copy_(host[:4], non_blocking=True)
         if input_ids.is_cuda:
             ids[0, :T].copy_(input_ids.view(-1))
