@@ -155,13 +155,35 @@ class _Job:
         self.new_ids = chat.tokenizer.encode(f"User: {text}\nAssistant:")
 
 
-def _sample(logits):
-    """One token id per row of [B, vocab] logits, one device sync for the batch."""
+def _sample_async(logits):
+    """Enqueue sampling of one token id per row of [B, vocab] logits; the ids
+    stay on the logits' device."""
     x = logits.float()
     if TEMPERATURE != 1:  # x / 1 is x: skip the extra pass over [B, vocab]
         x = x / TEMPERATURE
     probs = F.softmax(x, dim=-1)
-    return torch.multinomial(probs, num_samples=1).squeeze(1).tolist()
+    return torch.multinomial(probs, num_samples=1).squeeze(1)
+
+
+def _sample(logits):
+    """One token id per row of [B, vocab] logits, one device sync for the batch."""
+    return _sample_async(logits).tolist()
+
+
+class _PendingToken:
+    """A prompt's first sampled token, not yet read back: `_prefill` enqueues
+    the sampling and `_process` reads the id when it reaches the job, which
+    is last in FIFO order, so the host work for the jobs ahead of it runs
+    while the prefill is still on the GPU.  Same ids, same order of sampling
+    draws and of every scheduling decision as reading it at once."""
+
+    __slots__ = ("ids",)
+
+    def __init__(self, ids):
+        self.ids = ids
+
+    def get(self):
+        return self.ids.tolist()[0]
 
 
 _job_queue = queue.Queue()
@@ -241,7 +263,7 @@ def _prefill(job, prefill_ids):
     input_ids = _host_ids(prefill_ids)
     with torch.no_grad():
         logits = job.model(input_ids, _kv(), [job.chat.seq])
-    job.next_token = _sample(logits[:, -1])[0]
+    job.next_token = _PendingToken(_sample_async(logits[:, -1]))
     active.append(job)
 
 
@@ -326,6 +348,8 @@ def _process(active):
     for job in list(active):
         chat = job.chat
         token_id = job.next_token
+        if type(token_id) is _PendingToken:
+            token_id = job.next_token = token_id.get()
         chat.ids.append(token_id)
 
         if token_id == chat.eos_id:
