@@ -191,6 +191,21 @@ int pkv_silu_mul(const void* gu, int64_t gu_stride, void* out, int64_t o_stride,
                  int32_t inter, void* stream);
 
 /*
+ * Temperature sampling: one token id per row from softmax(logits / temperature).
+ * Replaces chat.py:103-107 (`torch.multinomial(F.softmax(logits.float() / T,
+ * dim=-1), num_samples=1)`) with one kernel pass over the logits and no
+ * probability tensor (Gumbel-max: argmax of logits / T plus i.i.d. Gumbel
+ * noise, an exact draw from that categorical).  The noise comes from
+ * Philox-4x32-10 keyed by `seed`, counter (element / 4, row, call): the same
+ * (seed, call) always gives the same ids.  logits: [rows][ld], bf16
+ * (dtype 0) or float32 (dtype 1), ld >= vocab.  temperature > 0.  out: int32
+ * device [rows]; a row with no finite logit gets -1 (the reference raises
+ * RuntimeError for such a row; the Python shim does too).
+ */
+int pkv_sample(const void* logits, int64_t ld, int32_t rows, int32_t vocab, int32_t dtype,
+               float temperature, uint64_t seed, uint64_t call, int32_t* out, void* stream);
+
+/*
  * Size of the library-owned scratch used by pkv_paged_decode_static_scratch:
  * one array of this many bytes per GPU that loads the library, held until
  * the process exits.

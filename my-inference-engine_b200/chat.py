@@ -38,6 +38,7 @@ import time
 import torch
 import torch.nn.functional as F
 
+import pagedkv
 from kv_cache import KVCache
 from model import Qwen2ForCausalLM
 
@@ -156,8 +157,17 @@ class _Job:
 
 
 def _sample_async(logits):
-    """Enqueue sampling of one token id per row of [B, vocab] logits; the ids
-    stay on the logits' device."""
+    """Enqueue sampling of one token id per row of [B, vocab] logits from
+    softmax(logits / TEMPERATURE); the ids stay on the logits' device.
+
+    CUDA logits: one pkv_sample kernel (Gumbel-max over the logits, keyed
+    from torch's default generator) instead of the float copy, softmax and
+    torch.multinomial of the reference (chat.py:103-107), whose argument
+    checks also cost ~0.5 ms of host time per call.  Host logits only come
+    from a stand-in model (the scheduler's CPU tests) and take the
+    reference's own three ops."""
+    if logits.is_cuda:
+        return pagedkv.sample(logits, TEMPERATURE)
     x = logits.float()
     if TEMPERATURE != 1:  # x / 1 is x: skip the extra pass over [B, vocab]
         x = x / TEMPERATURE
@@ -165,9 +175,18 @@ def _sample_async(logits):
     return torch.multinomial(probs, num_samples=1).squeeze(1)
 
 
+def _read_ids(ids):
+    """Sampled ids as Python ints (one device sync); a row the kernel could
+    not sample (no finite logit) raises as torch.multinomial does."""
+    out = ids.tolist()
+    if out and min(out) < 0:
+        raise RuntimeError("probability tensor contains either `inf`, `nan` or element < 0")
+    return out
+
+
 def _sample(logits):
     """One token id per row of [B, vocab] logits, one device sync for the batch."""
-    return _sample_async(logits).tolist()
+    return _read_ids(_sample_async(logits))
 
 
 class _PendingToken:
@@ -183,7 +202,7 @@ class _PendingToken:
         self.ids = ids
 
     def get(self):
-        return self.ids.tolist()[0]
+        return _read_ids(self.ids)[0]
 
 
 _job_queue = queue.Queue()

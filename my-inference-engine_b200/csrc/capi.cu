@@ -4,6 +4,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
 
@@ -433,6 +434,35 @@ int pkv_add_rmsnorm(const void* a, int64_t a_stride, const void* resid, int64_t 
   pkv::NormLaunch p{a, a_stride, resid, r_stride, resid_out, ro_stride, weight, out, o_stride,
                     rows, dim, eps};
   return launch_status(pkv::launch_add_rmsnorm(p, static_cast<cudaStream_t>(stream)), "add_rmsnorm");
+}
+
+int pkv_sample(const void* logits, int64_t ld, int32_t rows, int32_t vocab, int32_t dtype,
+               float temperature, uint64_t seed, uint64_t call, int32_t* out, void* stream) {
+  if (!logits || !out) return fail(PKV_ERR_INVALID, "null logits or out");
+  if (dtype != 0 && dtype != 1) return fail(PKV_ERR_UNSUPPORTED, "dtype must be 0 (bf16) or 1 (f32)");
+  if (rows < 0 || rows > 65535 || vocab <= 0 || ld < vocab)
+    return fail(PKV_ERR_INVALID, "bad sample shape: rows %d (<= 65535), vocab %d, ld %lld", rows,
+                vocab, static_cast<long long>(ld));
+  if (!(temperature > 0.f) || !(temperature < INFINITY))
+    return fail(PKV_ERR_INVALID, "temperature must be positive and finite");
+  const size_t esz = dtype == 1 ? 4 : 2;
+  if (reinterpret_cast<uintptr_t>(logits) % esz != 0)
+    return fail(PKV_ERR_ALIGN, "logits not aligned to their element size");
+  if (rows == 0) return ok();
+  pkv::SampleLaunch a{};
+  a.logits = logits;
+  a.ld = ld;
+  a.rows = rows;
+  a.vocab = vocab;
+  a.f32 = dtype == 1;
+  // 4-wide loads when every row starts on a 4-element boundary
+  a.vec = (ld % 4 == 0) && (reinterpret_cast<uintptr_t>(logits) % (4 * esz) == 0);
+  a.splits = pkv::sample_splits(rows, vocab);
+  a.inv_temp = 1.0f / temperature;
+  a.seed = seed;
+  a.call = call;
+  a.out = out;
+  return launch_status(pkv::launch_sample(a, static_cast<cudaStream_t>(stream)), "sample");
 }
 
 int pkv_silu_mul(const void* gu, int64_t gu_stride, void* out, int64_t o_stride, int32_t rows,

@@ -163,4 +163,19 @@ cudaError_t launch_pair_gate_up(const void* w, int64_t ldw, int32_t inter, int32
 cudaError_t launch_silu_mul(const void* gu, int64_t gu_stride, void* out, int64_t o_stride,
                             int32_t rows, int32_t inter, cudaStream_t stream);
 
+// Temperature sampling, one token per row (sample.cu).
+struct SampleLaunch {
+  const void* logits;  // [rows][ld], bf16 or f32
+  int64_t ld;
+  int32_t rows, vocab;
+  int32_t f32;     // logits are float32 (else bf16)
+  int32_t vec;     // rows start 4-element aligned: 4-wide loads
+  int32_t splits;  // CTAs (= cluster size) per row, sample_splits()
+  float inv_temp;
+  uint64_t seed, call;
+  int32_t* out;  // [rows]; -1 where a row has no finite score
+};
+int sample_splits(int32_t rows, int32_t vocab);
+cudaError_t launch_sample(const SampleLaunch& a, cudaStream_t stream);
+
 }  // namespace pkv

@@ -29,6 +29,7 @@ import itertools
 import math
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 import pagedkv
@@ -227,12 +228,18 @@ class KVCache(BlockTables):
     # ---- device side ----
     def flush_tables(self):
         """Upload queued (row, col, block) entries in one copy + one scatter."""
-        pend = self.take_pending()
+        pend, self._pending = self._pending, {}
         if not pend:
             return
-        d = torch.tensor(pend, dtype=torch.int64).pin_memory().to(self.device, non_blocking=True)
-        flat = d[:, 0] * self.table_pitch + d[:, 1]
-        self.block_tables.view(-1).index_copy_(0, flat, d[:, 2].to(torch.int32))
+        n = len(pend)
+        # flat table index and block id per entry, built on the host in numpy
+        rc = np.fromiter(itertools.chain.from_iterable(pend.keys()), dtype=np.int64, count=2 * n)
+        host = np.empty((2, n), dtype=np.int64)
+        np.multiply(rc[0::2], self.table_pitch, out=host[0])
+        host[0] += rc[1::2]
+        host[1] = np.fromiter(pend.values(), dtype=np.int64, count=n)
+        d = torch.from_numpy(host).pin_memory().to(self.device, non_blocking=True)
+        self.block_tables.view(-1).index_copy_(0, d[0], d[1].to(torch.int32))
 
     def prepare(self, seqs, T):
         """Set up one forward step that appends T tokens to every seq in `seqs`.

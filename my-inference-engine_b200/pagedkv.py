@@ -53,6 +53,9 @@ _SIGNATURES = {
         [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, ctypes.c_float, _vp],
         ctypes.c_int),
     "pkv_silu_mul": ([_vp, _i64, _vp, _i64, _i32, _i32, _vp], ctypes.c_int),
+    "pkv_sample": (
+        [_vp, _i64, _i32, _i32, _i32, ctypes.c_float, ctypes.c_uint64, ctypes.c_uint64, _vp, _vp],
+        ctypes.c_int),
     "pkv_paged_decode_static_scratch": (
         [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
          ctypes.c_float, _vp, _i64, _i64, _vp, _vp], ctypes.c_int),
@@ -263,6 +266,36 @@ def silu_mul(gu: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     st = lib().pkv_silu_mul(_ptr(gu), gu.stride(0), _ptr(out), out.stride(0), rows, inter,
                             _stream(gu.device))
     _check(st, "pkv_silu_mul")
+    return out
+
+
+def sample(logits: torch.Tensor, temperature: float = 1.0, *, seed: int | None = None,
+           call: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """pkv_sample: one token id per row of logits [rows, vocab] (bf16 or f32,
+    CUDA) drawn from softmax(logits / temperature) -> int32 [rows] on the same
+    device; -1 marks a row without a finite logit.
+
+    Without a seed, each call draws its 63-bit key from torch's default
+    (CPU) generator, so after torch.manual_seed(s) a run repeats its draws
+    call for call, as torch.multinomial's would."""
+    assert logits.is_cuda and logits.dim() == 2, "logits must be a 2-D CUDA tensor"
+    if logits.dtype == torch.bfloat16:
+        dtype = 0
+    elif logits.dtype == torch.float32:
+        dtype = 1
+    else:
+        raise AssertionError(f"logits must be bf16 or float32, got {logits.dtype}")
+    if logits.stride(1) != 1:
+        logits = logits.contiguous()
+    if seed is None:
+        seed = int(torch.randint(1 << 62, (1,)).item())
+    rows, vocab = logits.shape
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    st = lib().pkv_sample(_ptr(logits), logits.stride(0), rows, vocab, dtype, float(temperature),
+                          seed & 0xFFFFFFFFFFFFFFFF, call & 0xFFFFFFFFFFFFFFFF, _ptr(out),
+                          _stream(logits.device))
+    _check(st, "pkv_sample")
     return out
 
 

@@ -21,7 +21,8 @@ CSRC = HERE / "csrc"
 INCLUDE = HERE.parent / "include"
 LIB = HERE / "libpagedkv.so"
 BUILD_DIR = HERE / "_build"
-SOURCES = ["capi.cu", "append.cu", "decode.cu", "prefill_tc.cu", "fused.cu", "linear_tc.cu"]
+SOURCES = ["capi.cu", "append.cu", "decode.cu", "prefill_tc.cu", "fused.cu", "linear_tc.cu",
+           "sample.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 

@@ -141,3 +141,39 @@ def test_oracle_prefill_config1_matches_reference(golden):
         got = attention_ref.attention_np(inp["q"][b:b + 1].float().numpy(), kd[b].numpy(),
                                          vd[b].numpy(), [kd[b].shape[2]], True)
         assert np.abs(got - fx["out"][b:b + 1]).max() < 1e-4
+
+
+def test_oracle_philox_matches_published_known_answers():
+    """The sampler oracle's Philox-4x32-10 against the known-answer vectors of
+    the generator's authors (Random123 kat_vectors: zero, all-ones, and the
+    pi-digits counter/key)."""
+    import numpy as np
+
+    from oracle.sample_ref import philox4x32_10
+
+    kats = [
+        ((0, 0, 0, 0), (0, 0), (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)),
+        ((0xFFFFFFFF,) * 4, (0xFFFFFFFF, 0xFFFFFFFF), (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)),
+        ((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0),
+         (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1)),
+    ]
+    for ctr, key, want in kats:
+        got = philox4x32_10(np.array([ctr], dtype=np.uint32), key)[0]
+        assert [int(x) for x in got] == list(want)
+
+
+def test_oracle_gumbel_sampling_follows_softmax():
+    """The oracle's Gumbel-max draw has the reference sampler's distribution
+    (softmax(logits / T), chat.py:103-107) on a small vocabulary."""
+    import numpy as np
+
+    from oracle.sample_ref import sample
+
+    logits = np.array([[1.5, 0.0, -1.0, 2.0, 0.5, -3.0, 1.0, 0.25]], dtype=np.float32)
+    for temp in (1.0, 0.6):
+        ids = np.concatenate([sample(np.repeat(logits, 4000, 0), temp, 1234, c) for c in range(5)])
+        p = np.exp(logits[0] / temp - (logits[0] / temp).max())
+        p /= p.sum()
+        freq = np.bincount(ids, minlength=8) / ids.size
+        sigma = np.sqrt(p * (1 - p) / ids.size)
+        assert np.all(np.abs(freq - p) < 5 * sigma + 1e-3), (temp, freq, p)
