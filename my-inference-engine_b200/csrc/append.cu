@@ -113,16 +113,24 @@ __global__ void __launch_bounds__(256) append_rope_kernel(const AppendLaunch a, 
   *reinterpret_cast<__nv_bfloat162*>(dst + 64 + d) = ohi;
 }
 
-// One warp per (row, step token): 16 lanes per head, two heads per pass;
-// lane l owns dims 4l..4l+3 and their rotation partners 64+4l..64+4l+3
-// (8-byte accesses).  The token's cos/sin and pool slot are looked up once
-// for all its heads.  Same arithmetic per element as append_rope_kernel.
+// One warp per (row, step token, chunk of heads): 16 lanes per head, two
+// heads per pass; lane l owns dims 4l..4l+3 and their rotation partners
+// 64+4l..64+4l+3 (8-byte accesses).  The token's cos/sin and pool slot are
+// looked up once per warp.  A decode step has few tokens, so its heads are
+// split over up to `chunks` warps (one pass each at most) instead of one
+// warp walking all of them; and a warp issues the loads of up to kVecPass
+// passes before any of their stores, so the passes' memory latencies
+// overlap.  Same arithmetic per element as append_rope_kernel.
+constexpr int kVecPass = 4;
+
 __global__ void __launch_bounds__(256) append_rope_vec_kernel(const AppendLaunch a,
-                                                              int32_t num_blocks) {
+                                                              int32_t num_blocks, int32_t chunks) {
   pdl_trigger();
   pdl_wait();
-  const int64_t tok = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
+  const int64_t tok = w / chunks;
+  const int chunk = static_cast<int>(w % chunks);
   if (tok >= static_cast<int64_t>(a.batch) * a.seq_len_q) return;
   const int tt = static_cast<int>(tok % a.seq_len_q);
   const int b = static_cast<int>(tok / a.seq_len_q);
@@ -134,7 +142,13 @@ __global__ void __launch_bounds__(256) append_rope_vec_kernel(const AppendLaunch
   const bool rope = a.rope_cos != nullptr;
   const int nq = a.q_out ? a.num_q_heads : 0;
   const int per_tok = nq + 2 * a.num_kv_heads;
+  const int passes = (per_tok + 1) >> 1;
+  const int per_chunk = (passes + chunks - 1) / chunks;
+  const int p_begin = chunk * per_chunk, p_end = min(passes, p_begin + per_chunk);
+  if (p_begin >= p_end) return;
   const int d = 4 * (lane & 15);
+  // errors are reported by the warp of chunk 0 only (one report per token)
+  const bool reporter = lane == 0 && chunk == 0;
 
   // pool slot of this token (k and v heads), checked once
   int64_t slot = -1;
@@ -142,11 +156,11 @@ __global__ void __launch_bounds__(256) append_rope_vec_kernel(const AppendLaunch
     const int row = a.rows ? a.rows[b] : b;
     const int64_t bi = pos >> 4;
     if (pos < 0 || bi >= a.pitch) {
-      if (lane == 0) err.raise(PKV_DEVERR_POSITION);
+      if (reporter) err.raise(PKV_DEVERR_POSITION);
     } else {
       const int blk = a.tables[static_cast<int64_t>(row) * a.pitch + bi];
       if (blk < 0 || blk >= num_blocks) {
-        if (lane == 0) err.raise(PKV_DEVERR_BLOCK_ID);
+        if (reporter) err.raise(PKV_DEVERR_BLOCK_ID);
       } else {
         slot = static_cast<int64_t>(blk) * kBlockTokens + (pos & 15);
       }
@@ -157,7 +171,7 @@ __global__ void __launch_bounds__(256) append_rope_vec_kernel(const AppendLaunch
   __nv_bfloat16 c[8], sn[8];
   if (rope) {
     if (pos < 0 || pos >= a.rope_rows) {
-      if (lane == 0) err.raise(PKV_DEVERR_POSITION);
+      if (reporter) err.raise(PKV_DEVERR_POSITION);
       rope_ok = false;
     } else {
       const __nv_bfloat16* cr = static_cast<const __nv_bfloat16*>(a.rope_cos) + static_cast<int64_t>(pos) * kHeadDim;
@@ -169,44 +183,57 @@ __global__ void __launch_bounds__(256) append_rope_vec_kernel(const AppendLaunch
     }
   }
 
-  for (int which = lane >> 4; which < per_tok; which += 2) {
-    const __nv_bfloat16* src;
-    __nv_bfloat16* dst;
-    bool do_rope = rope;
-    if (which < nq) {
-      if (!rope_ok) continue;  // q needs its rotation
-      src = static_cast<const __nv_bfloat16*>(a.q) + b * a.q_sb + which * a.q_sh + tt * a.q_st;
-      dst = static_cast<__nv_bfloat16*>(a.q_out) + b * a.qo_sb + which * a.qo_sh + tt * a.qo_st;
-    } else {
-      const bool is_k = which < nq + a.num_kv_heads;
-      const int h = is_k ? which - nq : which - nq - a.num_kv_heads;
-      if (slot < 0) continue;
-      if (is_k) {
-        if (rope && !rope_ok) continue;
-        src = static_cast<const __nv_bfloat16*>(a.k) + b * a.k_sb + h * a.k_sh + tt * a.k_st;
-        dst = static_cast<__nv_bfloat16*>(a.k_pool) + (slot * a.num_kv_heads + h) * kHeadDim;
-      } else {
-        src = static_cast<const __nv_bfloat16*>(a.v) + b * a.v_sb + h * a.v_sh + tt * a.v_st;
-        dst = static_cast<__nv_bfloat16*>(a.v_pool) + (slot * a.num_kv_heads + h) * kHeadDim;
-        do_rope = false;
-      }
-    }
-    __nv_bfloat16 x[8];
-    *reinterpret_cast<uint2*>(x) = *reinterpret_cast<const uint2*>(src + d);
-    *reinterpret_cast<uint2*>(x + 4) = *reinterpret_cast<const uint2*>(src + 64 + d);
-    if (do_rope) {
-      __nv_bfloat16 o[8];
+  for (int p0 = p_begin; p0 < p_end; p0 += kVecPass) {
+    __nv_bfloat16 x[kVecPass][8];
+    __nv_bfloat16* dst[kVecPass];
+    bool do_rope[kVecPass];
+    // loads of every pass of this round first
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        // first half: x*cos + (-x2)*sin ; second half: x*cos + x1*sin
-        o[e] = rope1(x[e], c[e], __hneg(x[4 + e]), sn[e]);
-        o[4 + e] = rope1(x[4 + e], c[4 + e], x[e], sn[4 + e]);
+    for (int i = 0; i < kVecPass; ++i) {
+      dst[i] = nullptr;
+      do_rope[i] = rope;
+      const int which = 2 * (p0 + i) + (lane >> 4);
+      if (p0 + i >= p_end || which >= per_tok) continue;
+      const __nv_bfloat16* src;
+      if (which < nq) {
+        if (!rope_ok) continue;  // q needs its rotation
+        src = static_cast<const __nv_bfloat16*>(a.q) + b * a.q_sb + which * a.q_sh + tt * a.q_st;
+        dst[i] = static_cast<__nv_bfloat16*>(a.q_out) + b * a.qo_sb + which * a.qo_sh + tt * a.qo_st;
+      } else {
+        const bool is_k = which < nq + a.num_kv_heads;
+        const int h = is_k ? which - nq : which - nq - a.num_kv_heads;
+        if (slot < 0) continue;
+        if (is_k) {
+          if (rope && !rope_ok) continue;
+          src = static_cast<const __nv_bfloat16*>(a.k) + b * a.k_sb + h * a.k_sh + tt * a.k_st;
+          dst[i] = static_cast<__nv_bfloat16*>(a.k_pool) + (slot * a.num_kv_heads + h) * kHeadDim;
+        } else {
+          src = static_cast<const __nv_bfloat16*>(a.v) + b * a.v_sb + h * a.v_sh + tt * a.v_st;
+          dst[i] = static_cast<__nv_bfloat16*>(a.v_pool) + (slot * a.num_kv_heads + h) * kHeadDim;
+          do_rope[i] = false;
+        }
       }
-      *reinterpret_cast<uint2*>(dst + d) = *reinterpret_cast<const uint2*>(o);
-      *reinterpret_cast<uint2*>(dst + 64 + d) = *reinterpret_cast<const uint2*>(o + 4);
-    } else {
-      *reinterpret_cast<uint2*>(dst + d) = *reinterpret_cast<const uint2*>(x);
-      *reinterpret_cast<uint2*>(dst + 64 + d) = *reinterpret_cast<const uint2*>(x + 4);
+      *reinterpret_cast<uint2*>(x[i]) = *reinterpret_cast<const uint2*>(src + d);
+      *reinterpret_cast<uint2*>(x[i] + 4) = *reinterpret_cast<const uint2*>(src + 64 + d);
+    }
+    // then the rotations and stores
+#pragma unroll
+    for (int i = 0; i < kVecPass; ++i) {
+      if (!dst[i]) continue;
+      if (do_rope[i]) {
+        __nv_bfloat16 o[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          // first half: x*cos + (-x2)*sin ; second half: x*cos + x1*sin
+          o[e] = rope1(x[i][e], c[e], __hneg(x[i][4 + e]), sn[e]);
+          o[4 + e] = rope1(x[i][4 + e], c[4 + e], x[i][e], sn[4 + e]);
+        }
+        *reinterpret_cast<uint2*>(dst[i] + d) = *reinterpret_cast<const uint2*>(o);
+        *reinterpret_cast<uint2*>(dst[i] + 64 + d) = *reinterpret_cast<const uint2*>(o + 4);
+      } else {
+        *reinterpret_cast<uint2*>(dst[i] + d) = *reinterpret_cast<const uint2*>(x[i]);
+        *reinterpret_cast<uint2*>(dst[i] + 64 + d) = *reinterpret_cast<const uint2*>(x[i] + 4);
+      }
     }
   }
 }
@@ -229,10 +256,16 @@ bool vec8_ok(const AppendLaunch& a) {
 cudaError_t launch_append(const AppendLaunch& a, cudaStream_t stream) {
   const int32_t num_blocks_vec = static_cast<int32_t>(a.num_slots / kBlockTokens);
   if (vec8_ok(a)) {
-    const int64_t warps = static_cast<int64_t>(a.batch) * a.seq_len_q;
-    if (warps == 0) return cudaSuccess;
+    const int64_t tokens = static_cast<int64_t>(a.batch) * a.seq_len_q;
+    if (tokens == 0) return cudaSuccess;
+    // ~4096 warps in flight: a prefill keeps one or two warps per token, a
+    // decode step spreads each token's heads over up to one warp per pass
+    const int passes = ((a.q_out ? a.num_q_heads : 0) + 2 * a.num_kv_heads + 1) / 2;
+    const int64_t want = (4096 + tokens - 1) / tokens;
+    const int32_t chunks = static_cast<int32_t>(want < passes ? want : passes);
+    const int64_t warps = tokens * (chunks > 0 ? chunks : 1);
     return launch_k(append_rope_vec_kernel, dim3(static_cast<unsigned>((warps * 32 + 255) / 256)),
-                    dim3(256), 0, stream, a, num_blocks_vec);
+                    dim3(256), 0, stream, a, num_blocks_vec, chunks > 0 ? chunks : 1);
   }
   const int per_tok = (a.q_out ? a.num_q_heads : 0) + 2 * a.num_kv_heads;
   const int64_t warps = static_cast<int64_t>(a.batch) * a.seq_len_q * per_tok;
