@@ -89,6 +89,9 @@ def parse():
                     help="causal prefill attention on dense K/V (12 q / 2 kv heads, d 128) "
                          "per shape and per kernel (PKV_PREFILL_KERNEL one, pair), 20 "
                          "launches per CUDA graph")
+    ap.add_argument("--linear-one", type=str, default=None, metavar="OP:ROWS",
+                    help="one fused projection (qkv, o, gate_up or down) at ROWS rows, "
+                         "5 eager calls (a small case for an ncu capture of linear_tc_kernel)")
     ap.add_argument("--profile-range", action="store_true",
                     help="with --decode-step / --prefill-step: one eager step inside "
                          "cudaProfilerStart/Stop "
@@ -727,6 +730,43 @@ def linear_sweep(rows_list, device):
         paired = None
 
 
+def linear_one(spec, device):
+    """5 eager calls of one fused projection entry at ROWS rows (layer shapes
+    of Qwen2.5-1.5B), then the mean time of 20 more; prints one JSON line."""
+    import pagedkv
+
+    op, rows = spec.split(":")
+    rows = int(rows)
+    n, k = {"qkv": (2048, 1536), "o": (1536, 1536), "gate_up": (17920, 1536),
+            "down": (1536, 8960)}[op]
+    g = torch.Generator(device=device).manual_seed(rows)
+    w = (0.02 * torch.randn(n, k, device=device, generator=g)).to(torch.bfloat16)
+    x = torch.randn(rows, k, device=device, generator=g).to(torch.bfloat16)
+    resid = torch.randn(rows, 1536, device=device, generator=g).to(torch.bfloat16)
+    nw = torch.ones(1536, device=device, dtype=torch.bfloat16)
+    h = torch.empty(rows, 1536, device=device, dtype=torch.bfloat16)
+    if op == "gate_up":
+        w = pagedkv.PairedGateUp(w)
+        act = torch.empty(rows, n // 2, device=device, dtype=torch.bfloat16)
+        call = lambda: pagedkv.linear_silu_mul(x, w, out=act)  # noqa: E731
+    elif op == "qkv":
+        y = torch.empty(rows, n, device=device, dtype=torch.bfloat16)
+        call = lambda: pagedkv.linear(x, w, out=y)  # noqa: E731
+    else:
+        call = lambda: pagedkv.linear_add_rmsnorm(x, w, resid, nw, 1e-6, out=h)  # noqa: E731
+    for _ in range(5):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(20):
+        call()
+    e1.record()
+    e1.synchronize()
+    print(json.dumps({"diag": "linear_one", "op": op, "rows": rows, "n": n, "k": k,
+                      "eager_us_per_call": round(e0.elapsed_time(e1) / 20 * 1e3, 2)}), flush=True)
+
+
 def decode_step_diag(spec, device, profile_range=False):
     """Whole-model decode step (random-init Qwen2.5-1.5B, B rows of CTX
     tokens of history) replayed from a CUDA graph, under the skinny-GEMM
@@ -882,9 +922,12 @@ def main():
               "heads": [HQ, HKV, D], "l2": "inputs larger than L2 (KV read per step >> 126 MB)",
               "parallelism": f"replicas x{args.gpus} (request-sharded, no collective)"}
 
-    if args.linear_sweep or args.decode_step or args.prefill_step or args.prefill_sweep:
+    if (args.linear_sweep or args.decode_step or args.prefill_step or args.prefill_sweep
+            or args.linear_one):
         dev = torch.device("cuda", local)
         torch.cuda.set_device(dev)
+        if args.linear_one:
+            linear_one(args.linear_one, dev)
         if args.prefill_sweep:
             prefill_sweep([tuple(int(v) for v in x.split("x")) for x in args.prefill_sweep.split(",")],
                           dev)
