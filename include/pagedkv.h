@@ -27,6 +27,13 @@
  *  - Every call is asynchronous on `stream` and returns a pkv_status.  A
  *    nonzero status means nothing was launched.  Memory is owned by the
  *    caller; the library never allocates or frees device memory.
+ *  - Kernels are launched with programmatic dependent launch: a kernel may
+ *    start while the previous kernel on the stream drains and waits for it
+ *    before touching activations, tables or lengths.  The weights of the
+ *    pkv_linear* entries are constant operands and are read before that
+ *    wait, so they must not be written by the kernel right before the call
+ *    on the same stream.
+ *    PKV_PDL=0 in the environment launches without it.
  *  - err_flag (nullable, device int32) receives PKV_DEVERR_* bits when a
  *    kernel meets an out-of-range block id / position: the bad access is
  *    skipped (block 0 is read instead) and the flag is OR-ed, never a fault.
