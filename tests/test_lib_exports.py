@@ -103,3 +103,44 @@ def test_linear_workspace_plan_and_validation_without_a_gpu():
     assert st == 2  # inter not a multiple of 64
     st = L.pkv_linear(16, 1536, 16, 1536, 2, None, 16, 17920, 1536, 16, 17920, None, 0, None, None)
     assert st == 1  # the paired gate/up layout is only for pkv_linear_silu_mul
+
+
+def test_sample_validation_without_a_gpu():
+    """pkv_sample checks its arguments before any CUDA call."""
+    import pagedkv
+
+    L = pagedkv.lib()
+    out = 16
+    # dtype must be 0 (bf16) or 1 (f32)
+    assert L.pkv_sample(16, 1000, 4, 1000, 2, 1.0, 1, 0, out, None) == 2
+    # temperature must be positive and finite
+    assert L.pkv_sample(16, 1000, 4, 1000, 0, 0.0, 1, 0, out, None) == 1
+    assert L.pkv_sample(16, 1000, 4, 1000, 0, -1.0, 1, 0, out, None) == 1
+    assert L.pkv_sample(16, 1000, 4, 1000, 0, float("inf"), 1, 0, out, None) == 1
+    assert L.pkv_sample(16, 1000, 4, 1000, 0, float("nan"), 1, 0, out, None) == 1
+    # ld shorter than the vocabulary, too many rows, null pointers
+    assert L.pkv_sample(16, 999, 4, 1000, 0, 1.0, 1, 0, out, None) == 1
+    assert L.pkv_sample(16, 1000, 70000, 1000, 0, 1.0, 1, 0, out, None) == 1
+    assert L.pkv_sample(None, 1000, 4, 1000, 0, 1.0, 1, 0, out, None) == 1
+    assert L.pkv_sample(16, 1000, 4, 1000, 0, 1.0, 1, 0, None, None) == 1
+    # f32 logits not 4-byte aligned
+    assert L.pkv_sample(18, 1000, 4, 1000, 1, 1.0, 1, 0, out, None) == 3
+    # zero rows: nothing to launch
+    assert L.pkv_sample(16, 1000, 0, 1000, 0, 1.0, 1, 0, out, None) == 0
+
+
+def test_chat_reads_sampled_ids_and_raises_on_unsampled_rows():
+    """Host half of chat's sampling: ids come back as Python ints; a row the
+    device sampler marked -1 (no finite logit) raises as torch.multinomial
+    does on such a row (reference chat.py:103-107)."""
+    import pytest
+    import torch
+
+    import chat
+
+    assert chat._read_ids(torch.tensor([3, 0, 7], dtype=torch.int32)) == [3, 0, 7]
+    assert chat._read_ids(torch.tensor([], dtype=torch.int32)) == []
+    with pytest.raises(RuntimeError, match="probability tensor"):
+        chat._read_ids(torch.tensor([3, -1], dtype=torch.int32))
+    tok = chat._PendingToken(torch.tensor([42], dtype=torch.int32))
+    assert tok.get() == 42
