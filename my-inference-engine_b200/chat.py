@@ -15,10 +15,13 @@ same module-level names (the reference's benchmark monkey-patches `_admit`,
   * `_finish` trims unused reserved blocks (chat.py:194-211); `Chat.release`
     frees a chat's blocks from a request thread (chat.py:325-330).
 What changes is underneath: the cache's block tables live on the device, the
-decode step can replay a captured CUDA graph (model.DecodeGraphs), and
-nothing is allocated or started at import -- `KV_CACHE` is created on first
-use and the worker thread on the first message (`init()` sets both up
-explicitly).
+decode step can replay a captured CUDA graph (model.DecodeGraphs), sampling
+is one device kernel (pagedkv.sample: the same softmax(logits / T)
+distribution, drawn by Gumbel-max), a prompt's first token is read back only
+when the decode tick reaches its job (so the host work for the jobs ahead of
+it overlaps the prefill), and nothing is allocated or started at import --
+`KV_CACHE` is created on first use and the worker thread on the first
+message (`init()` sets both up explicitly).
 
 One opt-in departure (off by default, so the decisions above stay the
 reference's): with MIXED_PREFILL_MIN_TOKENS set, a tick that admits a prompt
