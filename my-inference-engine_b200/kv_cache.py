@@ -192,6 +192,21 @@ class BlockTables:
         self._pending = {}
         return pend
 
+    def take_pending_flat(self):
+        """The queued entries as one int64 numpy array [2, n]: flat table
+        index (row * table_pitch + col) and block id, in queue order (one
+        entry per cell, the last write).  None when nothing is queued."""
+        pend, self._pending = self._pending, {}
+        n = len(pend)
+        if not n:
+            return None
+        rc = np.fromiter(itertools.chain.from_iterable(pend.keys()), dtype=np.int64, count=2 * n)
+        out = np.empty((2, n), dtype=np.int64)
+        np.multiply(rc[0::2], self.table_pitch, out=out[0])
+        out[0] += rc[1::2]
+        out[1] = np.fromiter(pend.values(), dtype=np.int64, count=n)
+        return out
+
     def step_rows(self, seqs, T):
         """Host part of prepare(): reserve blocks, return (starts, rows)."""
         starts = [self._lengths[s] for s in seqs]
@@ -228,16 +243,9 @@ class KVCache(BlockTables):
     # ---- device side ----
     def flush_tables(self):
         """Upload queued (row, col, block) entries in one copy + one scatter."""
-        pend, self._pending = self._pending, {}
-        if not pend:
+        host = self.take_pending_flat()
+        if host is None:
             return
-        n = len(pend)
-        # flat table index and block id per entry, built on the host in numpy
-        rc = np.fromiter(itertools.chain.from_iterable(pend.keys()), dtype=np.int64, count=2 * n)
-        host = np.empty((2, n), dtype=np.int64)
-        np.multiply(rc[0::2], self.table_pitch, out=host[0])
-        host[0] += rc[1::2]
-        host[1] = np.fromiter(pend.values(), dtype=np.int64, count=n)
         d = torch.from_numpy(host).pin_memory().to(self.device, non_blocking=True)
         self.block_tables.view(-1).index_copy_(0, d[0], d[1].to(torch.int32))
 

@@ -166,3 +166,31 @@ def test_oracle_model_reproduces_reference_greedy_ids(golden):
         for r in range(2):
             ids[r].append(nxt[r])
     assert ids == fx["ids"]
+
+
+def test_pending_flat_arrays_match_pending_entries():
+    """The flat [2, n] upload array (what KVCache.flush_tables copies to the
+    device) holds exactly take_pending()'s cells: row * pitch + col and the
+    block id, last write winning."""
+    import numpy as np
+
+    def ops(bt):
+        a = bt.alloc()
+        bt.ensure_capacity(a, 70)  # 5 blocks
+        b = bt.alloc()
+        bt.ensure_capacity(b, 33)  # 3 blocks
+        bt.free(a)
+        c = bt.alloc()  # reuses a's row before any flush: its cells are rewritten
+        bt.ensure_capacity(c, 20)
+        bt.ensure_capacity(b, 64)
+
+    ref, flat = BlockTables(32, 16, max_seqs=4, max_blocks_per_seq=8), \
+        BlockTables(32, 16, max_seqs=4, max_blocks_per_seq=8)
+    ops(ref)
+    ops(flat)
+    want = {r * ref.table_pitch + c: blk for r, c, blk in ref.take_pending()}
+    got = flat.take_pending_flat()
+    assert got.dtype == np.int64 and got.shape == (2, len(want))
+    assert dict(zip(got[0].tolist(), got[1].tolist())) == want
+    assert flat.take_pending_flat() is None  # the queue is empty after a take
+    assert flat._block_tables == ref._block_tables and flat._free_blocks == ref._free_blocks
