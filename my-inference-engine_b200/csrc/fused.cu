@@ -145,16 +145,19 @@ __global__ void __launch_bounds__(kNormThreads)
   }
 }
 
-__global__ void __launch_bounds__(256)
+// grid (rows, column chunks of kSiluThreads x 8 elements): the row and
+// column come straight from the block index, no integer division per thread
+constexpr int kSiluThreads = 128;
+
+__global__ void __launch_bounds__(kSiluThreads)
     silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int64_t gu_stride,
                     __nv_bfloat16* __restrict__ out, int64_t o_stride, int rows, int inter) {
   pdl_trigger();
   pdl_wait();
-  const int per_row = inter / 8;
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= static_cast<int64_t>(rows) * per_row) return;
-  const int row = static_cast<int>(i / per_row);
-  const int col = static_cast<int>(i % per_row) * 8;
+  const int row = blockIdx.x;
+  const int j = blockIdx.y * kSiluThreads + threadIdx.x;
+  if (row >= rows || j >= inter / 8) return;
+  const int col = j * 8;
   const uint4 gv = *reinterpret_cast<const uint4*>(gu + row * gu_stride + col);
   const uint4 uv = *reinterpret_cast<const uint4*>(gu + row * gu_stride + inter + col);
   const __nv_bfloat16* gp = reinterpret_cast<const __nv_bfloat16*>(&gv);
@@ -210,10 +213,12 @@ cudaError_t launch_add_rmsnorm(const NormLaunch& p, cudaStream_t stream) {
 
 cudaError_t launch_silu_mul(const void* gu, int64_t gu_stride, void* out, int64_t o_stride,
                             int32_t rows, int32_t inter, cudaStream_t stream) {
-  const int64_t n = static_cast<int64_t>(rows) * (inter / 8);
-  if (n == 0) return cudaSuccess;
-  return launch_k(silu_mul_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0,
-                  stream, static_cast<const __nv_bfloat16*>(gu), gu_stride,
+  const int per_row = inter / 8;
+  if (rows == 0 || per_row == 0) return cudaSuccess;
+  const dim3 grid(static_cast<unsigned>(rows),
+                  static_cast<unsigned>((per_row + kSiluThreads - 1) / kSiluThreads));
+  return launch_k(silu_mul_kernel, grid, dim3(kSiluThreads), 0, stream,
+                  static_cast<const __nv_bfloat16*>(gu), gu_stride,
                   static_cast<__nv_bfloat16*>(out), o_stride, static_cast<int>(rows),
                   static_cast<int>(inter));
 }
