@@ -1,7 +1,8 @@
 """Generate the golden fixtures in this directory by running the REFERENCE
 implementation (shubhav1/my-inference-engine, pure Python/PyTorch) on the CPU.
 
-    python tests/golden/make_golden.py [--reference /path/to/reference]
+    python tests/golden/make_golden.py --reference /path/to/reference
+    (or PKV_REFERENCE_DIR=/path/to/reference python tests/golden/make_golden.py)
 
 Run only where the reference checkout exists (it is never read by tests, the
 bench or smoke(); the fixtures it writes are what travels).  Every fixture
@@ -33,6 +34,7 @@ from __future__ import annotations
 import argparse
 import hashlib
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -328,7 +330,9 @@ def gen_scheduler_trace(reference):
 def main():
     sys.path.insert(0, str(REPO))
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    env = os.environ.get("PKV_REFERENCE_DIR")
+    ap.add_argument("--reference", default=env, required=env is None,
+                    help="reference checkout (or set PKV_REFERENCE_DIR)")
     ap.add_argument("--only", default=None)
     a = ap.parse_args()
     sys.path.insert(0, a.reference)
