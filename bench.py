@@ -92,6 +92,9 @@ def parse():
     ap.add_argument("--linear-one", type=str, default=None, metavar="OP:ROWS",
                     help="one fused projection (qkv, o, gate_up or down) at ROWS rows, "
                          "5 eager calls (a small case for an ncu capture of linear_tc_kernel)")
+    ap.add_argument("--sample-one", type=str, default=None, metavar="ROWS,...",
+                    help="pkv_sample on [ROWS, 151936] bf16 logits: device time per call "
+                         "(CUDA graph of 20 calls) and GB/s of logits read")
     ap.add_argument("--profile-range", action="store_true",
                     help="with --decode-step / --prefill-step: one eager step inside "
                          "cudaProfilerStart/Stop "
@@ -767,6 +770,44 @@ def linear_one(spec, device):
                       "eager_us_per_call": round(e0.elapsed_time(e1) / 20 * 1e3, 2)}), flush=True)
 
 
+def sample_one(spec, device):
+    """Device time of pkv_sample (the engine's sampler) on the model's
+    vocabulary: 20 calls per CUDA graph, median of 5 replays; bytes = the
+    bf16 logits read once."""
+    import pagedkv
+
+    peaks, src = measured_peaks()
+    peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
+    vocab = 151936
+    for rows in (int(r) for r in spec.split(",")):
+        g = torch.Generator(device=device).manual_seed(rows)
+        logits = torch.randn(rows, vocab, device=device, generator=g).to(torch.bfloat16)
+        out = torch.empty(rows, dtype=torch.int32, device=device)
+        for c in range(3):
+            pagedkv.sample(logits, 1.0, seed=1, call=c, out=out)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for c in range(20):
+                pagedkv.sample(logits, 1.0, seed=1, call=c, out=out)
+        graph.replay()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            graph.replay()
+            e1.record()
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3 / 20)
+        us = statistics.median(ts)
+        gbs = rows * vocab * 2 / (us * 1e-6) / 1e9
+        print(json.dumps({"diag": "sample_one", "rows": rows, "vocab": vocab,
+                          "us_per_call": round(us, 2), "logits_gbs": round(gbs, 1),
+                          "frac_of_hbm": round(gbs / peak, 3), "peak_source": src}), flush=True)
+        del graph
+
+
 def decode_step_diag(spec, device, profile_range=False):
     """Whole-model decode step (random-init Qwen2.5-1.5B, B rows of CTX
     tokens of history) replayed from a CUDA graph, under the skinny-GEMM
@@ -923,9 +964,11 @@ def main():
               "parallelism": f"replicas x{args.gpus} (request-sharded, no collective)"}
 
     if (args.linear_sweep or args.decode_step or args.prefill_step or args.prefill_sweep
-            or args.linear_one):
+            or args.linear_one or args.sample_one):
         dev = torch.device("cuda", local)
         torch.cuda.set_device(dev)
+        if args.sample_one:
+            sample_one(args.sample_one, dev)
         if args.linear_one:
             linear_one(args.linear_one, dev)
         if args.prefill_sweep:
