@@ -419,6 +419,25 @@ class Qwen2ForCausalLM(torch.nn.Module):
         return self._prefill_graphs[id(cache)]
 
 
+def _pinned_free(events, key):
+    """Wait until the last copy out of bucket `key`'s pinned input buffer has
+    run, so the host can refill it.  Without a sampling sync between two
+    steps (two prompts admitted in one scheduler tick, or back-to-back
+    calls) the host runs ahead of the stream; usually the copy is long done
+    and this returns at once."""
+    ev = events.get(key)
+    if ev is not None:
+        ev.synchronize()
+
+
+def _pinned_used(events, key):
+    """Mark the copies just enqueued out of bucket `key`'s pinned buffer."""
+    ev = events.get(key)
+    if ev is None:
+        ev = events[key] = torch.cuda.Event()
+    ev.record()
+
+
 def _buckets(max_batch):
     b, out = 1, []
     while b < max_batch:
@@ -449,6 +468,7 @@ class DecodeGraphs:
         self.graphs = {}
         self.pool = torch.cuda.graph_pool_handle()
         self.capacity = cache.table_pitch * cache.block_size
+        self._copied = {}  # bucket -> event after the last copy out of its pinned inputs
 
     def covers(self, B):
         return 0 < B <= self.max_batch
@@ -483,6 +503,7 @@ class DecodeGraphs:
         g, ins, host, logits = self.graphs.get(Bp) or self._capture(Bp)
         starts, rows = self.cache.step_rows(seqs, 1)
         self.cache.flush_tables()
+        _pinned_free(self._copied, Bp)
         h = host.numpy()  # the pinned buffer, filled in place (no per-row torch ops)
         if not input_ids.is_cuda:
             h[0, :B] = input_ids.view(-1).numpy()
@@ -495,6 +516,7 @@ class DecodeGraphs:
             h[2, B:] = -1
             h[3, B:] = 0
         ins.copy_(host, non_blocking=True)
+        _pinned_used(self._copied, Bp)
         if input_ids.is_cuda:  # device ids: a device-side copy, no host sync
             ins[0, :B].copy_(input_ids.view(-1))
         g.replay()
@@ -526,6 +548,7 @@ class PrefillGraphs:
         self.buckets.append(top)
         self.graphs = {}
         self.pool = torch.cuda.graph_pool_handle()
+        self._copied = {}  # bucket -> event after the last copy out of its pinned inputs
 
     def covers(self, B, T):
         return B == 1 and 1 < T <= self.buckets[-1]
@@ -558,6 +581,7 @@ class PrefillGraphs:
         g, ids, meta, host, logits = self.graphs.get(Tp) or self._capture(Tp)
         starts, rows = self.cache.step_rows(seqs, T)
         self.cache.flush_tables()
+        _pinned_free(self._copied, Tp)
         h = host.numpy()
         h[:4] = (rows[0], starts[0], starts[0] + T, T)
         if not input_ids.is_cuda:
@@ -567,6 +591,7 @@ class PrefillGraphs:
             ids[0, :T].copy_(input_ids.view(-1))
         else:
             ids.view(-1).copy_(host[4:4 + Tp], non_blocking=True)
+        _pinned_used(self._copied, Tp)
         g.replay()
         self.cache.advance(seqs, T)
         return logits[:, 0]
