@@ -956,8 +956,11 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     metric = "paged decode-attn HBM GB/s"
-    config = {"workload": "config3: 256 rows, ctx U[2048,8192], ~150 GB bf16 pool, 28 layers "
-                          "of RoPE+append + paged decode per step",
+    default_c3 = (args.seqs, args.ctx_min, args.ctx_max, args.pool_gb, args.layers) == \
+        (256, 2048, 8192, 150.0, L)
+    config = {"workload": f"{'config3' if default_c3 else 'config3-shaped'}: {args.seqs} rows, "
+                          f"ctx U[{args.ctx_min},{args.ctx_max}], ~{args.pool_gb:g} GB bf16 pool, "
+                          f"{args.layers} layers of RoPE+append + paged decode per step",
               "seqs": args.seqs, "ctx_range": [args.ctx_min, args.ctx_max],
               "pool_gb": args.pool_gb, "layers": args.layers, "block_size": 16,
               "heads": [HQ, HKV, D], "l2": "inputs larger than L2 (KV read per step >> 126 MB)",
