@@ -23,6 +23,11 @@ it overlaps the prefill), and nothing is allocated or started at import --
 `KV_CACHE` is created on first use and the worker thread on the first
 message (`init()` sets both up explicitly).
 
+Not provided, being outside the attention path: weight loading from a
+checkpoint directory and the single-sequence `generate` loop of the
+reference (chat.py:39-46, :72-88).  A caller builds the model itself
+(model.Qwen2ForCausalLM + load_state_dict) and drives chats through `Chat`.
+
 One opt-in departure (off by default, so the decisions above stay the
 reference's): with MIXED_PREFILL_MIN_TOKENS set, a tick that admits a prompt
 of at least that many tokens while other jobs are decoding runs the prompt
@@ -35,6 +40,7 @@ from __future__ import annotations
 
 import array
 import queue
+import sys
 import threading
 import time
 
@@ -43,9 +49,7 @@ import torch.nn.functional as F
 
 import pagedkv
 from kv_cache import KVCache
-from model import Qwen2ForCausalLM
 
-MODEL_PATH = "./qwen2.5-1.5b"
 MAX_REPLY_TOKENS = 512  # safety net against a reply that never hits EOS
 TEMPERATURE = 1
 
@@ -95,56 +99,25 @@ def init(kv_cache=None, start_worker=True):
     return _kv_cache
 
 
-def load_qwen(model_path):
-    from safetensors.torch import load_file
-
-    model = Qwen2ForCausalLM()
-    state_dict = load_file(f"{model_path}/model.safetensors")
-    state_dict = {k.removeprefix("model."): v for k, v in state_dict.items()}
-    model.load_state_dict(state_dict)
-    model.eval()
-    return model.to(DEVICE, dtype=DTYPE)
-
-
 STOP_SEQUENCES = ["\nUser:", "\nUser"]
 
 
-def _overlap_len(text, patterns):
-    """Length of the longest suffix of `text` that could still grow into any of `patterns`."""
-    best = 0
-    for pattern in patterns:
-        for k in range(min(len(text), len(pattern) - 1), 0, -1):
-            if text.endswith(pattern[:k]):
-                best = max(best, k)
-                break
-    return best
-
-
-def _find_stop(text, patterns):
-    """The earliest-starting stop pattern found in `text`, or None."""
-    best = None
-    for pattern in patterns:
-        i = text.find(pattern)
-        if i != -1 and (best is None or i < text.find(best)):
-            best = pattern
-    return best
-
-
-def generate(model, new_ids, eos_id, max_tokens=MAX_REPLY_TOKENS):
-    """Single-sequence generation loop with its own private cache (chat.py:72-88)."""
-    cache = KVCache(MAX_SEQ_LEN // BLOCK_SIZE, BLOCK_SIZE, DEVICE, dtype=next(model.parameters()).dtype)
-    seq = cache.alloc()
-    next_id = new_ids
-    is_first = True
-    for _ in range(max_tokens):
-        with torch.no_grad():
-            input_id = torch.tensor([next_id] if is_first else [[next_id]], device=DEVICE)
-            is_first = False
-            logits = model(input_id, cache, [seq])
-        next_id = _sample(logits[:, -1])[0]
-        yield next_id
-        if next_id == eos_id:
-            break
+def _hold_back(text, patterns):
+    """Split a reply's undelivered text for streaming: returns (ready, held,
+    stopped).  If any stop pattern occurs, everything before its earliest
+    occurrence is ready and the reply stops.  Otherwise the longest tail of
+    `text` that is a proper prefix of some pattern (it may still grow into a
+    stop) is held back and the rest is ready.  Same pieces as the reference's
+    streaming (chat.py:51-69, :281-294)."""
+    hits = [i for i in (text.find(p) for p in patterns if p) if i >= 0]
+    if hits:
+        return text[:min(hits)], "", True
+    longest = max((len(p) for p in patterns), default=1) - 1
+    for k in range(min(longest, len(text)), 0, -1):
+        tail = text[len(text) - k:]
+        if any(len(p) > k and p.startswith(tail) for p in patterns):
+            return text[:len(text) - k], tail, False
+    return text, "", False
 
 
 class _Job:
@@ -378,19 +351,13 @@ def _process(active):
             _finish(job)
             continue
 
-        job.buffer += chat.tokenizer.decode([token_id])
-        stop = _find_stop(job.buffer, STOP_SEQUENCES)
-        if stop is not None:
-            job.buffer = job.buffer.split(stop)[0]
-            if job.buffer:
-                _emit(job, job.buffer)
+        ready, job.buffer, stopped = _hold_back(job.buffer + chat.tokenizer.decode([token_id]),
+                                                STOP_SEQUENCES)
+        if ready:
+            _emit(job, ready)
+        if stopped:
             _finish(job)
             continue
-
-        overlap = _overlap_len(job.buffer, STOP_SEQUENCES)
-        release, job.buffer = job.buffer[:len(job.buffer) - overlap], job.buffer[len(job.buffer) - overlap:]
-        if release:
-            _emit(job, release)
 
         job.steps += 1
         if job.steps >= MAX_REPLY_TOKENS:
@@ -435,21 +402,28 @@ def _process(active):
 
 
 class Chat:
+    """One conversation: its token ids, its sequence in the shared cache (None
+    while evicted) and its messages.  Same attributes and methods as the
+    reference's Chat (chat.py:314-377), which the scheduler and the
+    reference's benchmark use."""
+
     def __init__(self, tokenizer):
         self.tokenizer = tokenizer
-        self.ids = []
-        self.seq = None
-        self.messages = []
-        self.pending = []
-        self.in_progress = None
-        self.listeners = []
+        self.ids = []          # every token of the conversation so far
+        self.seq = None        # KV-cache sequence id, None when not resident
+        self.messages = []     # finished (role, text) pairs
+        self.pending = []      # submitted user texts not yet admitted
+        self.in_progress = None  # the reply being streamed, if any
+        self.listeners = []    # queues receiving the streamed reply pieces
         self.eos_id = tokenizer.encoder["<|endoftext|>"]
 
     def release(self):
-        """Free this chat's KV-cache blocks, if it holds any."""
+        """Give this chat's blocks back to the pool (a later message prefills
+        the whole history again)."""
         with _cache_lock:
-            if self.seq is not None:
-                _evict(self)
+            if self.seq is None:
+                return
+            _evict(self)
 
     def submit(self, model, text):
         """Queue a message without starting the worker thread; returns the
@@ -460,34 +434,34 @@ class Chat:
         return out_queue
 
     def send_stream(self, model, text):
-        """Yield decoded reply pieces as they are generated (chat.py:332-348)."""
-        out_queue = self.submit(model, text)
+        """Yield the reply's pieces as the worker produces them."""
+        pieces = self.submit(model, text)
         _ensure_worker()
-        while True:
-            piece = out_queue.get()
-            if piece is None:
-                break
+        for piece in iter(pieces.get, None):
             yield piece
 
     def all_messages(self):
-        result = list(self.messages)
-        if self.in_progress is not None:
-            result.append(("assistant", self.in_progress))
-        result.extend(("user", text) for text in self.pending)
-        return result
+        """Finished messages, then the reply in progress, then queued texts."""
+        live = [] if self.in_progress is None else [("assistant", self.in_progress)]
+        return [*self.messages, *live, *[("user", t) for t in self.pending]]
 
     def watch(self):
+        """(text so far, queue of further pieces) of the reply in progress,
+        or (None, None) when none is."""
         if self.in_progress is None:
             return None, None
-        q = queue.Queue()
-        self.listeners.append(q)
-        return self.in_progress, q
+        listener = queue.Queue()
+        self.listeners.append(listener)
+        return self.in_progress, listener
 
     def send(self, model, text):
+        """Blocking helper: stream the reply to stdout, return its text."""
         for piece in self.send_stream(model, text):
-            print(piece, end="", flush=True)
-        print()
+            sys.stdout.write(piece)
+            sys.stdout.flush()
+        sys.stdout.write("\n")
         return self.messages[-1][1]
 
     def transcript(self):
+        """The whole conversation decoded from its token ids."""
         return self.tokenizer.decode(self.ids)
