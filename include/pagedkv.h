@@ -110,6 +110,17 @@ size_t pkv_decode_workspace_size(int32_t batch, int32_t num_q_heads,
                                  int32_t num_kv_heads, int32_t max_kv_len);
 
 /*
+ * The split-K plan pkv_paged_decode takes for these sizes, written to
+ * plan[0..3] = {blocks_per_part, min_blocks_per_part, max_parts (grid.x),
+ * sub_groups}.  Host-only arithmetic (no GPU, no launch); lets a caller or a
+ * test see which partition sizing a launch of this shape uses.  Diagnostic,
+ * no counterpart in the reference (its kernel has no split-K,
+ * kernels/fa2.py:192-207).  Returns PKV_ERR_INVALID for invalid sizes.
+ */
+int pkv_decode_plan(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                    int32_t max_kv_len, int32_t* plan);
+
+/*
  * Paged decode attention (one query token per row) reading K/V blocks in
  * place through the block table: no dense gather copy.
  *

@@ -293,6 +293,19 @@ size_t pkv_decode_workspace_size(int32_t batch, int32_t num_q_heads, int32_t num
   return pkv::plan_decode(batch, num_q_heads, num_kv_heads, max_kv_len).workspace_bytes;
 }
 
+int pkv_decode_plan(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t max_kv_len,
+                    int32_t* plan) {
+  if (!plan || batch <= 0 || num_kv_heads <= 0 || num_q_heads <= 0 || max_kv_len < 0 ||
+      num_q_heads % num_kv_heads != 0)
+    return fail(PKV_ERR_INVALID, "decode_plan: bad sizes");
+  const pkv::DecodePlan pl = pkv::plan_decode(batch, num_q_heads, num_kv_heads, max_kv_len);
+  plan[0] = pl.blocks_per_part;
+  plan[1] = pl.min_blocks_per_part;
+  plan[2] = pl.max_parts;
+  plan[3] = pl.sub_groups;
+  return ok();
+}
+
 static int decode_common(const pkv::DecodeLaunch& a, const pkv::KVSource& src, cudaStream_t stream) {
   const pkv::DecodePlan plan = pkv::plan_decode(a.batch, a.num_q_heads, a.num_kv_heads, a.max_kv_len);
   if (static_cast<int64_t>(a.batch) * a.num_kv_heads * plan.sub_groups > pkv::decode_max_units())

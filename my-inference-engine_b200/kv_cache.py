@@ -217,6 +217,33 @@ class BlockTables:
         return starts, [self._row_of[s] for s in seqs]
 
 
+class _PinnedUpload:
+    """One persistent pinned staging buffer for small host-to-device uploads
+    (block-table deltas, per-step row vectors): no pinned allocation per
+    step.  A CUDA event recorded after each copy guards the buffer, so the
+    host never refills it while the previous copy is still queued (the host
+    can run ahead of the stream when no sync separates two steps)."""
+
+    def __init__(self, dtype):
+        self.dtype = dtype
+        self.buf = None
+        self.done = None
+
+    def send(self, flat: np.ndarray, device) -> torch.Tensor:
+        n = flat.shape[0]
+        if self.done is not None:
+            self.done.synchronize()  # usually long complete: returns at once
+        if self.buf is None or self.buf.numel() < n:
+            cap = max(n, 2 * (self.buf.numel() if self.buf is not None else 0), 1024)
+            self.buf = torch.empty(cap, dtype=self.dtype, pin_memory=True)
+        self.buf.numpy()[:n] = flat
+        out = self.buf[:n].to(device, non_blocking=True)
+        if self.done is None:
+            self.done = torch.cuda.Event()
+        self.done.record()
+        return out
+
+
 class KVCache(BlockTables):
     """Paged KV cache shared by every concurrently active sequence.
 
@@ -227,18 +254,22 @@ class KVCache(BlockTables):
     """
 
     def __init__(self, num_blocks, block_size, device, dtype, max_seqs=None,
-                 max_blocks_per_seq=None):
+                 max_blocks_per_seq=None, num_layers=NUM_LAYERS):
         device = torch.device(device)
         assert device.type == "cuda", "KVCache needs a CUDA device (no CPU fallback)"
         assert block_size == BLOCK_SIZE, f"block_size must be {BLOCK_SIZE}"
         assert dtype == torch.bfloat16, "the paged kernels store bf16 K/V"
         super().__init__(num_blocks, block_size, max_seqs, max_blocks_per_seq)
-        self.buf = torch.zeros(NUM_LAYERS, 2, num_blocks * block_size, NUM_KV_HEADS, HEAD_DIM,
+        # num_layers < 28 only for single-layer attention workloads (kernel
+        # tests and benchmarks); the model needs the full pool
+        self.buf = torch.zeros(num_layers, 2, num_blocks * block_size, NUM_KV_HEADS, HEAD_DIM,
                                device=device, dtype=dtype)
         self.device = device
         self.block_tables = torch.zeros(self.max_seqs, self.table_pitch, dtype=torch.int32,
                                         device=device)
         self.err_flag = torch.zeros(1, dtype=torch.int32, device=device)
+        self._tables_up = _PinnedUpload(torch.int64)  # (flat index, block id) pairs
+        self._step_up = _PinnedUpload(torch.int32)  # (row, start, kv_len) per batch row
 
     # ---- device side ----
     def flush_tables(self):
@@ -246,7 +277,8 @@ class KVCache(BlockTables):
         host = self.take_pending_flat()
         if host is None:
             return
-        d = torch.from_numpy(host).pin_memory().to(self.device, non_blocking=True)
+        n = host.shape[1]
+        d = self._tables_up.send(host.reshape(-1), self.device).view(2, n)
         self.block_tables.view(-1).index_copy_(0, d[0], d[1].to(torch.int32))
 
     def prepare(self, seqs, T):
@@ -259,12 +291,11 @@ class KVCache(BlockTables):
         starts, rows = self.step_rows(seqs, T)
         self.flush_tables()
         B = len(seqs)
-        host = torch.empty(3, B, dtype=torch.int32, pin_memory=True)
-        host[0] = torch.tensor(rows, dtype=torch.int32)
-        st = torch.tensor(starts, dtype=torch.int32)
-        host[1] = st
-        host[2] = st + T
-        dev = host.to(self.device, non_blocking=True)
+        host = np.empty((3, B), dtype=np.int32)
+        host[0] = rows
+        host[1] = starts
+        np.add(host[1], T, out=host[2])
+        dev = self._step_up.send(host.reshape(-1), self.device).view(3, B)
         step = PagedStep(self, T, starts, dev[0], dev[1], dev[2], max(starts) + T)
         return starts, step, step
 

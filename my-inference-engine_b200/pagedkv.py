@@ -43,6 +43,7 @@ _SIGNATURES = {
          _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _vp,
          _i32, _i32, _i32, _i32, _i32, _vp, _vp], ctypes.c_int),
     "pkv_decode_workspace_size": ([_i32, _i32, _i32, _i32], ctypes.c_size_t),
+    "pkv_decode_plan": ([_i32, _i32, _i32, _i32, _vp], ctypes.c_int),
     "pkv_paged_decode": (
         [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
          ctypes.c_float, _vp, _i64, _i64, _vp, ctypes.c_size_t, _vp, _vp], ctypes.c_int),
@@ -131,6 +132,14 @@ def _stream(device: torch.device) -> int:
 # ---------------------------------------------------------------- workspace
 _workspaces: dict[int, torch.Tensor] = {}
 _retired_workspaces: list[torch.Tensor] = []  # outgrown buffers stay alive (captured graphs)
+
+
+def decode_plan(batch: int, num_q_heads: int, num_kv_heads: int, max_kv_len: int) -> dict:
+    """The split-K plan pkv_paged_decode uses for these sizes (host arithmetic)."""
+    out = (ctypes.c_int32 * 4)()
+    _check(lib().pkv_decode_plan(batch, num_q_heads, num_kv_heads, max_kv_len, out), "decode_plan")
+    return {"blocks_per_part": out[0], "min_blocks_per_part": out[1], "max_parts": out[2],
+            "sub_groups": out[3]}
 
 
 def decode_workspace(batch: int, num_q_heads: int, num_kv_heads: int, max_kv_len: int,

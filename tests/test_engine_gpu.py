@@ -62,6 +62,45 @@ def test_decode_graph_matches_eager(cuda, small_model):
     assert int(view[:, :, unused].count_nonzero()) == 0
 
 
+def test_graph_inputs_survive_back_to_back_calls(cuda, small_model):
+    """A graph bucket's pinned input buffer is refilled on the next call; a
+    CUDA event makes the host wait until the previous copy out of it has run.
+    Three prompts of one prefill bucket, then two decode steps of one batch
+    bucket, each issued right after the other with host-side token ids and no
+    synchronisation between them, must give the eager forward's logits."""
+    from kv_cache import KVCache
+
+    m = small_model.fuse_weights_()
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, 151936, (n,), generator=g).tolist() for n in (40, 50, 33)]
+    results = []
+    for use_graph in (False, True):
+        c = KVCache(64, 16, cuda, torch.bfloat16)
+        if use_graph:
+            dg = m.enable_decode_graphs(c, max_batch=4)
+            pg = m.enable_prefill_graphs(c, max_len=256)
+        seqs = [c.alloc() for _ in prompts]
+        outs = []
+        with torch.no_grad():
+            for s, p in zip(seqs, prompts):  # same 64-token bucket, back to back
+                outs.append(m(torch.tensor([p]), c, [s])[:, -1].float().clone())
+            for ids in ([[11], [12], [13]], [[21], [22], [23]]):  # same 4-row bucket
+                outs.append(m(torch.tensor(ids), c, seqs)[:, -1].float().clone())
+        torch.cuda.synchronize()
+        c.check_errors()
+        if use_graph:
+            assert set(pg.graphs) == {64} and set(dg.graphs) == {4}
+        results.append(outs)
+    m._graphs.clear()
+    m._prefill_graphs.clear()
+    for a, b in zip(*results):
+        assert float((a - b).abs().max()) < 0.05
+        # the graph's top token is a top token of the eager logits (up to
+        # GEMM rounding: a padded graph can run another cuBLAS algorithm)
+        pick = a.gather(-1, b.argmax(-1, keepdim=True)).squeeze(-1)
+        assert bool((pick >= a.max(-1).values - 0.05).all())
+
+
 @pytest.mark.parametrize("mixed", [None, 1])
 def test_engine_serves_chats_with_eviction(cuda, small_model, mixed):
     """mixed=1: every prompt admitted while others decode joins their step

@@ -13,7 +13,7 @@ def _header_symbols():
 def test_header_declares_expected_entry_points():
     syms = _header_symbols()
     for s in ["pkv_append_rope", "pkv_paged_decode", "pkv_paged_prefill", "pkv_dense_attention",
-              "pkv_decode_workspace_size", "pkv_version", "pkv_status_string", "pkv_last_error"]:
+              "pkv_decode_workspace_size", "pkv_decode_plan", "pkv_version", "pkv_status_string", "pkv_last_error"]:
         assert s in syms
 
 
@@ -49,6 +49,21 @@ def test_decode_workspace_plan_is_host_only_and_sane():
     assert L.pkv_decode_workspace_size(1024, 12, 2, 8192) == 0
     # invalid head counts report 0 instead of failing
     assert L.pkv_decode_workspace_size(4, 12, 5, 8192) == 0
+
+
+def test_decode_plan_branches():
+    """pkv_decode_plan reports the partition sizing of a launch: the timed
+    config-3 launch (256 rows up to 8192 tokens) and the engine's 128-row
+    ~2100-token decode take 32-block partitions, a 4-row launch 4-block ones."""
+    import pagedkv
+
+    p = pagedkv.decode_plan(256, 12, 2, 8192)
+    assert (p["blocks_per_part"], p["min_blocks_per_part"], p["max_parts"]) == (128, 32, 4), p
+    p = pagedkv.decode_plan(128, 12, 2, 2100)
+    assert (p["min_blocks_per_part"], p["max_parts"]) == (32, 5), p
+    p = pagedkv.decode_plan(4, 12, 2, 8192)
+    assert p["min_blocks_per_part"] == 4 and p["sub_groups"] == 1, p
+    assert pagedkv.lib().pkv_decode_plan(4, 12, 5, 8192, None) == 1
 
 
 def test_entry_points_reject_bad_arguments_without_a_gpu():

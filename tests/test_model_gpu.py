@@ -40,39 +40,55 @@ def models(cuda, golden):
     return ours, ref32, ref16, fx
 
 
-def _greedy(m, cache, seqs, prompts, steps, device):
+def _greedy(m, cache, seqs, prompts, steps, device, mixed=False):
+    """Greedy ids and the logits that chose them, per row.  Default schedule:
+    each prompt prefilled alone, then `steps` batched decode steps.  mixed:
+    prompt 1 is prefilled in ONE forward with row 0's first decode step
+    (model.forward_mixed, the mixed prefill + decode tick), then the batched
+    decode steps; row 0 therefore ends one token ahead."""
     ids = [[] for _ in prompts]
-    logits_all = []
-    nxt = []
+    logits = [[] for _ in prompts]
+
+    def take(r, lg):
+        logits[r].append(lg)
+        ids[r].append(int(lg.argmax()))
+
     with torch.no_grad():
-        for r, p in enumerate(prompts):
-            lg = m(torch.tensor([p], device=device), cache, [seqs[r]])[:, -1].float()
-            logits_all.append(lg[0])
-            nxt.append(int(lg[0].argmax()))
-            ids[r].append(nxt[-1])
-        for _ in range(steps):
-            lg = m(torch.tensor([[t] for t in nxt], device=device), cache, seqs)[:, -1].float()
-            nxt = [int(lg[r].argmax()) for r in range(len(prompts))]
+        if mixed:
+            take(0, m(torch.tensor([prompts[0]], device=device), cache, [seqs[0]])[0, -1].float())
+            lg = m.forward_mixed(torch.tensor([prompts[1]], device=device), seqs[1],
+                                 torch.tensor([[ids[0][-1]]], device=device), [seqs[0]],
+                                 cache).float()
+            take(1, lg[0])
+            take(0, lg[1])
+            n_dec = steps - 1
+        else:
+            for r, p in enumerate(prompts):
+                take(r, m(torch.tensor([p], device=device), cache, [seqs[r]])[0, -1].float())
+            n_dec = steps
+        for _ in range(n_dec):
+            nxt = [[ids[r][-1]] for r in range(len(prompts))]
+            lg = m(torch.tensor(nxt, device=device), cache, seqs)[:, -1].float()
             for r in range(len(prompts)):
-                ids[r].append(nxt[r])
-                logits_all.append(lg[r])
-    return ids, logits_all
+                take(r, lg[r])
+    return ids, logits
 
 
-def _teacher_forced(ref, dtype, prompts, steps, ids, cuda):
-    """Oracle logits along OUR id sequence (so one flip does not cascade)."""
+def _teacher_forced(ref, dtype, prompts, ids, cuda):
+    """Oracle logits along OUR id sequence of each row (so one flip does not
+    cascade): the prompt, then one token at a time."""
     from oracle.kvcache_ref import RefKVCache
 
-    c = RefKVCache(64, 16, dtype)
-    c.buf = c.buf.to(cuda)
-    s = [c.alloc(), c.alloc()]
     out = []
     with torch.no_grad():
         for r, p in enumerate(prompts):
-            out.append(ref(torch.tensor([p], device=cuda), c, [s[r]])[0, -1].float())
-        for t in range(steps):
-            lg = ref(torch.tensor([[ids[0][t]], [ids[1][t]]], device=cuda), c, s)[:, -1].float()
-            out += [lg[0], lg[1]]
+            c = RefKVCache(64, 16, dtype)
+            c.buf = c.buf.to(cuda)
+            s = c.alloc()
+            row = [ref(torch.tensor([p], device=cuda), c, [s])[0, -1].float()]
+            for t in ids[r][:-1]:
+                row.append(ref(torch.tensor([[t]], device=cuda), c, [s])[0, -1].float())
+            out.append(row)
     return out
 
 
@@ -91,12 +107,18 @@ def _agreement(ref_logits, flat_ids, margin):
     return decisive, agree, worst
 
 
-@pytest.mark.parametrize("path", ["reference_ops", "fused_cublas", "fused_skinny"])
+@pytest.mark.parametrize("path", ["reference_ops", "fused_cublas", "fused_skinny", "graphs",
+                                  "mixed"])
 def test_greedy_ids_match_oracle_and_reference(cuda, models, path):
     """fused_*: merged q/k/v and gate/up GEMMs + fused add/RMSNorm/SwiGLU
     kernels (the engine's path), with the projections on cuBLAS or on the
     skinny tensor-core GEMMs (every step here has <= 256 rows);
-    reference_ops: the reference's op structure."""
+    reference_ops: the reference's op structure.
+    graphs: the engine's CUDA-graph replay (what the engine benchmark times):
+    prompts right-padded into the 64-token prefill bucket (q_lens rows), the
+    2-row decode steps padded to a 4-row bucket whose 2 extra rows are
+    inactive.  mixed: prompt 1 shares one forward with row 0's decode step
+    (model.forward_mixed)."""
     import copy
 
     from kv_cache import KVCache
@@ -104,25 +126,35 @@ def test_greedy_ids_match_oracle_and_reference(cuda, models, path):
     ours, ref32, ref16, fx = models
     if path != "reference_ops":
         ours = copy.deepcopy(ours).fuse_weights_()
-        ours.skinny_linears = path == "fused_skinny"
+        ours.skinny_linears = path != "fused_cublas"
     prompts, steps = fx["prompts"], fx["steps"]
     c1 = KVCache(64, 16, cuda, torch.bfloat16)
     s1 = [c1.alloc(), c1.alloc()]
-    got, got_logits = _greedy(ours, c1, s1, prompts, steps, cuda)
+    if path == "graphs":
+        dg = ours.enable_decode_graphs(c1, max_batch=8)
+        dg.buckets = [4, 8]  # the 2-row step runs in a 4-row graph: 2 padded, inactive rows
+        pg = ours.enable_prefill_graphs(c1, max_len=256)
+        assert all(len(p) < pg.buckets[0] for p in prompts)  # both prompts right-padded
+    got, got_logits = _greedy(ours, c1, s1, prompts, steps, cuda, mixed=path == "mixed")
     torch.cuda.synchronize()
     c1.check_errors()
-    flat = [got[r][0] for r in range(2)] + [got[r][t + 1] for t in range(steps) for r in range(2)]
+    if path == "graphs":
+        assert set(dg.graphs) == {4} and set(pg.graphs) == {pg.buckets[0]}, "graphs not replayed"
+        ours._graphs.clear()
+        ours._prefill_graphs.clear()
+    flat = [t for r in range(2) for t in got[r]]
+    flat_logits = [lg for r in range(2) for lg in got_logits[r]]
 
     torch.backends.cuda.matmul.allow_tf32 = False
-    l16 = _teacher_forced(ref16, torch.bfloat16, prompts, steps, got, cuda)
-    l32 = _teacher_forced(ref32, torch.float32, prompts, steps, got, cuda)
-    d16 = max(float((a - b).abs().max()) for a, b in zip(got_logits, l16))
-    d32 = max(float((a - b).abs().max()) for a, b in zip(got_logits, l32))
+    l16 = [lg for row in _teacher_forced(ref16, torch.bfloat16, prompts, got, cuda) for lg in row]
+    l32 = [lg for row in _teacher_forced(ref32, torch.float32, prompts, got, cuda) for lg in row]
+    d16 = max(float((a - b).abs().max()) for a, b in zip(flat_logits, l16))
+    d32 = max(float((a - b).abs().max()) for a, b in zip(flat_logits, l32))
     dec16, ag16, bad16 = _agreement(l16, flat, MARGIN_BF16)
     dec32, ag32, bad32 = _agreement(l32, flat, MARGIN_FP32)
-    diag = (f"bf16 oracle: {ag16}/{dec16} decisive agree (margin>{MARGIN_BF16}), max|dlogit| {d16:.4f}, "
-            f"misses at margins {bad16}; fp32 oracle: {ag32}/{dec32} (margin>{MARGIN_FP32}), "
-            f"max|dlogit| {d32:.4f}, misses {bad32}")
+    diag = (f"{path}: bf16 oracle: {ag16}/{dec16} decisive agree (margin>{MARGIN_BF16}), "
+            f"max|dlogit| {d16:.4f}, misses at margins {bad16}; fp32 oracle: {ag32}/{dec32} "
+            f"(margin>{MARGIN_FP32}), max|dlogit| {d32:.4f}, misses {bad32}")
     print(diag)
     assert dec16 >= len(flat) // 2 and dec32 >= 3, diag
     assert ag16 == dec16 and ag32 == dec32, diag

@@ -16,7 +16,7 @@ import math
 import pytest
 import torch
 
-from gpu_helpers import TOL, build_cache, max_err, write_history
+from gpu_helpers import build_cache, max_err, write_history
 from oracle import cases
 
 pytestmark = pytest.mark.gpu
@@ -83,7 +83,9 @@ def test_static_scratch_decode_matches_workspace_decode_twice(cuda):
         assert st == 0, lib.pkv_last_error().decode()
         torch.cuda.synchronize()
         cache.check_errors()
-        assert max_err(got, want) < TOL, lens
+        # same kernel, same plan, same merge order: identical bits, so leftover
+        # contents of the shared array from the previous call cannot leak in
+        assert torch.equal(got, want), (lens, max_err(got, want))
         assert torch.isfinite(got.float()).all()
 
 
