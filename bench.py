@@ -74,6 +74,14 @@ def parse():
     ap.add_argument("--engine4-mixed", type=int, default=None, metavar="MIN_TOKENS",
                     help="also serve config 4 with chat.MIXED_PREFILL_MIN_TOKENS=MIN_TOKENS "
                          "(prompts of at least MIN_TOKENS share the tick's decode forward)")
+    ap.add_argument("--no-engine3", action="store_true")
+    ap.add_argument("--engine3-chats", type=int, default=256)
+    ap.add_argument("--engine3-reply", type=int, default=512)
+    ap.add_argument("--engine3-arrival-reply", type=int, default=16)
+    ap.add_argument("--engine3-pool-gb", type=float, default=150.0)
+    ap.add_argument("--engine3-overflow", type=float, default=0.03,
+                    help="wave-2 reservations exceed the free blocks by this fraction of the pool")
+    ap.add_argument("--engine3-followups", type=int, default=16)
     ap.add_argument("--prefill-steps", type=int, default=20)
     # diagnostics (print their own JSON lines and exit; not the bench line)
     ap.add_argument("--linear-sweep", type=str, default=None, metavar="ROWS",
@@ -309,6 +317,9 @@ def e2e_run(w: DecodeWorkload, steps, warmup):
 
 
 # ---------------------------------------------------------------- CPU path
+CPU_WARMUP, CPU_MIN_STEPS, CPU_MIN_SECONDS = 3, 10, 10.0
+
+
 class CpuPath:
     """Reference CPU path (oracle restatement) on a bounded sample: the first
     --cpu-seqs rows of the same length distribution, all layers, fp32."""
@@ -325,15 +336,22 @@ class CpuPath:
         return (f"{len(self.lens)} rows (ctx {self.lens}) x {self.layers} layers per step, "
                 f"fp32 torch CPU")
 
-    def time_steps(self, n=None, seconds=None):
-        """Run steps until n steps or `seconds` elapse; return seconds per step."""
-        k, t0 = 0, time.perf_counter()
-        while True:
+    def measure(self, warmup=CPU_WARMUP, min_steps=CPU_MIN_STEPS, min_seconds=CPU_MIN_SECONDS):
+        """The one timing rule both arms use for the CPU path: `warmup`
+        untimed steps, then steps timed one by one until at least `min_steps`
+        steps AND `min_seconds` have passed.  Returns the median seconds per
+        step and the spread (min, max, n)."""
+        for _ in range(warmup):
             self.path.step()
-            k += 1
-            el = time.perf_counter() - t0
-            if (n is not None and k >= n) or (seconds is not None and el >= seconds):
-                return el / k, k
+        times, t0 = [], time.perf_counter()
+        while len(times) < min_steps or time.perf_counter() - t0 < min_seconds:
+            t = time.perf_counter()
+            self.path.step()
+            times.append(time.perf_counter() - t)
+        return statistics.median(times), {"min_ms": round(min(times) * 1e3, 2),
+                                          "max_ms": round(max(times) * 1e3, 2),
+                                          "median_ms": round(statistics.median(times) * 1e3, 2),
+                                          "steps": len(times), "warmup": warmup}
 
 
 def cpu_info():
@@ -469,12 +487,16 @@ class _CountingModel:
 
     def __call__(self, input_ids, cache, seqs):
         B, T = input_ids.shape
-        kv = sum(cache.length(s) for s in seqs) + B * T
+        starts = [cache.length(s) for s in seqs]
+        kv = sum(starts) + B * T
+        # causal (query, key) pairs of the attention: query i of a row that
+        # starts at s sees s + i + 1 keys
+        pairs = sum(T * s + T * (T + 1) // 2 for s in starts)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         out = self.model(input_ids, cache, seqs)
         e1.record()
-        self.calls.append(("decode" if T == 1 else "prefill", B * T, kv, e0, e1))
+        self.calls.append(("decode" if T == 1 else "prefill", B * T, kv, e0, e1, pairs))
         return out
 
     def forward_mixed(self, prefill_ids, prefill_seq, decode_ids, decode_seqs, cache):
@@ -482,10 +504,46 @@ class _CountingModel:
         kv = sum(cache.length(s) for s in decode_seqs) + B + cache.length(prefill_seq) + T
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
+        s0 = cache.length(prefill_seq)
+        pairs = T * s0 + T * (T + 1) // 2 + sum(cache.length(s) + 1 for s in decode_seqs)
         out = self.model.forward_mixed(prefill_ids, prefill_seq, decode_ids, decode_seqs, cache)
         e1.record()
-        self.calls.append(("mixed", T + B, kv, e0, e1))
+        self.calls.append(("mixed", T + B, kv, e0, e1, pairs))
         return out
+
+
+ROOFLINE_BASIS = ("per call: decode = (weights + KV read) / measured HBM; prefill = max((2*params"
+                  "*tokens + 4*12*128*causal pairs*28) / measured bf16 peak, bytes / HBM)")
+
+
+def call_roofline(calls, nparams):
+    """Per-call roofline time of an engine run and the device time split.
+
+    decode call : weights + every visible key's K/V read once at the measured
+                  HBM bandwidth;
+    prefill / mixed call : max(GEMM FLOPs 2 * params * rows + attention FLOPs
+                  4 * 12 heads * 128 * causal pairs * 28 layers at the measured
+                  bf16 peak, the same bytes at HBM)."""
+    peaks, _ = measured_peaks()
+    bw = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS)) * 1e9
+    flops_peak = float(peaks.get("bf16_tflops", 1590.0)) * 1e12
+    wbytes = nparams * 2
+    kv_tok = L * 2 * HKV * D * 2
+    out = {"t_roof": 0.0, "decode_steps": 0, "prefills": 0, "mixed": 0, "decode_ms": 0.0,
+           "prefill_ms": 0.0, "mixed_ms": 0.0}
+    for kind, rows, kv, e0, e1, pairs in calls:
+        ms = e0.elapsed_time(e1)
+        if kind == "decode":
+            out["decode_steps"] += 1
+            out["decode_ms"] += ms
+            out["t_roof"] += (wbytes + kv * kv_tok) / bw
+        else:
+            key = "mixed" if kind == "mixed" else "prefills"
+            out[key] += 1
+            out["mixed_ms" if kind == "mixed" else "prefill_ms"] += ms
+            flops = 2 * nparams * rows + 4 * HQ * D * pairs * L
+            out["t_roof"] += max(flops / flops_peak, (wbytes + kv * kv_tok) / bw)
+    return out
 
 
 def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_batch,
@@ -545,28 +603,9 @@ def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_b
     el, toks = one_round(mine, reply)
     torch.cuda.synchronize()
     nparams = sum(p.numel() for p in m.parameters())
-    wbytes = nparams * 2
-    peaks, _ = measured_peaks()
-    bw = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS)) * 1e9
-    flops_peak = float(peaks.get("bf16_tflops", 1590.0)) * 1e12
-    kv_tok = L * 2 * HKV * D * 2
-    t_roof = 0.0
-    decode_steps = prefills = mixed = 0
-    gpu_decode = gpu_prefill = gpu_mixed = 0.0
-    for kind, rows, kv, e0, e1 in cm.calls:
-        ms = e0.elapsed_time(e1)
-        if kind == "decode":
-            decode_steps += 1
-            gpu_decode += ms
-            t_roof += (wbytes + kv * kv_tok) / bw
-        else:
-            if kind == "mixed":
-                mixed += 1
-                gpu_mixed += ms
-            else:
-                prefills += 1
-                gpu_prefill += ms
-            t_roof += max(2 * nparams * rows / flops_peak, (wbytes + kv * kv_tok) / bw)
+    cr = call_roofline(cm.calls, nparams)
+    t_roof, decode_steps, prefills, mixed = cr["t_roof"], cr["decode_steps"], cr["prefills"], cr["mixed"]
+    gpu_decode, gpu_prefill, gpu_mixed = cr["decode_ms"], cr["prefill_ms"], cr["mixed_ms"]
     chat._kv_cache = None
     chat.MIXED_PREFILL_MIN_TOKENS = None
     m._graphs.clear()  # the graph runners and the model refer to each other
@@ -582,14 +621,181 @@ def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_b
                          "decode_per_step": round(gpu_decode / max(decode_steps, 1), 3),
                          "note": "CUDA events around each model call on the stream"},
             "roofline_tok_s": round(toks / t_roof, 1), "frac": round(t_roof / el, 4),
-            "roofline_basis": "per call: decode = (weights + KV read) / measured HBM; "
-                              "prefill = max(2*params*tokens / measured bf16 peak, bytes / HBM)",
+            "roofline_basis": ROOFLINE_BASIS,
             "config": f"{label}: {chats_total} chats ({len(mine)} on this GPU), prompts "
                       f"U[{lo},{hi}] random ids, {reply}-token replies, {blocks}-block pool, "
                       f"random-init bf16 Qwen2.5-1.5B (std 0.02), temperature-1 sampling, "
                       f"one prefill per tick (chat.py), CUDA-graph decode and prefill"
                       + (f"; prompts >= {mixed_min} tokens admitted while others decode share "
                          f"their forward (eager mixed step)" if mixed_min is not None else "")}
+
+
+def engine3_run(args, device, seed=0):
+    """BASELINE config 3 as an engine run through chat.py: a ~150 GB pool,
+    256 chats with prompts U[2048, 8192] decoding together, then arrivals
+    whose reservations exceed the free blocks, so chat.py's LRU eviction of
+    idle chats fires (chat.py:117-125 reserve, :128-146 _make_room), then
+    follow-up messages to evicted chats, whose whole history is prefilled
+    again (chat.py:157-185 _admit).  Three waves, each driven to idle:
+
+      wave 1  256 chats, prompts U[ctx_min, ctx_max], `engine3_reply`-token
+              replies (512 = the reference's MAX_REPLY_TOKENS): one prefill
+              per tick while the admitted chats decode, up to 256 rows per
+              decode step;
+      wave 2  chats with prompts U[ctx_min, ctx_max] and short replies, drawn
+              until their reservations exceed the free blocks left by wave 1
+              by `engine3_overflow` of the pool: the idle wave-1 chats are
+              evicted, least recently used first;
+      wave 3  a 64-token follow-up to each of the first `engine3_followups`
+              wave-1 chats (evicted first): re-prefill of history + message.
+
+    Token ids are random (seeded), weights random-init (std 0.02); EOS and
+    stop sequences are off so replies run their full length (as
+    metrics/benchmark_concurrency.py does).  Decode steps and one-row
+    prefills replay CUDA graphs captured before the timed region."""
+    import chat
+    import model as M
+    from kv_cache import KVCache
+
+    torch.manual_seed(seed)
+    m = M.Qwen2ForCausalLM().to(device, torch.bfloat16).eval()
+    random_init_(m, seed + 11)
+    block_bytes = L * 2 * 16 * HKV * D * 2
+    blocks = int(args.engine3_pool_gb * 1e9 // block_bytes)
+    lo, hi = args.ctx_min, args.ctx_max
+    r1, r2, r3 = args.engine3_reply, args.engine3_arrival_reply, 64
+    follow = 64
+    longest = hi + r1 + 1 + follow + r3 + 1  # a re-prefilled follow-up's whole reservation
+    pitch = -(-longest // 16) + 1
+    cache = KVCache(blocks, 16, device, torch.bfloat16, max_seqs=2048, max_blocks_per_seq=pitch)
+    chat.init(kv_cache=cache, start_worker=False)
+    saved = chat.STOP_SEQUENCES, chat.MAX_REPLY_TOKENS, chat.MIXED_PREFILL_MIN_TOKENS
+    chat.STOP_SEQUENCES = []
+    chat.MIXED_PREFILL_MIN_TOKENS = None
+    runner = m.enable_decode_graphs(cache, max_batch=256)
+    prunner = m.enable_prefill_graphs(cache, max_len=hi + r1 + 1 + follow)
+    t0 = time.perf_counter()
+    for b in runner.buckets:  # capture outside the timed region
+        runner._capture(b)
+    for b in prunner.buckets:
+        prunner._capture(b)
+    capture_s = time.perf_counter() - t0
+    g = torch.Generator().manual_seed(seed + 7)
+
+    def draw(n_tokens):
+        return torch.randint(0, M.VOCAB_SIZE, (n_tokens,), generator=g).tolist()
+
+    def draw_len():
+        return int(torch.randint(lo, hi + 1, (1,), generator=g))
+
+    prompts = [draw(draw_len()) for _ in range(args.engine3_chats)]
+    tok = SyntheticTokenizer(prompts)
+    cm = _CountingModel(m, cache)
+    evictions = [0]
+    real_evict = chat._evict
+
+    def counting_evict(c):
+        evictions[0] += 1
+        real_evict(c)
+
+    chat._evict = counting_evict
+
+    def run_wave(pairs, nreply):
+        """pairs: (Chat, message index); returns (wall s, generated tokens)."""
+        chat.MAX_REPLY_TOKENS = nreply
+        before = [len(c.ids) for c, _ in pairs]
+        for c, i in pairs:
+            c.submit(cm, f"p{i}")
+        t = time.perf_counter()
+        chat.run_until_idle()
+        torch.cuda.synchronize()
+        el = time.perf_counter() - t
+        toks = sum(len(c.ids) - b - len(tok.prompts[i]) - 1 for (c, i), b in zip(pairs, before))
+        return el, toks
+
+    def new_chat():
+        c = chat.Chat(tok)
+        c.eos_id = -1
+        return c
+
+    try:
+        # warm-up: sampling and one graph of each kind, outside the timed region
+        tok.prompts.append(draw(lo))
+        wc = new_chat()
+        run_wave([(wc, len(tok.prompts) - 1)], 4)
+        wc.release()
+        cm.calls.clear()
+        evictions[0] = 0
+        waves = {}
+        chats1 = [new_chat() for _ in prompts]
+        el, toks = run_wave([(c, i) for i, c in enumerate(chats1)], r1)
+        peak_batch = max((rows for kind, rows, *_ in cm.calls if kind == "decode"), default=0)
+        waves["wave1"] = {"chats": len(chats1), "wall_s": round(el, 3), "tokens": toks,
+                          "tok_s": round(toks / el, 1), "peak_decode_rows": peak_batch,
+                          "free_blocks_after": cache.free_block_count()}
+        # wave 2: arrivals whose reservations exceed the free blocks
+        free = cache.free_block_count()
+        want = free + int(args.engine3_overflow * blocks)
+        first, need = len(tok.prompts), 0
+        while need <= want:
+            n = draw_len()
+            tok.prompts.append(draw(n))
+            need += -(-(n + r2 + 1) // 16)
+        chats2 = [new_chat() for _ in range(first, len(tok.prompts))]
+        el2, toks2 = run_wave([(c, first + j) for j, c in enumerate(chats2)], r2)
+        ev2 = evictions[0]
+        n_calls2 = len(cm.calls)
+        waves["wave2"] = {"chats": len(chats2), "wall_s": round(el2, 3), "tokens": toks2,
+                          "tok_s": round(toks2 / el2, 1), "reserved_blocks": need,
+                          "free_blocks_before": free, "evictions": ev2}
+        # wave 3: follow-ups to the least recently used wave-1 chats
+        fol = chats1[:args.engine3_followups]
+        evicted = sum(1 for c in fol if c.seq is None)
+        first = len(tok.prompts)
+        for _ in fol:
+            tok.prompts.append(draw(follow))
+        el3, toks3 = run_wave([(c, first + j) for j, c in enumerate(fol)], r3)
+        # a follow-up to a resident chat prefills its 64 new tokens and the
+        # previous reply's trailing newline; an evicted one its whole history
+        re = [rows for kind, rows, *_ in cm.calls[n_calls2:] if kind == "prefill"
+              and rows > follow + 1]
+        re_prefills, re_prefill_tokens = len(re), sum(re)
+        waves["wave3"] = {"chats": len(fol), "wall_s": round(el3, 3), "tokens": toks3,
+                          "tok_s": round(toks3 / el3, 1), "evicted_before_followup": evicted,
+                          "evictions": evictions[0] - ev2}
+        torch.cuda.synchronize()
+        cache.check_errors()
+        nparams = sum(p.numel() for p in m.parameters())
+        cr = call_roofline(cm.calls, nparams)
+        wall = el + el2 + el3
+        tokens = toks + toks2 + toks3
+    finally:
+        chat._evict = real_evict
+        chat.STOP_SEQUENCES, chat.MAX_REPLY_TOKENS, chat.MIXED_PREFILL_MIN_TOKENS = saved
+        chat._kv_cache = None
+        m._graphs.clear()
+        m._prefill_graphs.clear()
+    del runner, prunner, m, cache, cm
+    gc.collect()
+    torch.cuda.empty_cache()
+    return {"tok_s": round(tokens / wall, 1), "tokens": tokens, "wall_s": round(wall, 3),
+            "evictions": evictions[0], "re_prefills": re_prefills,
+            "re_prefill_tokens": re_prefill_tokens, "pool_blocks": blocks,
+            "decode_steps": cr["decode_steps"], "prefills": cr["prefills"], "waves": waves,
+            "model_ms": {"decode_total": round(cr["decode_ms"], 2),
+                         "prefill_total": round(cr["prefill_ms"], 2),
+                         "decode_per_step": round(cr["decode_ms"] / max(cr["decode_steps"], 1), 3),
+                         "note": "CUDA events around each model call on the stream"},
+            "roofline_tok_s": round(tokens / cr["t_roof"], 1),
+            "frac": round(cr["t_roof"] / wall, 4), "roofline_basis": ROOFLINE_BASIS,
+            "graph_capture_s": round(capture_s, 2),
+            "config": f"config3 engine: {blocks}-block pool (~{args.engine3_pool_gb:g} GB bf16), "
+                      f"{len(chats1)} chats with prompts U[{lo},{hi}] random ids and "
+                      f"{r1}-token replies, then {len(chats2)} arrivals (prompts U[{lo},{hi}], "
+                      f"{r2}-token replies) reserving more than the free blocks, then "
+                      f"{len(fol)} {follow}-token follow-ups to the least recently used "
+                      f"wave-1 chats; random-init bf16 Qwen2.5-1.5B, temperature-1 sampling, "
+                      f"one prefill per tick (chat.py), CUDA-graph decode and prefill"}
 
 
 def engine_cpu_sample(seconds_budget=60.0):
@@ -629,6 +835,25 @@ def cross_rank(value, op, device, world):
     t = torch.tensor([float(value)], dtype=torch.float64, device=device)
     torch.distributed.all_reduce(t, op=op)
     return float(t.item())
+
+
+def gather_ranks(obj, world):
+    """Every rank's `obj` (a small dict), in rank order; every rank calls it
+    at the same point (a collective)."""
+    if world == 1:
+        return [obj]
+    out = [None] * world
+    torch.distributed.all_gather_object(out, obj)
+    return out
+
+
+def rank_summary(rank, r):
+    """One rank's share of an engine run: its own tokens, wall time and the
+    device-time split of its model calls."""
+    return {"rank": rank, "tok_s": r["tok_s"], "tokens": r["tokens"], "wall_s": r["wall_s"],
+            "decode_steps": r["decode_steps"], "prefills": r["prefills"],
+            "decode_ms": r["model_ms"]["decode_total"], "prefill_ms": r["model_ms"]["prefill_total"],
+            "decode_ms_per_step": r["model_ms"]["decode_per_step"], "frac": r["frac"]}
 
 
 def replica_rate(units_per_rank, ms_local, device, world):
@@ -993,17 +1218,20 @@ def main():
         # each timed step is a bounded sample: one pass of the CPU path over
         # --cpu-seqs rows and every layer
         cp = CpuPath(args)
-        cp.time_steps(n=args.warmup)
-        per_step, _ = cp.time_steps(n=args.steps)
+        # the same rule as the cpu_baseline leg of our arm (CpuPath.measure),
+        # at least the driver's warm-up and step counts
+        per_step, spread = cp.measure(warmup=max(args.warmup, CPU_WARMUP),
+                                      min_steps=max(args.steps, CPU_MIN_STEPS))
         val = cp.bytes / per_step / 1e9
-        sample = cp.sample()
+        sample = cp.sample() + ", median of the timed steps"
         line = {"metric": metric, "value": round(val, 3), "unit": "GB/s", "impl": "reference",
                 "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": round(per_step * 1e3, 3), "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                 "config": config,
                 "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": threads,
-                                 "kind": "port", "sample": sample, "cpu": cpu_info()},
+                                 "kind": "port", "sample": sample, "cpu": cpu_info(),
+                                 "spread": spread},
                 "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
@@ -1071,6 +1299,7 @@ def main():
         engine["wall_s_max_over_gpus"] = round(wall_max / 1e3, 4)
         engine["n_gpus"] = world
         engine["scaling"] = "weak (each GPU serves its own chats)"
+        engine["per_rank"] = gather_ranks(rank_summary(rank, engine), world)
     if not args.no_engine4:
         # config 4: 1024 chats split round-robin over the GPUs (strong scaling)
         block_bytes = L * 2 * 16 * HKV * D * 2
@@ -1089,13 +1318,19 @@ def main():
                                   dev, world)
             r.update({"tok_s_all_gpus": round(toks_all / wall_max, 1),
                       "tokens_all_gpus": int(toks_all), "wall_s_max_over_gpus": round(wall_max, 4),
-                      "n_gpus": world, "scaling": "strong (1024 chats split over the GPUs)"})
+                      "n_gpus": world, "scaling": "strong (1024 chats split over the GPUs)",
+                      "per_rank": gather_ranks(rank_summary(rank, r), world)})
             runs[mixed_min] = r
         engine4 = runs[None]
         engine4_mixed = runs.get(args.engine4_mixed) if args.engine4_mixed is not None else None
         if engine is not None and rank == 0 and world == 1 and not args.no_engine_cpu:
             torch.set_num_threads(os.cpu_count() or 1)
             engine["cpu_baseline"] = engine_cpu_sample()
+
+    engine3 = None
+    if not args.no_engine3 and world == 1:
+        # config 3 is a one-GPU configuration: the 1-GPU run serves it
+        engine3 = engine3_run(args, dev, seed=args.seed)
 
     peaks, src = measured_peaks()
     peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
@@ -1108,8 +1343,16 @@ def main():
                 "traffic": None}
     prof = REPO / "profiles" / "decode_traffic.json"
     if prof.exists():
+        # not measured in this run: ncu's dram bytes of one decode launch on a
+        # smaller case, scaled to this launch by algorithmic bytes
         try:
-            roofline["traffic"] = json.loads(prof.read_text()).get("traffic_bytes_per_launch")
+            t = json.loads(prof.read_text())
+            ratio = float(t["traffic_over_algorithmic"])
+            roofline["traffic"] = int(round(ratio * bytes_decode))
+            roofline["traffic_source"] = (
+                f"ncu dram__bytes_read.sum + dram__bytes_write.sum on {t.get('case', 'a smaller case')}"
+                f" ({t.get('source')}), not this run; traffic/algorithmic = {ratio} scaled to "
+                f"this launch's algorithmic bytes")
         except Exception:
             pass
 
@@ -1117,11 +1360,11 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
         cp = CpuPath(args)
-        cp.time_steps(n=1)
-        per_step, n = cp.time_steps(seconds=12.0)
+        per_step, spread = cp.measure()
         cpu = {"value": round(cp.bytes / per_step / 1e9, 3), "unit": "GB/s",
                "cores": torch.get_num_threads(), "kind": "port",
-               "sample": cp.sample() + f", {n} steps timed", "cpu": cpu_info()}
+               "sample": cp.sample() + ", median of the timed steps", "cpu": cpu_info(),
+               "spread": spread}
 
     if rank == 0:
         line = {"metric": metric, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
@@ -1131,6 +1374,7 @@ def main():
                 "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
                 "gpu_launches": args.steps * layers * 2,
                 "kv_bytes_per_step": step_bytes, "prefill": prefill, "engine": engine, "engine_config4": engine4,
+                **({"engine_config3": engine3} if engine3 is not None else {}),
                 **({"engine_config4_mixed": engine4_mixed} if engine4_mixed is not None else {})}
         print(json.dumps(line), flush=True)
     if world > 1:

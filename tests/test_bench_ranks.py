@@ -32,7 +32,8 @@ def _rank(rank, world, port, q):
     ms_local = 10.0 + 5.0 * rank  # rank 1 is slower
     ms_max, rate = bench.replica_rate(1e9, ms_local, dev, world)
     total = bench.cross_rank(rank + 1, torch.distributed.ReduceOp.SUM, dev, world)
-    q.put((rank, ms_max, rate, total))
+    per = bench.gather_ranks({"rank": rank, "tok_s": 100.0 * (rank + 1)}, world)
+    q.put((rank, ms_max, rate, total, per))
     torch.distributed.destroy_process_group()
 
 
@@ -47,10 +48,12 @@ def test_replica_rate_two_gloo_ranks():
         p.join(120)
         assert p.exitcode == 0
     got = sorted(q.get(timeout=10) for _ in range(2))
-    for rank, ms_max, rate, total in got:
+    for rank, ms_max, rate, total, per in got:
         assert ms_max == pytest.approx(15.0)           # the slowest rank
         assert rate == pytest.approx(2e9 / 15e-3)      # both ranks' units / job time
         assert total == pytest.approx(3.0)
+        # every rank sees every rank's summary, in rank order
+        assert per == [{"rank": 0, "tok_s": 100.0}, {"rank": 1, "tok_s": 200.0}]
 
 
 def test_replica_rate_single_process_is_identity():
