@@ -727,7 +727,7 @@ def engine3_run(args, device, seed=0):
         cm.calls.clear()
         evictions[0] = 0
         waves = {}
-        chats1 = [new_chat() for _ in prompts]
+        chats1 = [new_chat() for _ in range(args.engine3_chats)]
         el, toks = run_wave([(c, i) for i, c in enumerate(chats1)], r1)
         peak_batch = max((rows for kind, rows, *_ in cm.calls if kind == "decode"), default=0)
         waves["wave1"] = {"chats": len(chats1), "wall_s": round(el, 3), "tokens": toks,
@@ -1089,7 +1089,7 @@ def prefill_sweep(shapes, device):
     peak = float(peaks.get("bf16_tflops", 1590.0))
     saved = os.environ.get("PKV_PREFILL_KERNEL")
     try:
-        for kern in ("one", "pair"):
+        for kern in ("persist", "one", "pair"):
             os.environ["PKV_PREFILL_KERNEL"] = kern
             for B, T in shapes:
                 g = torch.Generator(device=device).manual_seed(B * 100000 + T)
