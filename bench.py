@@ -1089,7 +1089,7 @@ def prefill_sweep(shapes, device):
     peak = float(peaks.get("bf16_tflops", 1590.0))
     saved = os.environ.get("PKV_PREFILL_KERNEL")
     try:
-        for kern in ("persist", "one", "pair"):
+        for kern in ("one", "pair"):
             os.environ["PKV_PREFILL_KERNEL"] = kern
             for B, T in shapes:
                 g = torch.Generator(device=device).manual_seed(B * 100000 + T)

@@ -155,11 +155,6 @@ int pkv_paged_decode(const void* q, int64_t q_sb, int64_t q_sh,
  * q_lens (nullable, device int32 [B]): row b has q_lens[b] <= T real queries
  * at positions 0..q_lens[b]-1 (right padding); query i then sits at key
  * i + kv_lens[b] - q_lens[b], and output rows i >= q_lens[b] are not written.
- * workspace (nullable): >= pkv_prefill_workspace_size() bytes, 16-byte
- * aligned, zeroed before first use; the kernel leaves it zeroed.  With it the
- * persistent kernel runs (one CTA per SM claiming q-tiles from a counter in
- * the workspace); without it one CTA per q-tile.  Same results either way.
- * Launches sharing a workspace must be ordered on one stream.
  */
 int pkv_paged_prefill(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
                       const void* k_pool, const void* v_pool, int64_t num_slots,
@@ -169,15 +164,7 @@ int pkv_paged_prefill(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
                       int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
                       int32_t causal, float sm_scale,
                       void* out, int64_t o_sb, int64_t o_sh, int64_t o_st,
-                      void* workspace, size_t workspace_bytes,
                       int32_t* err_flag, void* stream);
-
-/*
- * Bytes of the optional prefill workspace (the persistent kernel's work
- * counters).  No counterpart in the reference (its kernel launches one
- * program per tile, kernels/fa2.py:192-207).
- */
-size_t pkv_prefill_workspace_size(void);
 
 /*
  * Attention over dense, padded K/V -- the exact argument contract of
@@ -186,8 +173,7 @@ size_t pkv_prefill_workspace_size(void);
  * multiple of 8 elements (16 bytes) and the bases 16-byte aligned.
  * Rows are masked to kv_lens[b] (<= S) and bottom-right causal when
  * causal != 0.  T == 1 uses the decode kernel (and the workspace, sized by
- * pkv_decode_workspace_size with max_kv_len = S), T > 1 the prefill kernel
- * (the workspace then optional, as pkv_paged_prefill's).
+ * pkv_decode_workspace_size with max_kv_len = S), T > 1 the prefill kernel.
  */
 int pkv_dense_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
                         const void* k, int64_t k_sb, int64_t k_sh, int64_t k_ss,

@@ -219,19 +219,6 @@ int check_linear_ws(void* workspace, size_t workspace_bytes, int32_t rows, int32
   return PKV_OK;
 }
 
-// Optional prefill workspace: the persistent kernel's two work counters.
-int prefill_work(void* workspace, size_t bytes, int32_t** work) {
-  *work = nullptr;
-  if (!workspace || bytes == 0) return PKV_OK;
-  if (bytes < pkv::kPrefillWorkspaceBytes)
-    return fail(PKV_ERR_WORKSPACE, "prefill workspace of %zu bytes, need %zu", bytes,
-                pkv::kPrefillWorkspaceBytes);
-  if (reinterpret_cast<uintptr_t>(workspace) & 15u)
-    return fail(PKV_ERR_ALIGN, "prefill workspace must be 16-byte aligned");
-  *work = static_cast<int32_t*>(workspace);
-  return PKV_OK;
-}
-
 int launch_prefill_any(const pkv::PrefillLaunch& a, const pkv::KVSource& src, cudaStream_t s) {
   CUtensorMap qmap;
   int st = encode_q(&qmap, a.q, a.batch, a.num_q_heads, a.seq_len_q, a.q_sb, a.q_sh, a.q_st);
@@ -306,8 +293,6 @@ size_t pkv_decode_workspace_size(int32_t batch, int32_t num_q_heads, int32_t num
   return pkv::plan_decode(batch, num_q_heads, num_kv_heads, max_kv_len).workspace_bytes;
 }
 
-size_t pkv_prefill_workspace_size(void) { return pkv::kPrefillWorkspaceBytes; }
-
 int pkv_decode_plan(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t max_kv_len,
                     int32_t* plan) {
   if (!plan || batch <= 0 || num_kv_heads <= 0 || num_q_heads <= 0 || max_kv_len < 0 ||
@@ -380,8 +365,8 @@ int pkv_paged_prefill(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, c
                       const int32_t* q_lens, int32_t max_kv_len, int32_t batch, int32_t seq_len_q,
                       int32_t num_q_heads,
                       int32_t num_kv_heads, int32_t head_dim, int32_t causal, float sm_scale,
-                      void* out, int64_t o_sb, int64_t o_sh, int64_t o_st, void* workspace,
-                      size_t workspace_bytes, int32_t* err_flag, void* stream) {
+                      void* out, int64_t o_sb, int64_t o_sh, int64_t o_st, int32_t* err_flag,
+                      void* stream) {
   (void)max_kv_len;
   int st = check_heads(num_q_heads, num_kv_heads, head_dim);
   if (st) return st;
@@ -389,8 +374,6 @@ int pkv_paged_prefill(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, c
   if ((st = check_qo(q, out, q_sb, q_sh, q_st, o_sb, o_sh, o_st))) return st;
   if (!kv_lens) return fail(PKV_ERR_INVALID, "null kv_lens");
   if (batch < 0 || seq_len_q < 0) return fail(PKV_ERR_INVALID, "negative batch / seq_len_q");
-  int32_t* work = nullptr;
-  if ((st = prefill_work(workspace, workspace_bytes, &work))) return st;
   if (batch == 0 || seq_len_q == 0) return ok();
   pkv::KVSource src{};
   src.paged = true;
@@ -405,7 +388,7 @@ int pkv_paged_prefill(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, c
   a.out = out; a.o_sb = o_sb; a.o_sh = o_sh; a.o_st = o_st;
   a.kv_lens = kv_lens; a.q_lens = q_lens; a.batch = batch; a.seq_len_q = seq_len_q;
   a.num_q_heads = num_q_heads; a.num_kv_heads = num_kv_heads; a.causal = causal ? 1 : 0;
-  a.sm_scale = sm_scale; a.err = err_flag; a.work = work;
+  a.sm_scale = sm_scale; a.err = err_flag;
   return launch_prefill_any(a, src, static_cast<cudaStream_t>(stream));
 }
 
@@ -447,7 +430,6 @@ int pkv_dense_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
   a.kv_lens = kv_lens; a.batch = batch; a.seq_len_q = seq_len_q;
   a.num_q_heads = num_q_heads; a.num_kv_heads = num_kv_heads; a.causal = causal ? 1 : 0;
   a.sm_scale = sm_scale; a.err = err_flag;
-  if ((st = prefill_work(workspace, workspace_bytes, &a.work))) return st;
   return launch_prefill_any(a, src, s);
 }
 

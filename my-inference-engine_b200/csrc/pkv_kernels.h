@@ -67,10 +67,7 @@ struct PrefillLaunch {
   int32_t causal;
   float sm_scale;
   int32_t* err;
-  int32_t* work = nullptr;  // nullable: 2 zeroed int32 work counters (persistent kernel)
 };
-// Bytes of the prefill work counters (kept zero between launches).
-constexpr size_t kPrefillWorkspaceBytes = 256;
 // tcgen05/TMEM prefill; qmap: 4-D map over q [B][Hq][T][128], box {64,128,1,1}
 cudaError_t launch_prefill_tc(const PrefillLaunch& a, const CUtensorMap& qmap, const KVSource& src,
                               cudaStream_t stream);

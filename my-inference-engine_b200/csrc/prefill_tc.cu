@@ -858,505 +858,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   }
 }
 
-// ---------------------------------------------------------------- persistent
-// One CTA per SM loops over work items (one 128-row q-tile of one head of one
-// row), claimed one at a time from a counter in the caller's workspace in
-// the one-head grid's order: q-tile index slowest and reversed, so the
-// heaviest causal tiles go first and the light ones fill in behind (greedy
-// list scheduling instead of fixed CTA waves).  A CTA keeps its barriers and
-// its 512 TMEM columns for the whole launch, so the per-tile fixed costs of
-// the one-CTA-per-tile kernels (set-up, TMEM allocation, the first Q/K
-// landing, the O epilogue) overlap the neighbouring item's work:
-//   warps 0-3   softmax (as the one-head kernel: one query row per thread, P
-//               written over its S buffer in TMEM), 240 registers
-//   warps 4-7   epilogue: O (double-buffered in TMEM) -> bf16 rows, so the
-//               softmax warps move on to the next item at once
-//   warp  8     TMA producer: claims items, writes their descriptors, loads
-//               Q (two slots) and the K / V rings, running ahead across items
-//   warp  9     TMEM owner and MMA issuer
-//   warps 10-11 idle (they complete warpgroup 2 for the register split)
-// Register split (setmaxnreg): launched at 168 per thread (384 x 168 =
-// 64512); softmax 240, epilogue 168, warpgroup 2 96: 128 x (240 + 168 + 96)
-// = 64512.  The host launches this kernel only when the compiled kernel has
-// exactly 168 registers, so the split always fits.
-// Tiles are counted across items (global tile g): K/V ring stage g & 1, S
-// buffer g & 1, each with its own barriers.  Every wait is bounded and also
-// gives up when another role has timed out (a shared abort flag).
-constexpr int kQThreads = 384;
-constexpr uint32_t kQColS0 = 0, kQColS1 = 128, kQColO0 = 256, kQColO1 = 384;
-constexpr int kQOffQ = 0;                             // 2 Q slots x 32 KiB
-constexpr int kQOffK = kQOffQ + 2 * kOperand;         // 2 K stages
-constexpr int kQOffV = kQOffK + kStages * kOperand;   // 2 V stages
-constexpr int kQOffL = kQOffV + kStages * kOperand;   // row sums l: 2 x 128 fp32
-constexpr int kQOffItem = kQOffL + 2 * kRows * 4;     // 2 item descriptors
-constexpr int kQOffBar = kQOffItem + 2 * 64;
-constexpr int kQNumBars = 14 * 2 + 1;
-constexpr int kQSmemBytes = kQOffBar + kQNumBars * 8 + 16 + 1024;
-constexpr int kQLaunchRegs = 168;
-static_assert(kQSmemBytes <= 227 * 1024, "persistent prefill shared memory exceeds the limit");
-static_assert(128 * (240 + kQLaunchRegs + 96) <= kQThreads * kQLaunchRegs,
-              "register split exceeds the launch allocation");
-
-struct PItem {
-  int32_t hq, b, q0, T, kv_len, offset, nblk, ntiles;  // hq < 0: no more items
-};
-
-__device__ __forceinline__ bool pwait(uint64_t* bar, uint32_t parity, volatile int32_t* abort,
-                                      const DevErr& err) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    if (mbar_test(bar, parity)) return true;
-    if ((i & 255u) == 255u && *abort) return false;
-  }
-  err.raise(PKV_DEVERR_TIMEOUT);
-  *abort = 1;
-  return false;
-}
-
-template <bool kPaged>
-__global__ void __launch_bounds__(kQThreads, 1)
-    prefill_tc_persist_kernel(const TcParams p, int32_t* work, int32_t total_items,
-                              int32_t qtiles, int32_t batch, int32_t num_q_heads,
-                              const __grid_constant__ CUtensorMap qmap,
-                              const __grid_constant__ CUtensorMap kmap,
-                              const __grid_constant__ CUtensorMap vmap) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kQOffBar);
-  uint64_t* it_full = bars;        // producer wrote the item descriptor
-  uint64_t* it_empty = bars + 2;   // MMA, 4 softmax and 4 epilogue warps read it
-  uint64_t* q_full = bars + 4;
-  uint64_t* q_empty = bars + 6;    // commit after the item's last Q.K^T
-  uint64_t* k_full = bars + 8;
-  uint64_t* k_empty = bars + 10;
-  uint64_t* v_full = bars + 12;
-  uint64_t* v_empty = bars + 14;
-  uint64_t* s_full = bars + 16;    // [S buffer]
-  uint64_t* p_full = bars + 18;    // [S buffer], 4 softmax warps
-  uint64_t* pv_done = bars + 20;   // [S buffer]
-  uint64_t* o_full = bars + 22;    // [O buffer], commit after the item's last P.V
-  uint64_t* o_empty = bars + 24;   // [O buffer], 4 epilogue warps read O and l
-  uint64_t* l_full = bars + 26;    // [O buffer], 128 softmax threads wrote l
-  uint64_t* mma_done = bars + 28;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kQNumBars);
-  volatile int32_t* abort = reinterpret_cast<volatile int32_t*>(tmem_slot + 1);
-  PItem* items = reinterpret_cast<PItem*>(smem + kQOffItem);
-  float* lbuf = reinterpret_cast<float*>(smem + kQOffL);
-
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5, lane = tid & 31;
-  if (tid == 0) {
-    prefetch_tmap(&qmap);
-    prefetch_tmap(&kmap);
-    prefetch_tmap(&vmap);
-  }
-  pdl_wait();
-  const DevErr err{p.err};
-  if (tid == 0) {
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&it_full[s], 1);
-      mbar_init(&it_empty[s], 9);
-      mbar_init(&q_full[s], 1);
-      mbar_init(&q_empty[s], 1);
-      mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
-      mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
-      mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], 4);
-      mbar_init(&pv_done[s], 1);
-      mbar_init(&o_full[s], 1);
-      mbar_init(&o_empty[s], 4);
-      mbar_init(&l_full[s], kRows);
-    }
-    mbar_init(mma_done, 1);
-    *abort = 0;
-    fence_mbar_init();
-  }
-  if (warp == 9) tmem_alloc(tmem_slot, kTmemCols);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  pdl_trigger();  // dependents launch once this CTA holds its TMEM
-  const uint32_t tmem = *tmem_slot;
-  // Each role's code sits inside the branch that set its register limit, so
-  // the compiler allocates that role's registers under that limit.
-  if (warp >= 8) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 96;");
-    if (warp == 8) {
-      // ------------------------------------------------------------ producer
-      if (lane == 0) {
-        const uint64_t keep = policy_evict_last();
-        int last_q[2] = {-1, -1}, last_k[2] = {-1, -1}, last_v[2] = {-1, -1};
-        bool dead = false;
-        int g = 0, n = 0;
-        for (int k = 0; !dead; ++k) {
-          const int slot = k & 1;
-          if (k >= 2 && !pwait(&it_empty[slot], ((k >> 1) - 1) & 1, abort, err)) break;
-          const int it = atomicAdd(work, 1);
-          PItem d{};
-          d.hq = -1;
-          const int32_t* trow = nullptr;
-          if (it < total_items) {
-            const int per = batch * num_q_heads;
-            const int qt_rev = it / per, rem = it - qt_rev * per;
-            d.b = rem / num_q_heads;
-            d.hq = rem - d.b * num_q_heads;
-            d.q0 = (qtiles - 1 - qt_rev) * kRows;
-            d.T = p.q_lens ? min(max(p.q_lens[d.b], 0), p.T) : p.T;
-            int kv_len = max(p.kv_lens[d.b], 0);
-            if constexpr (kPaged) {
-              const int row = p.rows ? p.rows[d.b] : d.b;
-              trow = p.tables + static_cast<int64_t>(row) * p.pitch;
-              if (kv_len > p.pitch * kBlockTokens) {
-                err.raise(PKV_DEVERR_POSITION);
-                kv_len = static_cast<int>(p.pitch) * kBlockTokens;
-              }
-            }
-            d.kv_len = kv_len;
-            d.offset = kv_len - d.T;
-            int kv_end = kv_len;
-            if (p.causal) kv_end = min(kv_len, min(d.q0 + kRows, d.T) + d.offset);
-            kv_end = max(kv_end, 0);
-            d.nblk = (kv_end + kBlockTokens - 1) / kBlockTokens;
-            // a tile past the row's real queries (right padding) writes nothing
-            d.ntiles = d.q0 < d.T ? (d.nblk + kTileBlocks - 1) / kTileBlocks : 0;
-          }
-          items[slot] = d;
-          mbar_arrive(&it_full[slot]);
-          if (d.hq < 0) break;
-          if (d.ntiles == 0) continue;
-          const int qs = n & 1;
-          if (n >= 2 && !pwait(&q_empty[qs], ((n >> 1) - 1) & 1, abort, err)) break;
-          mbar_arrive_expect_tx(&q_full[qs], kOperand);
-          uint8_t* qd = smem + kQOffQ + qs * kOperand;
-          tma_load_4d(qd, &qmap, &q_full[qs], 0, d.q0, d.hq, d.b, keep);
-          tma_load_4d(qd + kRegion, &qmap, &q_full[qs], 64, d.q0, d.hq, d.b, keep);
-          last_q[qs] = n;
-          const int kvh = d.hq / p.group;
-          auto fetch = [&](int j, int (&ids)[kTileBlocks]) {
-            if constexpr (kPaged) {
-#pragma unroll
-              for (int jb = 0; jb < kTileBlocks; ++jb) {
-                const int lb = j * kTileBlocks + jb;
-                ids[jb] = trow[lb < d.nblk ? lb : 0];  // past the end: finite, masked
-              }
-#pragma unroll
-              for (int jb = 0; jb < kTileBlocks; ++jb) {
-                if (ids[jb] < 0 || ids[jb] >= p.num_blocks) {
-                  err.raise(PKV_DEVERR_BLOCK_ID);
-                  ids[jb] = 0;
-                }
-              }
-            }
-          };
-          auto issue = [&](int j, const int (&ids)[kTileBlocks], bool is_v) -> bool {
-            const int gj = g + j, st = gj & 1;
-            uint64_t* full = is_v ? &v_full[st] : &k_full[st];
-            uint64_t* empty = is_v ? &v_empty[st] : &k_empty[st];
-            if (gj >= 2 && !pwait(empty, ((gj >> 1) - 1) & 1, abort, err)) return false;
-            uint8_t* dst = smem + (is_v ? kQOffV : kQOffK) + st * kOperand;
-            const CUtensorMap* map = is_v ? &vmap : &kmap;
-            mbar_arrive_expect_tx(full, kOperand);
-#pragma unroll
-            for (int jb = 0; jb < kTileBlocks; ++jb) {
-              if constexpr (kPaged) {
-                const int slot_tok = ids[jb] * kBlockTokens;
-                tma_load_3d(dst + jb * 2048, map, full, 0, kvh, slot_tok, keep);
-                tma_load_3d(dst + kRegion + jb * 2048, map, full, 64, kvh, slot_tok, keep);
-              } else {
-                const int tok = (j * kTileBlocks + jb) * kBlockTokens;
-                tma_load_4d(dst + jb * 2048, map, full, 0, tok, kvh, d.b, keep);
-                tma_load_4d(dst + kRegion + jb * 2048, map, full, 64, tok, kvh, d.b, keep);
-              }
-            }
-            if (is_v)
-              last_v[st] = gj;
-            else
-              last_k[st] = gj;
-            return true;
-          };
-          int idk[kTileBlocks] = {}, idv[kTileBlocks] = {};
-          fetch(0, idk);
-          if (!issue(0, idk, false)) break;
-          for (int j = 0; j < d.ntiles; ++j) {  // K runs one tile ahead of V
-#pragma unroll
-            for (int jb = 0; jb < kTileBlocks; ++jb) idv[jb] = idk[jb];
-            if (j + 1 < d.ntiles) {
-              fetch(j + 1, idk);
-              if (!issue(j + 1, idk, false)) {
-                dead = true;
-                break;
-              }
-            }
-            if (!issue(j, idv, true)) {
-              dead = true;
-              break;
-            }
-          }
-          g += d.ntiles;
-          ++n;
-        }
-        if (*abort) {
-          // drain: every load issued must land before the CTA exits
-          for (int s = 0; s < 2; ++s) {
-            if (last_q[s] >= 0) mbar_wait(&q_full[s], (last_q[s] >> 1) & 1, err);
-            if (last_k[s] >= 0) mbar_wait(&k_full[s], (last_k[s] >> 1) & 1, err);
-            if (last_v[s] >= 0) mbar_wait(&v_full[s], (last_v[s] >> 1) & 1, err);
-          }
-        }
-      }
-    } else if (warp == 9) {
-      // ------------------------------------------------------------ MMA issuer
-      if (lane == 0) {
-        bool dead = false;
-        int g = 0, n = 0;
-        for (int k = 0; !dead; ++k) {
-          const int slot = k & 1;
-          if (!pwait(&it_full[slot], (k >> 1) & 1, abort, err)) break;
-          const PItem d = items[slot];
-          mbar_arrive(&it_empty[slot]);
-          if (d.hq < 0) break;
-          if (d.ntiles == 0) continue;
-          const int qs = n & 1, ob = n & 1;
-          if (!pwait(&q_full[qs], (n >> 1) & 1, abort, err)) break;
-          tc_fence_after();
-          const uint32_t sQ = smem_u32(smem + kQOffQ + qs * kOperand);
-          const uint32_t tO = tmem + (ob ? kQColO1 : kQColO0);
-          auto issue_pv = [&](int jl) -> bool {
-            const int gj = g + jl, sb = gj & 1;
-            if (!pwait(&p_full[sb], (gj >> 1) & 1, abort, err)) return false;
-            if (!pwait(&v_full[sb], (gj >> 1) & 1, abort, err)) return false;
-            // O[ob] is free once the epilogue read item n-2's O
-            if (jl == 0 && n >= 2 && !pwait(&o_empty[ob], ((n >> 1) - 1) & 1, abort, err))
-              return false;
-            tc_fence_after();
-            const uint32_t sV = smem_u32(smem + kQOffV + sb * kOperand);
-            const uint32_t pS = tmem + (sb ? kQColS1 : kQColS0);
-            const int nb = min(kTileBlocks, d.nblk - jl * kTileBlocks);
-            for (int kb = 0; kb < nb; ++kb)
-              umma_ts(tO, pS + kb * 8, sdesc(sV + kb * 2048, kRegion, 1024), kIdescPV,
-                      (jl > 0 || kb > 0) ? 1u : 0u);
-            umma_commit(&pv_done[sb]);
-            umma_commit(&v_empty[sb]);
-            return true;
-          };
-          for (int jl = 0; jl < d.ntiles; ++jl) {
-            const int gj = g + jl, sb = gj & 1;
-            if (!pwait(&k_full[sb], (gj >> 1) & 1, abort, err)) {
-              dead = true;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t sK = smem_u32(smem + kQOffK + sb * kOperand);
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              umma(tmem + (sb ? kQColS1 : kQColS0), kmajor_desc(sQ, kk), kmajor_desc(sK, kk),
-                   kIdescQK, kk > 0 ? 1u : 0u);
-            umma_commit(&s_full[sb]);
-            umma_commit(&k_empty[sb]);
-            if (jl == d.ntiles - 1) umma_commit(&q_empty[qs]);
-            if (jl >= 1 && !issue_pv(jl - 1)) {
-              dead = true;
-              break;
-            }
-          }
-          if (dead || !issue_pv(d.ntiles - 1)) break;
-          umma_commit(&o_full[ob]);
-          g += d.ntiles;
-          ++n;
-        }
-        umma_commit(mma_done);
-        mbar_wait(mma_done, 0, err);  // every MMA retired before TMEM is freed
-      }
-    }
-  } else if (warp < 4) {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 240;");
-    // ------------------------------------------------------------ softmax
-    const int quarter = warp;
-    const int r = quarter * 32 + lane;  // query row within the tile == TMEM lane
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    bool dead = false;
-    int g = 0, n = 0;
-    for (int k = 0; !dead; ++k) {
-      const int slot = k & 1;
-      if (!__all_sync(0xffffffffu, pwait(&it_full[slot], (k >> 1) & 1, abort, err))) break;
-      const PItem d = items[slot];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&it_empty[slot]);
-      if (d.hq < 0) break;
-      if (d.ntiles == 0) continue;
-      const int ob = n & 1;
-      const uint32_t colO = ob ? kQColO1 : kQColO0;
-      const int qi = d.q0 + r;
-      const int lim = p.causal ? min(d.kv_len, qi + d.offset + 1) : d.kv_len;  // keys < lim
-      float m = -INFINITY, l = 0.f;
-      for (int jl = 0; jl < d.ntiles; ++jl) {
-        const int gj = g + jl, sb = gj & 1;
-        const uint32_t colS = sb ? kQColS1 : kQColS0;
-        if (!__all_sync(0xffffffffu, pwait(&s_full[sb], (gj >> 1) & 1, abort, err))) {
-          dead = true;
-          break;
-        }
-        tc_fence_after();
-        float s[128];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float v[32];
-          tmem_ld32(lane_addr + colS + c * 32, v);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) s[c * 32 + i] = v[i];
-        }
-        tmem_wait_ld();
-        const int key0 = jl * kKeys;
-        float pm[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) pm[u] = -INFINITY;
-        if (key0 + kKeys <= lim) {
-#pragma unroll
-          for (int i = 0; i < 128; ++i) pm[i & 7] = fmaxf(pm[i & 7], s[i]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 128; ++i) {
-            if (key0 + i >= lim) s[i] = -INFINITY;
-            pm[i & 7] = fmaxf(pm[i & 7], s[i]);
-          }
-        }
-        const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                               fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) *
-                         p.scale_log2;
-        float mn = m;
-        if (mx > m + kRescaleThreshold || m == -INFINITY) mn = mx;
-        const float base = mn == -INFINITY ? 0.f : mn;
-        const float alpha = (mn == m) ? 1.f : ex2(m - base);
-        float ps[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) ps[u] = 0.f;
-#pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          s[i] = ex2(fmaf(s[i], p.scale_log2, -base));
-          ps[i & 7] += s[i];
-        }
-        const float rs =
-            ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-        l = l * alpha + rs;
-        m = mn;
-        const bool rescale = __any_sync(0xffffffffu, alpha != 1.f);
-        if (jl >= 1 && rescale) {
-          // O is stable once the previous tile's P.V retired
-          const int gp = gj - 1;
-          if (!__all_sync(0xffffffffu, pwait(&pv_done[gp & 1], (gp >> 1) & 1, abort, err))) {
-            dead = true;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float v[32];
-            tmem_ld32(lane_addr + colO + c * 32, v);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] *= alpha;
-            tmem_st32(lane_addr + colO + c * 32, v);
-          }
-        }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1]);
-          tmem_st16u(lane_addr + colS + c * 16, pk);
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[sb]);
-      }
-      if (dead) break;
-      // lbuf[ob] is free once the epilogue read item n-2's O and l (it reads
-      // l before releasing O): otherwise a short item could overwrite a row
-      // sum the epilogue has not read yet
-      if (n >= 2 &&
-          !__all_sync(0xffffffffu, pwait(&o_empty[ob], ((n >> 1) - 1) & 1, abort, err)))
-        break;
-      lbuf[ob * kRows + r] = l;
-      mbar_arrive(&l_full[ob]);
-      g += d.ntiles;
-      ++n;
-    }
-  } else {
-    // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    int n = 0;
-    for (int k = 0;; ++k) {
-      const int slot = k & 1;
-      if (!__all_sync(0xffffffffu, pwait(&it_full[slot], (k >> 1) & 1, abort, err))) break;
-      const PItem d = items[slot];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&it_empty[slot]);
-      if (d.hq < 0) break;
-      const int qi = d.q0 + r;
-      __nv_bfloat16* orow = p.out + d.b * p.o_sb + d.hq * p.o_sh +
-                            static_cast<int64_t>(qi < d.T ? qi : 0) * p.o_st;
-      if (d.ntiles == 0) {
-        // no visible key (left padding, kv_len 0): 0/0 rows, as the reference
-        if (qi < d.T) {
-          const uint32_t nan2 = 0x7fc07fc0u;
-          const uint4 nv = make_uint4(nan2, nan2, nan2, nan2);
-#pragma unroll
-          for (int e = 0; e < 128; e += 8) *reinterpret_cast<uint4*>(orow + e) = nv;
-        }
-        continue;
-      }
-      const int ob = n & 1;
-      const bool ok = pwait(&o_full[ob], (n >> 1) & 1, abort, err) &&
-                      pwait(&l_full[ob], (n >> 1) & 1, abort, err);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      tc_fence_after();
-      float v[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + (ob ? kQColO1 : kQColO0) + c * 32, v[c]);
-      const float inv = 1.f / lbuf[ob * kRows + r];  // 0/0 -> NaN: no visible key
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_empty[ob]);  // O[ob] and lbuf[ob] read
-      if (qi < d.T) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            uint4 pk;
-            pk.x = pack_bf16(v[c][e + 0] * inv, v[c][e + 1] * inv);
-            pk.y = pack_bf16(v[c][e + 2] * inv, v[c][e + 3] * inv);
-            pk.z = pack_bf16(v[c][e + 4] * inv, v[c][e + 5] * inv);
-            pk.w = pack_bf16(v[c][e + 6] * inv, v[c][e + 7] * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + e) = pk;
-          }
-        }
-      }
-      ++n;
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 9) {
-    tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
-  }
-  if (tid == 0) {
-    // the last CTA to finish re-arms the work counter for the next launch
-    __threadfence();
-    if (atomicAdd(work + 1, 1) == static_cast<int>(gridDim.x) - 1) {
-      atomicExch(work, 0);
-      atomicExch(work + 1, 0);
-      __threadfence();
-    }
-  }
-}
-
 enum class TcKernel { kOneHead, kHeadPair };
 
 template <bool kPaged, TcKernel kKind>
@@ -1375,43 +876,6 @@ cudaError_t launch_tc_t(const TcParams& prm, const CUtensorMap& qmap, const KVSo
   }
   return launch_k(kern, grid, dim3(kPair ? kPairThreads : kThreads), static_cast<size_t>(smem),
                   stream, prm, qmap, src.kmap, src.vmap);
-}
-
-// The persistent kernel's register split needs exactly kQLaunchRegs
-// registers per thread at launch; any other compiled count (a different
-// toolkit) disables it and the one-CTA-per-tile kernels run instead.
-template <bool kPaged>
-bool persist_usable() {
-  static int state = -1;  // per process: the same binary on every device
-  if (state < 0) {
-    cudaFuncAttributes fa{};
-    state = (cudaFuncGetAttributes(&fa, prefill_tc_persist_kernel<kPaged>) == cudaSuccess &&
-             fa.numRegs == kQLaunchRegs)
-                ? 1
-                : 0;
-  }
-  return state == 1;
-}
-
-template <bool kPaged>
-cudaError_t launch_persist_t(const TcParams& prm, const CUtensorMap& qmap, const KVSource& src,
-                             int32_t* work, int32_t batch, int32_t num_q_heads, int32_t qtiles,
-                             int sms, cudaStream_t stream) {
-  auto kern = prefill_tc_persist_kernel<kPaged>;
-  static int configured_device = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (configured_device != dev) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kQSmemBytes);
-    if (e != cudaSuccess) return e;
-    configured_device = dev;
-  }
-  const int64_t total = static_cast<int64_t>(num_q_heads) * batch * qtiles;
-  const unsigned grid = static_cast<unsigned>(total < sms ? total : sms);
-  return launch_k(kern, dim3(grid), dim3(kQThreads), static_cast<size_t>(kQSmemBytes), stream,
-                  prm, work, static_cast<int32_t>(total), qtiles, batch, num_q_heads, qmap,
-                  src.kmap, src.vmap);
 }
 
 template <TcKernel kKind>
@@ -1459,20 +923,9 @@ cudaError_t launch_prefill_tc(const PrefillLaunch& a, const CUtensorMap& qmap, c
   const int64_t pair_ctas = static_cast<int64_t>(a.num_q_heads / 2) * a.batch * qtiles;
   TcKernel kind = (prm.group % 2 == 0 && qtiles <= 8 && pair_ctas >= sms) ? TcKernel::kHeadPair
                                                                           : TcKernel::kOneHead;
-  // the persistent kernel whenever the caller gave it a work counter
-  bool persist = a.work != nullptr;
   if (const char* force = getenv("PKV_PREFILL_KERNEL")) {
     if (!strcmp(force, "one")) kind = TcKernel::kOneHead;
     if (!strcmp(force, "pair") && prm.group % 2 == 0) kind = TcKernel::kHeadPair;
-    if (!strcmp(force, "one") || !strcmp(force, "pair")) persist = false;
-  }
-  if (persist && (src.paged ? persist_usable<true>() : persist_usable<false>())) {
-    const int64_t total = static_cast<int64_t>(a.num_q_heads) * a.batch * qtiles;
-    if (total < (int64_t(1) << 30))
-      return src.paged ? launch_persist_t<true>(prm, qmap, src, a.work, a.batch, a.num_q_heads,
-                                                static_cast<int32_t>(qtiles), sms, stream)
-                       : launch_persist_t<false>(prm, qmap, src, a.work, a.batch, a.num_q_heads,
-                                                 static_cast<int32_t>(qtiles), sms, stream);
   }
   if (kind == TcKernel::kHeadPair)
     return launch_tc_kind<TcKernel::kHeadPair>(prm, qmap, src,

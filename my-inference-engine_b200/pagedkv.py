@@ -10,7 +10,6 @@ from __future__ import annotations
 
 import ctypes
 import math
-import os
 import threading
 from pathlib import Path
 
@@ -45,14 +44,12 @@ _SIGNATURES = {
          _i32, _i32, _i32, _i32, _i32, _vp, _vp], ctypes.c_int),
     "pkv_decode_workspace_size": ([_i32, _i32, _i32, _i32], ctypes.c_size_t),
     "pkv_decode_plan": ([_i32, _i32, _i32, _i32, _vp], ctypes.c_int),
-    "pkv_prefill_workspace_size": ([], ctypes.c_size_t),
     "pkv_paged_decode": (
         [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
          ctypes.c_float, _vp, _i64, _i64, _vp, ctypes.c_size_t, _vp, _vp], ctypes.c_int),
     "pkv_paged_prefill": (
         [_vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
-         _i32, _i32, _i32, ctypes.c_float, _vp, _i64, _i64, _i64, _vp, ctypes.c_size_t, _vp,
-         _vp], ctypes.c_int),
+         _i32, _i32, _i32, ctypes.c_float, _vp, _i64, _i64, _i64, _vp, _vp], ctypes.c_int),
     "pkv_add_rmsnorm": (
         [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, ctypes.c_float, _vp],
         ctypes.c_int),
@@ -222,24 +219,6 @@ def paged_decode(q: torch.Tensor, k_plane: torch.Tensor, v_plane: torch.Tensor,
     _check(st, "pkv_paged_decode")
 
 
-_prefill_workspaces: dict[int, torch.Tensor] = {}
-
-
-def prefill_workspace(device: torch.device) -> torch.Tensor | None:
-    """The per-device work counters of the persistent prefill kernel (zeroed
-    once; every launch leaves them zero).  PKV_PREFILL_KERNEL=one|pair runs
-    the one-CTA-per-tile kernels instead (returns None)."""
-    if os.environ.get("PKV_PREFILL_KERNEL") in ("one", "pair"):
-        return None
-    idx = device.index if device.index is not None else torch.cuda.current_device()
-    ws = _prefill_workspaces.get(idx)
-    if ws is None:
-        ws = torch.zeros(lib().pkv_prefill_workspace_size(), dtype=torch.uint8,
-                         device=torch.device("cuda", idx))
-        _prefill_workspaces[idx] = ws
-    return ws
-
-
 def paged_prefill(q: torch.Tensor, k_plane: torch.Tensor, v_plane: torch.Tensor,
                   tables: torch.Tensor, rows: torch.Tensor | None, kv_lens: torch.Tensor,
                   max_kv_len: int, out: torch.Tensor, causal: bool, sm_scale: float,
@@ -247,14 +226,12 @@ def paged_prefill(q: torch.Tensor, k_plane: torch.Tensor, v_plane: torch.Tensor,
                   q_lens: torch.Tensor | None = None) -> None:
     """pkv_paged_prefill.  q, out: [B, Hq, T, 128]; q_lens: right-padded rows."""
     B, Hq, T, D = q.shape
-    ws = prefill_workspace(q.device)
     st = lib().pkv_paged_prefill(
         _ptr(q), q.stride(0), q.stride(1), q.stride(2), _ptr(k_plane), _ptr(v_plane),
         k_plane.shape[0], _ptr(tables), tables.stride(0), _ptr(rows), _ptr(kv_lens),
         _ptr(q_lens), max_kv_len,
         B, T, Hq, num_kv_heads, D, int(causal), sm_scale, _ptr(out), out.stride(0),
-        out.stride(1), out.stride(2), _ptr(ws), ws.numel() if ws is not None else 0, _ptr(err),
-        _stream(q.device))
+        out.stride(1), out.stride(2), _ptr(err), _stream(q.device))
     _check(st, "pkv_paged_prefill")
 
 
@@ -264,7 +241,7 @@ def dense_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_lens: 
     """pkv_dense_attention.  q, out: [B, Hq, T, 128]; k, v: [B, Hkv, S, 128]."""
     B, Hq, T, D = q.shape
     Hkv, S = k.shape[1], k.shape[2]
-    ws = decode_workspace(B, Hq, Hkv, S, q.device) if T == 1 else prefill_workspace(q.device)
+    ws = decode_workspace(B, Hq, Hkv, S, q.device) if T == 1 else None
     st = lib().pkv_dense_attention(
         _ptr(q), q.stride(0), q.stride(1), q.stride(2), _ptr(k), k.stride(0), k.stride(1),
         k.stride(2), _ptr(v), v.stride(0), v.stride(1), v.stride(2), _ptr(kv_lens), B, T, S,

@@ -13,8 +13,7 @@ def _header_symbols():
 def test_header_declares_expected_entry_points():
     syms = _header_symbols()
     for s in ["pkv_append_rope", "pkv_paged_decode", "pkv_paged_prefill", "pkv_dense_attention",
-              "pkv_decode_workspace_size", "pkv_decode_plan", "pkv_prefill_workspace_size",
-              "pkv_version", "pkv_status_string", "pkv_last_error"]:
+              "pkv_decode_workspace_size", "pkv_decode_plan", "pkv_version", "pkv_status_string", "pkv_last_error"]:
         assert s in syms
 
 
@@ -78,13 +77,8 @@ def test_entry_points_reject_bad_arguments_without_a_gpu():
     assert st == 2 and b"head_dim" in L.pkv_last_error()
     # Hq not a multiple of Hkv -> PKV_ERR_INVALID
     st = L.pkv_paged_prefill(16, 0, 0, 0, 16, 16, 16, 16, 1, None, 16, None, 1, 1, 1, 12, 5, 128,
-                             1, 1.0, 16, 0, 0, 0, None, 0, None, None)
+                             1, 1.0, 16, 0, 0, 0, None, None)
     assert st == 1
-    # a prefill workspace smaller than pkv_prefill_workspace_size -> PKV_ERR_WORKSPACE
-    assert L.pkv_prefill_workspace_size() == 256
-    st = L.pkv_paged_prefill(16, 0, 0, 0, 16, 16, 16, 16, 1, None, 16, None, 1, 1, 1, 12, 2, 128,
-                             1, 1.0, 16, 0, 0, 0, 16, 64, None, None)
-    assert st == 6 and b"prefill workspace" in L.pkv_last_error()
     # misaligned pool plane -> PKV_ERR_ALIGN
     st = L.pkv_paged_decode(16, 0, 0, 18, 16, 16, 16, 1, None, 16, 1, 1, 12, 2, 128, 1.0,
                             16, 0, 0, None, 0, None, None)

@@ -194,11 +194,11 @@ def test_right_padded_rows_with_q_lens(cuda):
                                                (4, 2, 5, 129, True), (12, 2, 2, 256, False),
                                                (12, 4, 2, 200, True)])
 def test_prefill_kernels_give_identical_bits(cuda, monkeypatch, hq, hkv, B, T, causal):
-    """Three tensor-core prefill kernels: the persistent one (one CTA per SM
-    claiming q-tiles, the default), one head per CTA (P in tensor memory) and
-    two q-heads of an even GQA group per CTA over shared K/V tiles (P staged
-    in shared memory).  The per-head arithmetic is the same, so all give the
-    same bits (and match the oracle).  PKV_PREFILL_KERNEL pins the kernel."""
+    """Two tensor-core prefill kernels: one head per CTA (P in tensor memory)
+    and two q-heads of an even GQA group per CTA over shared K/V tiles (P
+    staged in shared memory).  The per-head arithmetic is the same, so both
+    give the same bits (and match the oracle).  PKV_PREFILL_KERNEL pins the
+    kernel."""
     import pagedkv
 
     g = torch.Generator().manual_seed(hq * 100 + T)
@@ -208,7 +208,7 @@ def test_prefill_kernels_give_identical_bits(cuda, monkeypatch, hq, hkv, B, T, c
     v = torch.randn(B, hkv, S, 128, generator=g).to(torch.bfloat16)
     kv_lens = [S - (b * 13) % 29 for b in range(B)]
     outs = []
-    kernels = ("persist", "one", "pair") if (hq // hkv) % 2 == 0 else ("persist", "one")
+    kernels = ("one", "pair") if (hq // hkv) % 2 == 0 else ("one",)
     for force in kernels:
         monkeypatch.setenv("PKV_PREFILL_KERNEL", force)
         out = torch.full((B, hq, T, 128), 5.0, dtype=torch.bfloat16, device=cuda)
@@ -227,7 +227,7 @@ def test_prefill_kernels_give_identical_bits(cuda, monkeypatch, hq, hkv, B, T, c
 
 @pytest.mark.parametrize("prior,T", [([0, 0, 7], 300), ([1000, 3], 129)])
 def test_paged_prefill_kernels_give_identical_bits(cuda, monkeypatch, prior, T):
-    """All three prefill kernels on block-table K/V (shuffled, poisoned pool)."""
+    """Both prefill kernels on block-table K/V (shuffled, poisoned pool)."""
     from kernels.fa2 import flash_attention
 
     g = torch.Generator().manual_seed(sum(prior) * 3 + T)
@@ -246,7 +246,7 @@ def test_paged_prefill_kernels_give_identical_bits(cuda, monkeypatch, prior, T):
     cache.write(0, step, kn.to(cuda), vn.to(cuda))
     kh, vh = cache.read(0, gidx)
     outs = []
-    for force in ("persist", "one", "pair"):
+    for force in ("one", "pair"):
         monkeypatch.setenv("PKV_PREFILL_KERNEL", force)
         outs.append(flash_attention(q.to(cuda), kh, vh, True, step.kv_lens))
     torch.cuda.synchronize()

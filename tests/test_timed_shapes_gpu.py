@@ -13,7 +13,7 @@ themselves and compare sampled rows with the float64 oracle
   * the engine's 128-row decode of ~2100-token rows (config 4), both with
     the true max_kv_len and with a CUDA graph's capacity as max_kv_len;
   * config 1 as bench.py times it: ONE paged, left-padded 8-row causal
-    launch with starts = kv_len - T, through each tensor-core prefill kernel.
+    launch with starts = kv_len - T, through both tensor-core prefill kernels.
 """
 import math
 
@@ -129,7 +129,7 @@ def test_engine_128_row_decode_launch_vs_oracle(cuda, capacity):
     _check_rows(cache, seqs, lens, q_rot, out, _sample_rows(lens, 16, 1))
 
 
-@pytest.mark.parametrize("kernel", ["persist", "one", "pair"])
+@pytest.mark.parametrize("kernel", ["one", "pair"])
 def test_config1_bench_prefill_launch_vs_oracle(cuda, monkeypatch, kernel):
     """bench.py prefill_run's launch: 8 prompts U[16, 1024] (seed 42) in a
     shuffled pool, then ONE causal launch over the paged K/V with the queries
