@@ -74,6 +74,7 @@ def parse():
     ap.add_argument("--engine4-mixed", type=int, default=None, metavar="MIN_TOKENS",
                     help="also serve config 4 with chat.MIXED_PREFILL_MIN_TOKENS=MIN_TOKENS "
                          "(prompts of at least MIN_TOKENS share the tick's decode forward)")
+    ap.add_argument("--no-fp8", action="store_true", help="skip the FP8-pool decode line")
     ap.add_argument("--no-engine3", action="store_true")
     ap.add_argument("--engine3-chats", type=int, default=256)
     ap.add_argument("--engine3-reply", type=int, default=512)
@@ -250,6 +251,108 @@ class DecodeWorkload:
 
     def step_bytes(self):
         return self.layers * (self.bytes_decode + self.bytes_append)
+
+
+def fp8_decode_bytes(lens):
+    """Algorithmic bytes of one FP8-pool decode launch (one layer): per
+    visible token and KV head 128 B of K, 128 B of V and two fp32 scales."""
+    B = len(lens)
+    kv = sum(lens) * HKV * (2 * D + 8)
+    qo = 2 * B * HQ * D * 2
+    tables = sum(math.ceil(n / 16) for n in lens) * 4 + 2 * B * 4
+    return kv + qo + tables
+
+
+def fp8_decode_run(args, device, bf16_ms_per_step):
+    """BASELINE config 3's decode step on the opt-in FP8 pool
+    (KVCache(kv_format="fp8_e4m3")): the same 256 rows, contexts, block
+    permutation and layer count as the bf16 step, the pool holding random
+    e4m3 history (valid codes, scales U[0.001, 0.011]); per layer the
+    quantising RoPE + append and the FP8 paged decode kernel."""
+    import model
+    from kernels.fa2 import flash_attention
+    from kv_cache import KVCache
+
+    lens = context_lengths(args)
+    B = len(lens)
+    bytes_per_block = L * 2 * 16 * HKV * D * 2
+    num_blocks = int(args.pool_gb * 1e9 // bytes_per_block)  # same blocks as the bf16 pool
+    pitch = math.ceil((args.ctx_max + 1) / 16)
+    cache = KVCache(num_blocks, 16, device, torch.bfloat16, max_seqs=B,
+                    max_blocks_per_seq=pitch, num_layers=args.layers, kv_format="fp8_e4m3")
+    g = torch.Generator().manual_seed(args.seed + 1)
+    cache._free_blocks = torch.randperm(num_blocks, generator=g).tolist()
+    seqs = [cache.alloc() for _ in lens]
+    for s_, n in zip(seqs, lens):
+        cache.ensure_capacity(s_, n)
+        cache._lengths[s_] = n - 1
+    gd = torch.Generator(device=device).manual_seed(args.seed + 2)
+    for l in range(args.layers):
+        body = cache.pool8[l, :, :, :4096]
+        body.random_(0, 256, generator=gd)
+        body[(body & 0x7F) == 0x7F] ^= 1  # no NaN codes
+        sc = torch.rand(num_blocks, HKV, 32, device=device, generator=gd) * 0.01 + 0.001
+        cache.pool8[l, :, :, 4096:] = sc.view(torch.uint8).view(num_blocks, HKV, 128)
+        del sc
+    _, step, _ = cache.prepare(seqs, 1)
+    cos, sin = model.rope_table(pitch * 16, torch.bfloat16, device)
+    q = torch.randn(args.layers, B, HQ, 1, D, device=device, generator=gd).to(torch.bfloat16)
+    k = torch.randn(args.layers, B, HKV, 1, D, device=device, generator=gd).to(torch.bfloat16)
+    v = torch.randn(args.layers, B, HKV, 1, D, device=device, generator=gd).to(torch.bfloat16)
+    q_rot = torch.empty_like(q)
+    out = torch.empty_like(q)
+    handles = [cache.read(l, step) for l in range(args.layers)]
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.layers)]
+
+    def one(events=False):
+        for l in range(args.layers):
+            cache.append(l, step, q[l], k[l], v[l], cos, sin, q_rot[l])
+            kh, vh = handles[l]
+            if events:
+                ev[l][0].record()
+            flash_attention(q_rot[l], kh, vh, False, step.kv_lens, out=out[l])
+            if events:
+                ev[l][1].record()
+
+    for _ in range(max(3, args.warmup)):
+        one()
+    torch.cuda.synchronize()
+    steps = max(5, args.steps // 4)
+    kern = []  # mean decode-launch time of each step (CUDA events on the stream)
+    for _ in range(steps):
+        one(events=True)
+        torch.cuda.synchronize()
+        kern.append(statistics.mean(a.elapsed_time(b) for a, b in ev))
+    cache.check_errors()
+    kern_ms = statistics.mean(kern)
+    # whole-step time without the per-step host sync of the kernel timing
+    t2, t3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t2.record()
+    for _ in range(steps):
+        one()
+    t3.record()
+    t3.synchronize()
+    ms = t2.elapsed_time(t3) / steps
+    bytes_decode = fp8_decode_bytes(lens)
+    step_bytes = args.layers * (bytes_decode + append_bytes(B))
+    peaks, src = measured_peaks()
+    peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
+    achieved = bytes_decode / (kern_ms * 1e-3) / 1e9
+    del cache, q, k, v, q_rot, out, handles
+    torch.cuda.empty_cache()
+    return {"metric": "paged decode-attn HBM GB/s on the FP8 (e4m3) pool", "kv_format": "fp8_e4m3",
+            "value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(ms, 4), "steps": steps,
+            "tokens_per_s": round(B / (ms * 1e-3), 1),
+            "speedup_vs_bf16_step": round(bf16_ms_per_step / ms, 3),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": src,
+                         "kernel": "paged_decode_kernel<fp8>", "bytes_per_launch": bytes_decode,
+                         "avg_launch_ms": round(kern_ms, 4)},
+            "config": f"config3 decode on an FP8 pool: {B} rows, ctx U[{args.ctx_min},"
+                      f"{args.ctx_max}], {num_blocks}-block pool (528 B per token and layer), "
+                      f"{args.layers} layers of quantising RoPE+append + FP8 paged decode"}
 
 
 def e2e_run(w: DecodeWorkload, steps, warmup):
@@ -1286,6 +1389,7 @@ def main():
 
     del w
     torch.cuda.empty_cache()
+    fp8 = None if args.no_fp8 else fp8_decode_run(args, dev, ms)
     prefill = None if args.no_prefill else prefill_run(args, dev, seed=args.seed)
     engine = engine4 = engine4_mixed = None
     if not args.no_engine:
@@ -1375,6 +1479,7 @@ def main():
                 "gpu_launches": args.steps * layers * 2,
                 "kv_bytes_per_step": step_bytes, "prefill": prefill, "engine": engine, "engine_config4": engine4,
                 **({"engine_config3": engine3} if engine3 is not None else {}),
+                **({"fp8_decode": fp8} if fp8 is not None else {}),
                 **({"engine_config4_mixed": engine4_mixed} if engine4_mixed is not None else {})}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -186,6 +186,83 @@ int pkv_dense_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
                         int32_t* err_flag, void* stream);
 
 /*
+ * FP8 (e4m3) KV pool -- opt-in storage format, no counterpart in the
+ * reference (whose pool is the activation dtype, kv_cache.py:20-22).  Half
+ * the bytes per token (528 B per token and layer instead of 1024), so decode
+ * reads half as much; values are rounded to 3 mantissa bits.
+ *
+ * Layout of one layer: [num_blocks][num_kv_heads][pkv_fp8_block_bytes()]
+ * bytes, one chunk per (16-token block, KV head):
+ *   [0, 2048)     K: 16 token rows of 128 bytes.  16-byte group c of token t
+ *                 is stored at group c ^ (t & 7); inside a group, byte 4i+u
+ *                 holds dim 2i+u (u = 0, 1) or dim 2i+8+u-2 (u = 2, 3).
+ *   [2048, 4096)  V transposed: 128 dim rows of 16 bytes; byte 4i+u holds
+ *                 token 2i+u (u = 0, 1) or token 2i+8+u-2 (u = 2, 3).
+ *   [4096, 4160)  fp32 K scale per token, [4160, 4224) fp32 V scale per token.
+ * A row x (128 values of one token and head, k after RoPE) is stored as
+ * e4m3 = RNE(x * (448 / amax)) with saturation, scale = amax / 448, where
+ * amax = max |x| (each quotient one IEEE fp32 division; an all-zero row
+ * stores zeros and scale 1); it reads back as e4m3 * scale.
+ */
+size_t pkv_fp8_block_bytes(void);
+
+/*
+ * pkv_append_rope for the FP8 pool: q is rotated into q_out exactly as
+ * pkv_append_rope does; k (rotated, the same bf16 bits) and v are quantised
+ * into their token's slot of the FP8 pool (kv8_pool = one layer's chunks,
+ * num_blocks blocks).  Block tables, starts, q_lens and padding rows as
+ * pkv_append_rope.  Replaces apply_rope + KVCache.write (model.py:62-65,
+ * kv_cache.py:108-115) for a cache created in FP8 mode.
+ */
+int pkv_append_rope_fp8(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
+                        const void* k, int64_t k_sb, int64_t k_sh, int64_t k_st,
+                        const void* v, int64_t v_sb, int64_t v_sh, int64_t v_st,
+                        const void* rope_cos, const void* rope_sin, int64_t rope_rows,
+                        void* q_out, int64_t qo_sb, int64_t qo_sh, int64_t qo_st,
+                        void* kv8_pool, int64_t num_blocks,
+                        const int32_t* block_tables, int64_t table_pitch,
+                        const int32_t* seq_rows, const int32_t* starts, const int32_t* q_lens,
+                        int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                        int32_t seq_len_q, int32_t head_dim,
+                        int32_t* err_flag, void* stream);
+
+/*
+ * pkv_paged_decode over the FP8 pool (same arguments and workspace sizing,
+ * kv8_pool/num_blocks in place of the two bf16 planes).  Each block is one
+ * bulk copy per KV head; K and V are widened to f16 in registers (exactly),
+ * the products are f16 tensor-core MMAs accumulating in fp32, and the
+ * per-token scales are applied to the scores and the probabilities.
+ * Replaces KVCache.read + fa2_forward at T = 1 (kv_cache.py:117-121,
+ * kernels/fa2.py:23-162) for a cache in FP8 mode.
+ */
+int pkv_paged_decode_fp8(const void* q, int64_t q_sb, int64_t q_sh,
+                         const void* kv8_pool, int64_t num_blocks,
+                         const int32_t* block_tables, int64_t table_pitch,
+                         const int32_t* seq_rows, const int32_t* kv_lens,
+                         int32_t max_kv_len, int32_t batch, int32_t num_q_heads,
+                         int32_t num_kv_heads, int32_t head_dim, float sm_scale,
+                         void* out, int64_t o_sb, int64_t o_sh,
+                         void* workspace, size_t workspace_bytes,
+                         int32_t* err_flag, void* stream);
+
+/*
+ * FP8 pool -> dense bf16 K and V [B][Hkv][seq_len][128] (strides in
+ * elements, rows 8-byte aligned): position p < kv_lens[b] of row b becomes
+ * bf16(e4m3 * scale); later positions are left untouched.  A prefill step
+ * of a cache in FP8 mode attends over these rows with pkv_dense_attention
+ * (the compute-bound prefill reads each key once per query tile, so the
+ * extra copy is small next to it).  Replaces KVCache.read
+ * (kv_cache.py:117-121) for that step.
+ */
+int pkv_fp8_dequant(const void* kv8_pool, int64_t num_blocks,
+                    const int32_t* block_tables, int64_t table_pitch,
+                    const int32_t* seq_rows, const int32_t* kv_lens, int32_t batch,
+                    int32_t num_kv_heads, int32_t seq_len,
+                    void* k_out, int64_t k_sb, int64_t k_sh, int64_t k_ss,
+                    void* v_out, int64_t v_sb, int64_t v_sh, int64_t v_ss,
+                    int32_t* err_flag, void* stream);
+
+/*
  * Residual add + RMSNorm of the Qwen2 block, one launch.
  *
  * Replaces `x = x + sublayer_out` (model.py:136-137) followed by RMSNorm

@@ -287,6 +287,84 @@ int pkv_append_rope(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, con
   return launch_status(pkv::launch_append(a, static_cast<cudaStream_t>(stream)), "append_rope");
 }
 
+// ---------------------------------------------------------------- FP8 pool
+size_t pkv_fp8_block_bytes(void) { return pkv::kFp8HeadBlockBytes; }
+
+static int check_pool8(const void* kv8, int64_t num_blocks, const int32_t* tables, int64_t pitch) {
+  if (!kv8 || !tables) return fail(PKV_ERR_INVALID, "null FP8 pool or block-table pointer");
+  if (num_blocks <= 0 || num_blocks > INT32_MAX / 16)
+    return fail(PKV_ERR_INVALID, "num_blocks (%lld) out of range", (long long)num_blocks);
+  if (pitch <= 0) return fail(PKV_ERR_INVALID, "table_pitch must be positive");
+  if (!aligned16(kv8)) return fail(PKV_ERR_ALIGN, "FP8 pool not 16-byte aligned");
+  return PKV_OK;
+}
+
+int pkv_append_rope_fp8(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, const void* k,
+                        int64_t k_sb, int64_t k_sh, int64_t k_st, const void* v, int64_t v_sb,
+                        int64_t v_sh, int64_t v_st, const void* rope_cos, const void* rope_sin,
+                        int64_t rope_rows, void* q_out, int64_t qo_sb, int64_t qo_sh,
+                        int64_t qo_st, void* kv8_pool, int64_t num_blocks,
+                        const int32_t* block_tables, int64_t table_pitch, const int32_t* seq_rows,
+                        const int32_t* starts, const int32_t* q_lens, int32_t batch,
+                        int32_t num_q_heads, int32_t num_kv_heads, int32_t seq_len_q,
+                        int32_t head_dim, int32_t* err_flag, void* stream) {
+  int st = check_heads(num_q_heads, num_kv_heads, head_dim);
+  if (st) return st;
+  if ((st = check_pool8(kv8_pool, num_blocks, block_tables, table_pitch))) return st;
+  if (batch < 0 || seq_len_q < 0) return fail(PKV_ERR_INVALID, "negative batch / seq_len_q");
+  if (!k || !v || !starts) return fail(PKV_ERR_INVALID, "null k, v or starts");
+  if ((rope_cos == nullptr) != (rope_sin == nullptr))
+    return fail(PKV_ERR_INVALID, "rope_cos and rope_sin must both be set or both NULL");
+  if (rope_cos && rope_rows <= 0) return fail(PKV_ERR_INVALID, "rope_rows must be positive");
+  if (q_out && (!q || !rope_cos)) return fail(PKV_ERR_INVALID, "q_out needs q and rope tables");
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 3u ||
+      (q && (reinterpret_cast<uintptr_t>(q) & 3u)) ||
+      (q_out && (reinterpret_cast<uintptr_t>(q_out) & 3u)) ||
+      (rope_cos && ((reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin)) & 3u)))
+    return fail(PKV_ERR_ALIGN, "append pointers must be 4-byte aligned");
+  if ((k_sb | k_sh | k_st | v_sb | v_sh | v_st) & 1 ||
+      (q_out && ((q_sb | q_sh | q_st | qo_sb | qo_sh | qo_st) & 1)))
+    return fail(PKV_ERR_ALIGN, "append strides must be even (4-byte rows pairs)");
+  if (batch == 0 || seq_len_q == 0) return ok();
+  pkv::AppendLaunch a{};
+  a.q = q; a.q_sb = q_sb; a.q_sh = q_sh; a.q_st = q_st;
+  a.k = k; a.k_sb = k_sb; a.k_sh = k_sh; a.k_st = k_st;
+  a.v = v; a.v_sb = v_sb; a.v_sh = v_sh; a.v_st = v_st;
+  a.rope_cos = rope_cos; a.rope_sin = rope_sin; a.rope_rows = rope_rows;
+  a.q_out = q_out; a.qo_sb = qo_sb; a.qo_sh = qo_sh; a.qo_st = qo_st;
+  a.kv8 = static_cast<uint8_t*>(kv8_pool); a.num_slots = num_blocks * 16;
+  a.tables = block_tables; a.pitch = table_pitch; a.rows = seq_rows; a.starts = starts;
+  a.q_lens = q_lens;
+  a.batch = batch; a.num_q_heads = num_q_heads; a.num_kv_heads = num_kv_heads;
+  a.seq_len_q = seq_len_q; a.err = err_flag;
+  return launch_status(pkv::launch_append(a, static_cast<cudaStream_t>(stream)), "append_rope_fp8");
+}
+
+int pkv_fp8_dequant(const void* kv8_pool, int64_t num_blocks, const int32_t* block_tables,
+                    int64_t table_pitch, const int32_t* seq_rows, const int32_t* kv_lens,
+                    int32_t batch, int32_t num_kv_heads, int32_t seq_len, void* k_out,
+                    int64_t k_sb, int64_t k_sh, int64_t k_ss, void* v_out, int64_t v_sb,
+                    int64_t v_sh, int64_t v_ss, int32_t* err_flag, void* stream) {
+  int st = check_pool8(kv8_pool, num_blocks, block_tables, table_pitch);
+  if (st) return st;
+  if (num_kv_heads <= 0) return fail(PKV_ERR_INVALID, "num_kv_heads must be positive");
+  if (!kv_lens || !k_out || !v_out) return fail(PKV_ERR_INVALID, "null kv_lens, k_out or v_out");
+  if (batch < 0 || seq_len < 0) return fail(PKV_ERR_INVALID, "negative batch / seq_len");
+  if (((reinterpret_cast<uintptr_t>(k_out) | reinterpret_cast<uintptr_t>(v_out)) & 7u) ||
+      ((k_sb | k_sh | k_ss | v_sb | v_sh | v_ss) & 3))
+    return fail(PKV_ERR_ALIGN, "dequant outputs need 8-byte aligned rows");
+  if (batch == 0 || seq_len == 0) return ok();
+  pkv::Fp8DequantLaunch a{};
+  a.kv8 = static_cast<const uint8_t*>(kv8_pool);
+  a.num_blocks = static_cast<int32_t>(num_blocks);
+  a.tables = block_tables; a.pitch = table_pitch; a.rows = seq_rows; a.kv_lens = kv_lens;
+  a.batch = batch; a.num_kv_heads = num_kv_heads; a.seq_len = seq_len;
+  a.k_out = k_out; a.k_sb = k_sb; a.k_sh = k_sh; a.k_ss = k_ss;
+  a.v_out = v_out; a.v_sb = v_sb; a.v_sh = v_sh; a.v_ss = v_ss;
+  a.err = err_flag;
+  return launch_status(pkv::launch_fp8_dequant(a, static_cast<cudaStream_t>(stream)), "fp8_dequant");
+}
+
 size_t pkv_decode_workspace_size(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
                                  int32_t max_kv_len) {
   if (batch <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0) return 0;
@@ -356,6 +434,36 @@ int pkv_paged_decode(const void* q, int64_t q_sb, int64_t q_sh, const void* k_po
   a.kv_lens = kv_lens; a.batch = batch; a.num_q_heads = num_q_heads; a.num_kv_heads = num_kv_heads;
   a.max_kv_len = max_kv_len; a.sm_scale = sm_scale;
   a.workspace = workspace; a.workspace_bytes = workspace_bytes; a.err = err_flag;
+  return decode_common(a, src, static_cast<cudaStream_t>(stream));
+}
+
+int pkv_paged_decode_fp8(const void* q, int64_t q_sb, int64_t q_sh, const void* kv8_pool,
+                         int64_t num_blocks, const int32_t* block_tables, int64_t table_pitch,
+                         const int32_t* seq_rows, const int32_t* kv_lens, int32_t max_kv_len,
+                         int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                         int32_t head_dim, float sm_scale, void* out, int64_t o_sb, int64_t o_sh,
+                         void* workspace, size_t workspace_bytes, int32_t* err_flag,
+                         void* stream) {
+  int st = check_heads(num_q_heads, num_kv_heads, head_dim);
+  if (st) return st;
+  if ((st = check_pool8(kv8_pool, num_blocks, block_tables, table_pitch))) return st;
+  if ((st = check_qo(q, out, q_sb, q_sh, 0, o_sb, o_sh, 0))) return st;
+  if (!kv_lens) return fail(PKV_ERR_INVALID, "null kv_lens");
+  if (batch < 0 || max_kv_len < 0) return fail(PKV_ERR_INVALID, "negative batch / max_kv_len");
+  if (batch == 0) return ok();
+  pkv::KVSource src{};
+  src.paged = true;
+  src.tables = block_tables;
+  src.pitch = table_pitch;
+  src.rows = seq_rows;
+  src.num_blocks = static_cast<int32_t>(num_blocks);
+  pkv::DecodeLaunch a{};
+  a.q = q; a.q_sb = q_sb; a.q_sh = q_sh;
+  a.out = out; a.o_sb = o_sb; a.o_sh = o_sh;
+  a.kv_lens = kv_lens; a.batch = batch; a.num_q_heads = num_q_heads; a.num_kv_heads = num_kv_heads;
+  a.max_kv_len = max_kv_len; a.sm_scale = sm_scale;
+  a.workspace = workspace; a.workspace_bytes = workspace_bytes; a.err = err_flag;
+  a.kv8 = static_cast<const uint8_t*>(kv8_pool);
   return decode_common(a, src, static_cast<cudaStream_t>(stream));
 }
 

@@ -57,21 +57,37 @@ struct DecodeParams {
   float* part_lse;
   int32_t* counters;
   int32_t* err;
+  const uint8_t* kv8;  // FP8 pool of the layer (FP8 kernel only)
 };
 
-template <int NST>
+// FP8 pool: one stage is one (block, KV head) chunk, half the bytes of a bf16
+// stage, so each warp keeps more of them in flight.
+constexpr int kDecodeStagesFp8 = 6;
+
+template <int NST, bool kFp8>
+constexpr int decode_stage_bytes() {
+  return kFp8 ? kFp8HeadBlockBytes : kStageBytes;
+}
+template <int NST, bool kFp8 = false>
 constexpr int decode_smem_bytes() {
-  return kDecodeWarps * NST * kStageBytes + kDecodeWarps * NST * 8 + 1024;
+  return kDecodeWarps * NST * decode_stage_bytes<NST, kFp8>() + kDecodeWarps * NST * 8 + 1024;
 }
 
-template <bool kPaged, int NST>
+// kFp8: K/V come from the FP8 pool (layout in pkv_kernels.h) by one bulk copy
+// per (block, KV head); K and V fragments are e4m3 pairs loaded with
+// ldmatrix and widened to f16 in registers (exact), the products run as f16
+// MMAs with Q scaled by 1/16 (exact: keeps any bf16 q inside f16 range), and
+// each token's K scale (with the 16) multiplies its scores, its V scale its
+// probabilities after the row sum.  Everything else is the bf16 kernel.
+template <bool kPaged, int NST, bool kFp8 = false>
 __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
     paged_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap) {
+  constexpr int kSB = decode_stage_bytes<NST, kFp8>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kDecodeWarps * NST * kStageBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kDecodeWarps * NST * kSB);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -123,12 +139,12 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
   const int span = blk_end - blk_begin;
   const int my_n = span > warp ? (span - warp + kDecodeWarps - 1) / kDecodeWarps : 0;
 
-  uint8_t* wstage = smem + warp * NST * kStageBytes;
+  uint8_t* wstage = smem + warp * NST * kSB;
   uint64_t* wbar = bars + warp * NST;
   if (lane == 0) {
     for (int s = 0; s < NST; ++s) mbar_init(&wbar[s], 1);
     fence_mbar_init();
-    if (warp == 0) {
+    if (warp == 0 && !kFp8) {
       prefetch_tmap(&kmap);
       prefetch_tmap(&vmap);
     }
@@ -139,10 +155,18 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
   auto issue = [&](int i) {
     const int j = blk_begin + warp + kDecodeWarps * i;
     const int st = i % NST;
-    uint8_t* kst = wstage + st * kStageBytes;
+    uint8_t* kst = wstage + st * kSB;
     uint8_t* vst = kst + kHeadBlockBytes;
-    mbar_arrive_expect_tx(&wbar[st], kStageBytes);
-    if constexpr (kPaged) {
+    mbar_arrive_expect_tx(&wbar[st], kSB);
+    if constexpr (kFp8) {
+      int blk = trow[j];
+      if (blk < 0 || blk >= p.num_blocks) {
+        err.raise(PKV_DEVERR_BLOCK_ID);
+        blk = 0;
+      }
+      bulk_load(kst, p.kv8 + (static_cast<int64_t>(blk) * (gridDim.y / p.sub_groups) + kvh) * kSB,
+                kSB, &wbar[st], policy);
+    } else if constexpr (kPaged) {
       int blk = trow[j];
       if (blk < 0 || blk >= p.num_blocks) {
         err.raise(PKV_DEVERR_BLOCK_ID);
@@ -175,6 +199,14 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
     for (int kk = 0; kk < 8; ++kk) {
       qb[kk][0] = live ? *reinterpret_cast<const uint32_t*>(qp + kk * 16 + 2 * t) : 0u;
       qb[kk][1] = live ? *reinterpret_cast<const uint32_t*>(qp + kk * 16 + 8 + 2 * t) : 0u;
+      if constexpr (kFp8) {  // bf16 pairs -> f16 pairs of q / 16
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(&qb[kk][h]);
+          const float2 f = __bfloat1622float2(v);
+          qb[kk][h] = pack_f16(f.x * 0.0625f, f.y * 0.0625f);
+        }
+      }
     }
   }
 
@@ -197,26 +229,50 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
     ok = mbar_wait(&wbar[st], (i / NST) & 1, err);
     ok = __all_sync(0xffffffffu, ok);
     if (!ok) break;
-    const uint32_t kst = smem_u32(wstage + st * kStageBytes);
-    const uint32_t vst = kst + kHeadBlockBytes;
+    const uint32_t kst = smem_u32(wstage + st * kSB);
+    const uint32_t vst = kst + (kFp8 ? kFp8VOff : kHeadBlockBytes);
     const int j = blk_begin + warp + kDecodeWarps * i;
 
     float s[4] = {0.f, 0.f, 0.f, 0.f};
     float s2[4] = {0.f, 0.f, 0.f, 0.f};
+    float ks0 = p.scale_log2, ks1 = p.scale_log2;  // score scale of tokens g and g+8
+    float vs0 = 1.f, vs1 = 1.f;                    // probability scale of tokens g, g+8
+    if constexpr (kFp8) {
+      // ldmatrix of e4m3 pairs: matrix m covers tokens (m & 1) * 8 + 0..7 of
+      // 16-dim group 2c + (m >> 1); each register widens to the A fragment
+      // halves of one k-step (a0 | a2 from the low | high pair)
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      uint32_t a0, a1, a2, a3;
-      ldsm_x4(kst + (kk >> 2) * kBoxBytes + swz128(a_row, (kk & 3) * 2 + a_chk), a0, a1, a2, a3);
-      if (kk & 1)
-        mma_bf16(s2, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
-      else
-        mma_bf16(s, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+      for (int c = 0; c < 4; ++c) {
+        const int chunk = 2 * c + a_chk;
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4(kst + a_row * 128 + ((chunk ^ (a_row & 7)) << 4), r0, r1, r2, r3);
+        mma_f16(s, e4m3x2_to_f16x2(r0), e4m3x2_to_f16x2(r1), e4m3x2_to_f16x2(r0 >> 16),
+                e4m3x2_to_f16x2(r1 >> 16), qb[2 * c][0], qb[2 * c][1]);
+        mma_f16(s2, e4m3x2_to_f16x2(r2), e4m3x2_to_f16x2(r3), e4m3x2_to_f16x2(r2 >> 16),
+                e4m3x2_to_f16x2(r3 >> 16), qb[2 * c + 1][0], qb[2 * c + 1][1]);
+      }
+      const float* sc = reinterpret_cast<const float*>(wstage + st * kSB + kFp8KScaleOff);
+      ks0 = sc[g] * (16.f * p.scale_log2);
+      ks1 = sc[g + 8] * (16.f * p.scale_log2);
+      vs0 = sc[16 + g];
+      vs1 = sc[16 + g + 8];
+    } else {
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(kst + (kk >> 2) * kBoxBytes + swz128(a_row, (kk & 3) * 2 + a_chk), a0, a1, a2,
+                a3);
+        if (kk & 1)
+          mma_bf16(s2, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+        else
+          mma_bf16(s, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+      }
     }
     const int tok0 = j * kBlockTokens + g;
-    float x0 = (s[0] + s2[0]) * p.scale_log2;
-    float x1 = (s[1] + s2[1]) * p.scale_log2;
-    float x2 = (s[2] + s2[2]) * p.scale_log2;
-    float x3 = (s[3] + s2[3]) * p.scale_log2;
+    float x0 = (s[0] + s2[0]) * ks0;
+    float x1 = (s[1] + s2[1]) * ks0;
+    float x2 = (s[2] + s2[2]) * ks1;
+    float x3 = (s[3] + s2[3]) * ks1;
     if (tok0 >= kv_len) x0 = x1 = -INFINITY;
     if (tok0 + 8 >= kv_len) x2 = x3 = -INFINITY;
 
@@ -243,13 +299,31 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
       o[mt][2] *= al0;
       o[mt][3] *= al1;
     }
-    const uint32_t pb0 = movm_t(pack_bf16(p0, p1));
-    const uint32_t pb1 = movm_t(pack_bf16(p2, p3));
+    if constexpr (kFp8) {
+      const uint32_t pb0 = movm_t(pack_f16(p0 * vs0, p1 * vs0));
+      const uint32_t pb1 = movm_t(pack_f16(p2 * vs1, p3 * vs1));
+      // V^T rows (dims) of 16 e4m3 tokens: matrix m covers dims
+      // 16 * (2c + (m >> 1)) + (m & 1) * 8 + 0..7
 #pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-      uint32_t a0, a1, a2, a3;
-      ldsm_x4_t(vst + (mt >> 2) * kBoxBytes + swz128(v_tok, (mt & 3) * 2 + v_chk), a0, a1, a2, a3);
-      mma_bf16(o[mt], a0, a1, a2, a3, pb0, pb1);
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4(vst + (32 * c + (lane & 7) + ((lane >> 3) & 1) * 8 + (lane >> 4) * 16) * 16, r0,
+                r1, r2, r3);
+        mma_f16(o[2 * c], e4m3x2_to_f16x2(r0), e4m3x2_to_f16x2(r1), e4m3x2_to_f16x2(r0 >> 16),
+                e4m3x2_to_f16x2(r1 >> 16), pb0, pb1);
+        mma_f16(o[2 * c + 1], e4m3x2_to_f16x2(r2), e4m3x2_to_f16x2(r3),
+                e4m3x2_to_f16x2(r2 >> 16), e4m3x2_to_f16x2(r3 >> 16), pb0, pb1);
+      }
+    } else {
+      const uint32_t pb0 = movm_t(pack_bf16(p0, p1));
+      const uint32_t pb1 = movm_t(pack_bf16(p2, p3));
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_t(vst + (mt >> 2) * kBoxBytes + swz128(v_tok, (mt & 3) * 2 + v_chk), a0, a1, a2,
+                  a3);
+        mma_bf16(o[mt], a0, a1, a2, a3, pb0, pb1);
+      }
     }
     __syncwarp();
     if (lane == 0 && i + NST < my_n) issue(i + NST);
@@ -401,12 +475,13 @@ constexpr int kMaxParts = 16;
 constexpr int64_t kBusyCtas = 600;
 constexpr int kMinBlocksPerPartSmall = kDecodeWarps;
 
-template <bool kPaged>
+template <bool kPaged, bool kFp8 = false>
 cudaError_t launch_decode_t(const DecodeParams& prm, const KVSource& src, dim3 grid,
                             cudaStream_t stream) {
-  constexpr int NST = kDecodeStages;
-  auto kern = paged_decode_kernel<kPaged, NST>;
-  constexpr int smem = decode_smem_bytes<NST>();
+  constexpr int NST = kFp8 ? kDecodeStagesFp8 : kDecodeStages;
+  auto kern = paged_decode_kernel<kPaged, NST, kFp8>;
+  constexpr int smem = decode_smem_bytes<NST, kFp8>();
+  static_assert(smem <= 113 * 1024, "two decode CTAs must fit on one SM");
   static int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -472,6 +547,7 @@ cudaError_t launch_decode(const DecodeLaunch& a, const KVSource& src, const Deco
   prm.min_blocks_per_part = plan.min_blocks_per_part;
   prm.scale_log2 = a.sm_scale * 1.4426950408889634f;
   prm.err = a.err;
+  prm.kv8 = a.kv8;
   if (plan.max_parts > 1) {
     const int64_t units = static_cast<int64_t>(a.batch) * a.num_kv_heads * plan.sub_groups;
     const int64_t slots = units * plan.max_parts;
@@ -484,6 +560,7 @@ cudaError_t launch_decode(const DecodeLaunch& a, const KVSource& src, const Deco
     prm.part_o = prm.part_lse + slots * 8;
   }
   dim3 grid(plan.max_parts, a.num_kv_heads * plan.sub_groups, a.batch);
+  if (a.kv8) return launch_decode_t<true, true>(prm, src, grid, stream);
   return src.paged ? launch_decode_t<true>(prm, src, grid, stream)
                    : launch_decode_t<false>(prm, src, grid, stream);
 }

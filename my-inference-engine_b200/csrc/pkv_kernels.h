@@ -21,6 +21,22 @@ struct KVSource {
   int32_t num_blocks;
 };
 
+// FP8 (e4m3) KV pool, opt-in: per layer [num_blocks][Hkv][kFp8HeadBlockBytes],
+// one chunk per (16-token block, KV head), fetched by one bulk copy:
+//   [0, 2048)     K, 16 token rows of 128 bytes; 16-byte chunk c of token t
+//                 sits at chunk c ^ (t & 7) (conflict-free ldmatrix); inside
+//                 a chunk byte 4i+u holds dim 2i+u (u < 2) or 2i+8+u-2 (u >= 2),
+//                 the order an m16n8k16 A fragment wants
+//   [2048, 4096)  V transposed, 128 dim rows of 16 bytes; byte 4i+u holds
+//                 token 2i+u (u < 2) or 2i+8+u-2 (u >= 2)
+//   [4096, 4160)  fp32 dequantisation scale of each token's K row
+//   [4160, 4224)  fp32 scale of each token's V row
+// value = e4m3 * scale, scale = amax(|row|) / 448 (1 for an all-zero row).
+constexpr int kFp8VOff = 2048;
+constexpr int kFp8KScaleOff = 4096;
+constexpr int kFp8VScaleOff = 4160;
+constexpr int kFp8HeadBlockBytes = 4224;
+
 struct DecodeLaunch {
   const void* q;
   int64_t q_sb, q_sh;
@@ -33,6 +49,7 @@ struct DecodeLaunch {
   void* workspace;
   size_t workspace_bytes;
   int32_t* err;
+  const uint8_t* kv8 = nullptr;  // FP8 pool of one layer (KVSource.paged tables)
 };
 
 struct DecodePlan {
@@ -94,8 +111,26 @@ struct AppendLaunch {
   const int32_t* q_lens;  // nullable
   int32_t batch, num_q_heads, num_kv_heads, seq_len_q;
   int32_t* err;
+  uint8_t* kv8 = nullptr;  // FP8 pool of one layer: k/v quantised there (k_pool/v_pool unused)
 };
 cudaError_t launch_append(const AppendLaunch& a, cudaStream_t stream);
+
+// FP8 pool -> dense bf16 K and V [B][Hkv][S][128] (positions < kv_lens[b]).
+struct Fp8DequantLaunch {
+  const uint8_t* kv8;
+  int32_t num_blocks;
+  const int32_t* tables;
+  int64_t pitch;
+  const int32_t* rows;
+  const int32_t* kv_lens;
+  int32_t batch, num_kv_heads, seq_len;
+  void* k_out;
+  int64_t k_sb, k_sh, k_ss;
+  void* v_out;
+  int64_t v_sb, v_sh, v_ss;
+  int32_t* err;
+};
+cudaError_t launch_fp8_dequant(const Fp8DequantLaunch& a, cudaStream_t stream);
 
 struct NormLaunch {
   const void* a;

@@ -59,6 +59,22 @@ def flash_attention(Q, K, V, is_causal=False, kv_lens=None, out=None):
     if paged:
         assert isinstance(V, PagedKV) and V.step is K.step, "K and V handles come from one read()"
         cache, step = K.cache, K.step
+        if cache.fp8:
+            if seq_len == 1:
+                pagedkv.paged_decode_fp8(Q[:, :, 0], cache.pool8[K.layer_idx], cache.block_tables,
+                                         step.rows, kv_lens, step.max_kv_len, out[:, :, 0],
+                                         sm_scale, cache.err_flag)
+            else:
+                # prefill over an FP8 pool: the rows' K/V dequantised into bf16
+                # planes (one block per 16 positions, identity tables), then
+                # the bf16 tensor-core prefill kernel
+                S = step.max_kv_len
+                kd, vd = cache.dequant_step(K.layer_idx, step, S)
+                S16 = kd.shape[0] // batch_size
+                tables = cache.identity_tables(batch_size, S16, Q.device)
+                pagedkv.paged_prefill(Q, kd, vd, tables, None, kv_lens, S, out, bool(is_causal),
+                                      sm_scale, num_kv_heads, cache.err_flag, step.q_lens)
+            return out
         if seq_len == 1:
             pagedkv.paged_decode(Q[:, :, 0], K.plane, V.plane, cache.block_tables, step.rows,
                                  kv_lens, step.max_kv_len, out[:, :, 0], sm_scale, num_kv_heads,

@@ -68,27 +68,36 @@ class PagedKV:
         return self.cache.buf[self.layer_idx, self.which]
 
     @property
+    def fp8(self) -> bool:
+        return self.cache.fp8
+
+    @property
     def shape(self) -> torch.Size:
         return torch.Size((self.step.batch, NUM_KV_HEADS, self.step.max_kv_len, HEAD_DIM))
 
     @property
     def dtype(self) -> torch.dtype:
-        return self.cache.buf.dtype
+        return torch.bfloat16  # what the attention sees (an FP8 pool reads back as bf16)
 
     @property
     def device(self) -> torch.device:
-        return self.cache.buf.device
+        return self.cache.device
 
     @property
     def is_cuda(self) -> bool:
-        return self.cache.buf.is_cuda
+        return self.cache.device.type == "cuda"
 
     def materialize(self) -> torch.Tensor:
         """Dense [B, Hkv, S, D] copy (test/debug only; the kernels never use it).
         Positions past a row's kv_len read block 0's slots, as the reference's
-        padded gather does (kv_cache.py:95)."""
+        padded gather does (kv_cache.py:95); an FP8 pool reads back as
+        bf16(e4m3 * scale), zeros past kv_len."""
         c, st = self.cache, self.step
         S = st.max_kv_len
+        if c.fp8:
+            kd, vd = c.dequant_step(self.layer_idx, st, S)
+            return (kd if self.which == 0 else vd).view(st.batch, -1, NUM_KV_HEADS, HEAD_DIM)[
+                :, :S].transpose(1, 2)
         nb = math.ceil(S / c.block_size)
         tbl = c.block_tables[st.rows.long(), :nb].long()
         lens_blocks = (st.kv_lens.long() + c.block_size - 1) // c.block_size
@@ -254,16 +263,26 @@ class KVCache(BlockTables):
     """
 
     def __init__(self, num_blocks, block_size, device, dtype, max_seqs=None,
-                 max_blocks_per_seq=None, num_layers=NUM_LAYERS):
+                 max_blocks_per_seq=None, num_layers=NUM_LAYERS, kv_format="bf16"):
         device = torch.device(device)
         assert device.type == "cuda", "KVCache needs a CUDA device (no CPU fallback)"
         assert block_size == BLOCK_SIZE, f"block_size must be {BLOCK_SIZE}"
         assert dtype == torch.bfloat16, "the paged kernels store bf16 K/V"
+        assert kv_format in ("bf16", "fp8_e4m3"), "kv_format is 'bf16' or 'fp8_e4m3'"
         super().__init__(num_blocks, block_size, max_seqs, max_blocks_per_seq)
         # num_layers < 28 only for single-layer attention workloads (kernel
         # tests and benchmarks); the model needs the full pool
-        self.buf = torch.zeros(num_layers, 2, num_blocks * block_size, NUM_KV_HEADS, HEAD_DIM,
-                               device=device, dtype=dtype)
+        self.kv_format = kv_format
+        if kv_format == "fp8_e4m3":
+            # opt-in FP8 pool: [layer][block][kv head][chunk] bytes, half the
+            # bytes per token (layout in include/pagedkv.h); no bf16 planes
+            self.buf = None
+            self.pool8 = torch.zeros(num_layers, num_blocks, NUM_KV_HEADS,
+                                     pagedkv.fp8_block_bytes(), device=device, dtype=torch.uint8)
+        else:
+            self.pool8 = None
+            self.buf = torch.zeros(num_layers, 2, num_blocks * block_size, NUM_KV_HEADS,
+                                   HEAD_DIM, device=device, dtype=dtype)
         self.device = device
         self.block_tables = torch.zeros(self.max_seqs, self.table_pitch, dtype=torch.int32,
                                         device=device)
@@ -299,11 +318,20 @@ class KVCache(BlockTables):
         step = PagedStep(self, T, starts, dev[0], dev[1], dev[2], max(starts) + T)
         return starts, step, step
 
+    @property
+    def fp8(self) -> bool:
+        return self.pool8 is not None
+
     def write(self, layer_idx, slot_mapping, k, v):
         """Scatter this step's new k/v for one layer into their physical slots
         (reference kv_cache.py:108-115).  k, v: [B, NUM_KV_HEADS, T, HEAD_DIM];
-        slot_mapping is the PagedStep from prepare()."""
+        slot_mapping is the PagedStep from prepare().  FP8 mode quantises them."""
         step = slot_mapping
+        if self.fp8:
+            pagedkv.append_rope_fp8(None, k, v, None, None, None, self.pool8[layer_idx],
+                                    self.block_tables, step.rows, step.starts, self.err_flag,
+                                    step.q_lens)
+            return
         pagedkv.append_rope(None, k, v, None, None, None, self.buf[layer_idx, 0],
                             self.buf[layer_idx, 1], self.block_tables, step.rows, step.starts,
                             self.err_flag, step.q_lens)
@@ -311,9 +339,37 @@ class KVCache(BlockTables):
     def append(self, layer_idx, step, q, k, v, rope_cos, rope_sin, q_out):
         """Fused apply_rope(q, k) + write (model.py:92-96): roped q goes to
         q_out, roped k and v into the pool.  rope_cos/sin: bf16 [positions, 128]."""
+        if self.fp8:
+            pagedkv.append_rope_fp8(q, k, v, rope_cos, rope_sin, q_out, self.pool8[layer_idx],
+                                    self.block_tables, step.rows, step.starts, self.err_flag,
+                                    step.q_lens)
+            return
         pagedkv.append_rope(q, k, v, rope_cos, rope_sin, q_out, self.buf[layer_idx, 0],
                             self.buf[layer_idx, 1], self.block_tables, step.rows, step.starts,
                             self.err_flag, step.q_lens)
+
+    def dequant_step(self, layer_idx, step, S):
+        """FP8 mode: the step's rows (positions < kv_len) as bf16 K and V
+        planes in the bf16 pool layout, [B * S16, NUM_KV_HEADS, HEAD_DIM] each
+        with S16 = S rounded up to 16: row b's position p at plane slot
+        b * S16 + p, i.e. row b owns blocks b * S16 / 16 ... (see
+        identity_tables).  Positions past kv_len are zero."""
+        B = step.batch
+        S16 = -(-max(S, 1) // BLOCK_SIZE) * BLOCK_SIZE
+        kd = torch.zeros(B * S16, NUM_KV_HEADS, HEAD_DIM, device=self.device, dtype=torch.bfloat16)
+        vd = torch.zeros_like(kd)
+        # [B, Hkv, S16, D] views of the [B*S16, Hkv, D] planes
+        k4 = kd.view(B, S16, NUM_KV_HEADS, HEAD_DIM).transpose(1, 2)
+        v4 = vd.view(B, S16, NUM_KV_HEADS, HEAD_DIM).transpose(1, 2)
+        pagedkv.fp8_dequant(self.pool8[layer_idx], self.block_tables, step.rows, step.kv_lens,
+                            S16, k4, v4, self.err_flag)
+        return kd, vd
+
+    @staticmethod
+    def identity_tables(B, S16, device):
+        """Block tables of dequant_step's planes: row b -> blocks b*n .. b*n+n-1."""
+        n = S16 // BLOCK_SIZE
+        return torch.arange(B * n, device=device, dtype=torch.int32).view(B, n)
 
     def read(self, layer_idx, gather_idx):
         """This layer's K and V as zero-copy PagedKV handles (the reference

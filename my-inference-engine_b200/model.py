@@ -258,7 +258,9 @@ class Qwen2ForCausalLM(torch.nn.Module):
         if segs is None:
             segs = [(0, B, T, step, is_causal)]
         use = {op: self.skinny_linears and N <= lim for op, lim in self.skinny_rows.items()}
-        fused_qkv = use["qkv"] and len(segs) == 1
+        # the q/k/v GEMM's fused RoPE + append epilogue writes the bf16 pool;
+        # an FP8 pool takes the separate quantising append
+        fused_qkv = use["qkv"] and len(segs) == 1 and not cache.fp8
         err = cache.err_flag
         m = None
         last = len(self.layers) - 1

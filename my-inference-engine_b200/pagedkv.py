@@ -50,6 +50,17 @@ _SIGNATURES = {
     "pkv_paged_prefill": (
         [_vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
          _i32, _i32, _i32, ctypes.c_float, _vp, _i64, _i64, _i64, _vp, _vp], ctypes.c_int),
+    "pkv_fp8_block_bytes": ([], ctypes.c_size_t),
+    "pkv_append_rope_fp8": (
+        [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64,
+         _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _vp,
+         _i32, _i32, _i32, _i32, _i32, _vp, _vp], ctypes.c_int),
+    "pkv_paged_decode_fp8": (
+        [_vp, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
+         ctypes.c_float, _vp, _i64, _i64, _vp, ctypes.c_size_t, _vp, _vp], ctypes.c_int),
+    "pkv_fp8_dequant": (
+        [_vp, _i64, _vp, _i64, _vp, _vp, _i32, _i32, _i32, _vp, _i64, _i64, _i64, _vp, _i64,
+         _i64, _i64, _vp, _vp], ctypes.c_int),
     "pkv_add_rmsnorm": (
         [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, ctypes.c_float, _vp],
         ctypes.c_int),
@@ -217,6 +228,60 @@ def paged_decode(q: torch.Tensor, k_plane: torch.Tensor, v_plane: torch.Tensor,
         num_kv_heads, D, sm_scale, _ptr(out), out.stride(0), out.stride(1),
         _ptr(ws), ws.numel() if ws is not None else 0, _ptr(err), _stream(q.device))
     _check(st, "pkv_paged_decode")
+
+
+# ---------------------------------------------------------------- FP8 pool
+def fp8_block_bytes() -> int:
+    """Bytes of one (16-token block, KV head) chunk of the FP8 pool."""
+    return int(lib().pkv_fp8_block_bytes())
+
+
+def append_rope_fp8(q: torch.Tensor | None, k: torch.Tensor, v: torch.Tensor,
+                    rope_cos: torch.Tensor | None, rope_sin: torch.Tensor | None,
+                    q_out: torch.Tensor | None, pool8: torch.Tensor, tables: torch.Tensor,
+                    rows: torch.Tensor | None, starts: torch.Tensor,
+                    err: torch.Tensor | None = None, q_lens: torch.Tensor | None = None) -> None:
+    """pkv_append_rope_fp8.  q/k/v [B, H, T, 128]; pool8 uint8 [blocks, Hkv, chunk]."""
+    B, Hkv, T, D = k.shape
+    Hq = q.shape[1] if q is not None else Hkv
+    qs = q.stride() if q is not None else (0, 0, 0, 1)
+    qos = q_out.stride() if q_out is not None else (0, 0, 0, 1)
+    st = lib().pkv_append_rope_fp8(
+        _ptr(q), qs[0], qs[1], qs[2], _ptr(k), k.stride(0), k.stride(1), k.stride(2),
+        _ptr(v), v.stride(0), v.stride(1), v.stride(2),
+        _ptr(rope_cos), _ptr(rope_sin), rope_cos.shape[0] if rope_cos is not None else 0,
+        _ptr(q_out), qos[0], qos[1], qos[2], _ptr(pool8), pool8.shape[0],
+        _ptr(tables), tables.stride(0), _ptr(rows), _ptr(starts), _ptr(q_lens),
+        B, Hq, Hkv, T, D, _ptr(err), _stream(k.device))
+    _check(st, "pkv_append_rope_fp8")
+
+
+def paged_decode_fp8(q: torch.Tensor, pool8: torch.Tensor, tables: torch.Tensor,
+                     rows: torch.Tensor | None, kv_lens: torch.Tensor, max_kv_len: int,
+                     out: torch.Tensor, sm_scale: float, err: torch.Tensor | None = None) -> None:
+    """pkv_paged_decode_fp8.  q, out: [B, Hq, 128]; pool8 uint8 [blocks, Hkv, chunk]."""
+    B, Hq, D = q.shape
+    Hkv = pool8.shape[1]
+    ws = decode_workspace(B, Hq, Hkv, max_kv_len, q.device)
+    st = lib().pkv_paged_decode_fp8(
+        _ptr(q), q.stride(0), q.stride(1), _ptr(pool8), pool8.shape[0],
+        _ptr(tables), tables.stride(0), _ptr(rows), _ptr(kv_lens), max_kv_len, B, Hq,
+        Hkv, D, sm_scale, _ptr(out), out.stride(0), out.stride(1),
+        _ptr(ws), ws.numel() if ws is not None else 0, _ptr(err), _stream(q.device))
+    _check(st, "pkv_paged_decode_fp8")
+
+
+def fp8_dequant(pool8: torch.Tensor, tables: torch.Tensor, rows: torch.Tensor | None,
+                kv_lens: torch.Tensor, seq_len: int, k_out: torch.Tensor, v_out: torch.Tensor,
+                err: torch.Tensor | None = None) -> None:
+    """pkv_fp8_dequant into dense bf16 k_out / v_out [B, Hkv, seq_len, 128]."""
+    B = k_out.shape[0]
+    st = lib().pkv_fp8_dequant(
+        _ptr(pool8), pool8.shape[0], _ptr(tables), tables.stride(0), _ptr(rows), _ptr(kv_lens),
+        B, pool8.shape[1], seq_len, _ptr(k_out), k_out.stride(0), k_out.stride(1),
+        k_out.stride(2), _ptr(v_out), v_out.stride(0), v_out.stride(1), v_out.stride(2),
+        _ptr(err), _stream(k_out.device))
+    _check(st, "pkv_fp8_dequant")
 
 
 def paged_prefill(q: torch.Tensor, k_plane: torch.Tensor, v_plane: torch.Tensor,
