@@ -12,6 +12,8 @@
 //
 // One warp per (row, step token, head-of-{q, k, v}); lane l owns dims
 // {2l, 2l+1} and their rotation partners {64+2l, 64+2l+1}.
+#include <cuda_fp8.h>
+
 #include "pkv_device.cuh"
 #include "pkv_kernels.h"
 

@@ -62,7 +62,7 @@ struct DecodeParams {
 
 // FP8 pool: one stage is one (block, KV head) chunk, half the bytes of a bf16
 // stage, so each warp keeps more of them in flight.
-constexpr int kDecodeStagesFp8 = 6;
+constexpr int kDecodeStagesFp8 = 3;  // 4 CTAs per SM: 16 warps hide the per-block latency
 
 template <int NST, bool kFp8>
 constexpr int decode_stage_bytes() {
@@ -80,7 +80,7 @@ constexpr int decode_smem_bytes() {
 // each token's K scale (with the 16) multiplies its scores, its V scale its
 // probabilities after the row sum.  Everything else is the bf16 kernel.
 template <bool kPaged, int NST, bool kFp8 = false>
-__global__ void __launch_bounds__(kDecodeWarps * 32, 2)
+__global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? 4 : 2)
     paged_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap) {
   constexpr int kSB = decode_stage_bytes<NST, kFp8>();
@@ -244,12 +244,14 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int chunk = 2 * c + a_chk;
-        uint32_t r0, r1, r2, r3;
+        uint32_t r0, r1, r2, r3, a0, a1, a2, a3, b0, b1, b2, b3;
         ldsm_x4(kst + a_row * 128 + ((chunk ^ (a_row & 7)) << 4), r0, r1, r2, r3);
-        mma_f16(s, e4m3x2_to_f16x2(r0), e4m3x2_to_f16x2(r1), e4m3x2_to_f16x2(r0 >> 16),
-                e4m3x2_to_f16x2(r1 >> 16), qb[2 * c][0], qb[2 * c][1]);
-        mma_f16(s2, e4m3x2_to_f16x2(r2), e4m3x2_to_f16x2(r3), e4m3x2_to_f16x2(r2 >> 16),
-                e4m3x2_to_f16x2(r3 >> 16), qb[2 * c + 1][0], qb[2 * c + 1][1]);
+        e4m3x4_to_f16x2x2(r0, a0, a2);
+        e4m3x4_to_f16x2x2(r1, a1, a3);
+        e4m3x4_to_f16x2x2(r2, b0, b2);
+        e4m3x4_to_f16x2x2(r3, b1, b3);
+        mma_f16(s, a0, a1, a2, a3, qb[2 * c][0], qb[2 * c][1]);
+        mma_f16(s2, b0, b1, b2, b3, qb[2 * c + 1][0], qb[2 * c + 1][1]);
       }
       const float* sc = reinterpret_cast<const float*>(wstage + st * kSB + kFp8KScaleOff);
       ks0 = sc[g] * (16.f * p.scale_log2);
@@ -306,13 +308,15 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 2)
       // 16 * (2c + (m >> 1)) + (m & 1) * 8 + 0..7
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t r0, r1, r2, r3;
+        uint32_t r0, r1, r2, r3, a0, a1, a2, a3, b0, b1, b2, b3;
         ldsm_x4(vst + (32 * c + (lane & 7) + ((lane >> 3) & 1) * 8 + (lane >> 4) * 16) * 16, r0,
                 r1, r2, r3);
-        mma_f16(o[2 * c], e4m3x2_to_f16x2(r0), e4m3x2_to_f16x2(r1), e4m3x2_to_f16x2(r0 >> 16),
-                e4m3x2_to_f16x2(r1 >> 16), pb0, pb1);
-        mma_f16(o[2 * c + 1], e4m3x2_to_f16x2(r2), e4m3x2_to_f16x2(r3),
-                e4m3x2_to_f16x2(r2 >> 16), e4m3x2_to_f16x2(r3 >> 16), pb0, pb1);
+        e4m3x4_to_f16x2x2(r0, a0, a2);
+        e4m3x4_to_f16x2x2(r1, a1, a3);
+        e4m3x4_to_f16x2x2(r2, b0, b2);
+        e4m3x4_to_f16x2x2(r3, b1, b3);
+        mma_f16(o[2 * c], a0, a1, a2, a3, pb0, pb1);
+        mma_f16(o[2 * c + 1], b0, b1, b2, b3, pb0, pb1);
       }
     } else {
       const uint32_t pb0 = movm_t(pack_bf16(p0, p1));
@@ -481,7 +485,7 @@ cudaError_t launch_decode_t(const DecodeParams& prm, const KVSource& src, dim3 g
   constexpr int NST = kFp8 ? kDecodeStagesFp8 : kDecodeStages;
   auto kern = paged_decode_kernel<kPaged, NST, kFp8>;
   constexpr int smem = decode_smem_bytes<NST, kFp8>();
-  static_assert(smem <= 113 * 1024, "two decode CTAs must fit on one SM");
+  static_assert(smem <= (kFp8 ? 56 : 113) * 1024, "decode CTAs per SM (2 bf16, 4 FP8)");
   static int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);

@@ -10,7 +10,6 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
-#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdlib.h>
@@ -219,12 +218,13 @@ __device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Two e4m3 values (low byte first) -> f16x2 (exact: every e4m3 value is an
-// f16 value).
-__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two) {
-  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(
-      static_cast<__nv_fp8x2_storage_t>(two & 0xFFFFu), __NV_E4M3);
-  return static_cast<uint32_t>(h.x) | (static_cast<uint32_t>(h.y) << 16);
+// Four e4m3 values (byte 0 first) -> two f16x2 registers: lo = bytes 0, 1,
+// hi = bytes 2, 3 (exact: every e4m3 value is an f16 value).
+__device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t four, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, l;\n\tcvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(four));
 }
 
 // Byte offset of 16-byte chunk `chunk` (0..7) of row `row` inside a
