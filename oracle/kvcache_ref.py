@@ -19,7 +19,11 @@ NUM_LAYERS, NUM_KV_HEADS, HEAD_DIM = 28, 2, 128
 
 class RefKVCache:
     def __init__(self, num_blocks, block_size=16, dtype=torch.float32, num_layers=NUM_LAYERS,
-                 with_pool=True):
+                 with_pool=True, fp8=False):
+        # fp8: every written k / v row goes through the FP8 pool's e4m3
+        # round trip (oracle/fp8_ref.py) before it is stored -- the oracle of
+        # the product's opt-in FP8 mode, which the reference does not have
+        self.fp8 = fp8
         self.num_blocks = num_blocks
         self.block_size = block_size
         self.buf = (torch.zeros(num_layers, 2, num_blocks * block_size, NUM_KV_HEADS, HEAD_DIM,
@@ -93,6 +97,8 @@ class RefKVCache:
     def write(self, layer, slot_mapping, k, v):
         B, H, T, D = k.shape
         idx = torch.as_tensor(slot_mapping, dtype=torch.long)
+        if self.fp8:
+            k, v = fp8_round_trip(k), fp8_round_trip(v)
         self.buf[layer, 0].index_copy_(0, idx, k.transpose(1, 2).reshape(B * T, H, D).to(self.buf.dtype))
         self.buf[layer, 1].index_copy_(0, idx, v.transpose(1, 2).reshape(B * T, H, D).to(self.buf.dtype))
 
@@ -100,3 +106,16 @@ class RefKVCache:
     def read(self, layer, gather):
         idx = torch.as_tensor(gather, dtype=torch.long)
         return self.buf[layer, 0][idx].transpose(1, 2), self.buf[layer, 1][idx].transpose(1, 2)
+
+
+def fp8_round_trip(x: torch.Tensor) -> torch.Tensor:
+    """Rows of 128 (last dim) through the FP8 pool's quantisation: the fp32
+    value e4m3 * scale each row reads back as."""
+    import numpy as np
+
+    from oracle import fp8_ref
+
+    rows = x.detach().float().cpu().numpy().reshape(-1, x.shape[-1])
+    b, scale = fp8_ref.quantize_rows(rows)
+    back = fp8_ref.e4m3_decode(b) * scale[:, None]
+    return torch.from_numpy(np.ascontiguousarray(back.reshape(x.shape))).to(x.device)

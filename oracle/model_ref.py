@@ -102,6 +102,10 @@ class RefQwen2(nn.Module):
             v = a.v_proj(h).view(B, T, KV_HEADS, HEAD_DIM).transpose(1, 2)
             q = (q * cos) + (_rot(q) * sin)
             k = (k * cos) + (_rot(k) * sin)
+            if getattr(cache, "fp8", False):  # the FP8 pool's e4m3 round trip (not the reference's)
+                from oracle.kvcache_ref import fp8_round_trip
+
+                k, v = fp8_round_trip(k).to(k.dtype), fp8_round_trip(v).to(v.dtype)
             cache.buf[li, 0].index_copy_(0, slot_t, k.transpose(1, 2).reshape(B * T, KV_HEADS, HEAD_DIM))
             cache.buf[li, 1].index_copy_(0, slot_t, v.transpose(1, 2).reshape(B * T, KV_HEADS, HEAD_DIM))
             kd = cache.buf[li, 0][gather_t].transpose(1, 2)

@@ -74,15 +74,16 @@ def _greedy(m, cache, seqs, prompts, steps, device, mixed=False):
     return ids, logits
 
 
-def _teacher_forced(ref, dtype, prompts, ids, cuda):
+def _teacher_forced(ref, dtype, prompts, ids, cuda, fp8=False):
     """Oracle logits along OUR id sequence of each row (so one flip does not
-    cascade): the prompt, then one token at a time."""
+    cascade): the prompt, then one token at a time.  fp8: the oracle's cache
+    stores every K/V row through the FP8 pool's e4m3 round trip."""
     from oracle.kvcache_ref import RefKVCache
 
     out = []
     with torch.no_grad():
         for r, p in enumerate(prompts):
-            c = RefKVCache(64, 16, dtype)
+            c = RefKVCache(64, 16, dtype, fp8=fp8)
             c.buf = c.buf.to(cuda)
             s = c.alloc()
             row = [ref(torch.tensor([p], device=cuda), c, [s])[0, -1].float()]
@@ -108,7 +109,7 @@ def _agreement(ref_logits, flat_ids, margin):
 
 
 @pytest.mark.parametrize("path", ["reference_ops", "fused_cublas", "fused_skinny", "graphs",
-                                  "mixed"])
+                                  "mixed", "fp8_pool"])
 def test_greedy_ids_match_oracle_and_reference(cuda, models, path):
     """fused_*: merged q/k/v and gate/up GEMMs + fused add/RMSNorm/SwiGLU
     kernels (the engine's path), with the projections on cuBLAS or on the
@@ -118,7 +119,8 @@ def test_greedy_ids_match_oracle_and_reference(cuda, models, path):
     prompts right-padded into the 64-token prefill bucket (q_lens rows), the
     2-row decode steps padded to a 4-row bucket whose 2 extra rows are
     inactive.  mixed: prompt 1 shares one forward with row 0's decode step
-    (model.forward_mixed)."""
+    (model.forward_mixed).  fp8_pool: the engine on an FP8 (e4m3) cache,
+    against oracles whose caches apply the same e4m3 round trip."""
     import copy
 
     from kv_cache import KVCache
@@ -128,7 +130,8 @@ def test_greedy_ids_match_oracle_and_reference(cuda, models, path):
         ours = copy.deepcopy(ours).fuse_weights_()
         ours.skinny_linears = path != "fused_cublas"
     prompts, steps = fx["prompts"], fx["steps"]
-    c1 = KVCache(64, 16, cuda, torch.bfloat16)
+    fp8 = path == "fp8_pool"
+    c1 = KVCache(64, 16, cuda, torch.bfloat16, kv_format="fp8_e4m3" if fp8 else "bf16")
     s1 = [c1.alloc(), c1.alloc()]
     if path == "graphs":
         dg = ours.enable_decode_graphs(c1, max_batch=8)
@@ -146,21 +149,26 @@ def test_greedy_ids_match_oracle_and_reference(cuda, models, path):
     flat_logits = [lg for r in range(2) for lg in got_logits[r]]
 
     torch.backends.cuda.matmul.allow_tf32 = False
-    l16 = [lg for row in _teacher_forced(ref16, torch.bfloat16, prompts, got, cuda) for lg in row]
-    l32 = [lg for row in _teacher_forced(ref32, torch.float32, prompts, got, cuda) for lg in row]
+    l16 = [lg for row in _teacher_forced(ref16, torch.bfloat16, prompts, got, cuda, fp8)
+           for lg in row]
+    l32 = [lg for row in _teacher_forced(ref32, torch.float32, prompts, got, cuda, fp8)
+           for lg in row]
     d16 = max(float((a - b).abs().max()) for a, b in zip(flat_logits, l16))
     d32 = max(float((a - b).abs().max()) for a, b in zip(flat_logits, l32))
-    dec16, ag16, bad16 = _agreement(l16, flat, MARGIN_BF16)
-    dec32, ag32, bad32 = _agreement(l32, flat, MARGIN_FP32)
-    diag = (f"{path}: bf16 oracle: {ag16}/{dec16} decisive agree (margin>{MARGIN_BF16}), "
+    m16, m32 = MARGIN_BF16, MARGIN_FP32
+    dec16, ag16, bad16 = _agreement(l16, flat, m16)
+    dec32, ag32, bad32 = _agreement(l32, flat, m32)
+    diag = (f"{path}: bf16 oracle: {ag16}/{dec16} decisive agree (margin>{m16}), "
             f"max|dlogit| {d16:.4f}, misses at margins {bad16}; fp32 oracle: {ag32}/{dec32} "
-            f"(margin>{MARGIN_FP32}), max|dlogit| {d32:.4f}, misses {bad32}")
+            f"(margin>{m32}), max|dlogit| {d32:.4f}, misses {bad32}")
     print(diag)
     assert dec16 >= len(flat) // 2 and dec32 >= 3, diag
     assert ag16 == dec16 and ag32 == dec32, diag
+    if fp8:  # the reference's own ids come from an unquantised cache
+        return
     # the reference's own CPU fp32 greedy ids agree wherever it was decisive
     # (and our prefix matched, so the inputs were identical)
     for r in range(2):
         for t, (a, b, m) in enumerate(zip(got[r], fx["ids"][r], fx["margins"][r])):
-            if m > MARGIN_FP32 and got[r][:t] == fx["ids"][r][:t]:
+            if m > m32 and got[r][:t] == fx["ids"][r][:t]:
                 assert a == b, (r, t, diag)
