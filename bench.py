@@ -343,6 +343,7 @@ def fp8_decode_run(args, device, bf16_ms_per_step):
     torch.cuda.empty_cache()
     return {"metric": "paged decode-attn HBM GB/s on the FP8 (e4m3) pool", "kv_format": "fp8_e4m3",
             "value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "step_bytes": step_bytes,
             "ms_per_step": round(ms, 4), "steps": steps,
             "tokens_per_s": round(B / (ms * 1e-3), 1),
             "speedup_vs_bf16_step": round(bf16_ms_per_step / ms, 3),
@@ -1389,7 +1390,13 @@ def main():
 
     del w
     torch.cuda.empty_cache()
-    fp8 = None if args.no_fp8 else fp8_decode_run(args, dev, ms)
+    fp8 = None
+    if not args.no_fp8:
+        fp8 = fp8_decode_run(args, dev, ms)
+        # replicas: every rank ran the same step on its own pool
+        f_ms, f_rate = replica_rate(fp8.pop("step_bytes"), fp8["ms_per_step"], dev, world)
+        fp8.update({"value": round(f_rate / 1e9, 2), "ms_per_step": round(f_ms, 4),
+                    "tokens_per_s": round(args.seqs * world / (f_ms * 1e-3), 1), "n_gpus": world})
     prefill = None if args.no_prefill else prefill_run(args, dev, seed=args.seed)
     engine = engine4 = engine4_mixed = None
     if not args.no_engine:
@@ -1422,7 +1429,8 @@ def main():
                                   dev, world)
             r.update({"tok_s_all_gpus": round(toks_all / wall_max, 1),
                       "tokens_all_gpus": int(toks_all), "wall_s_max_over_gpus": round(wall_max, 4),
-                      "n_gpus": world, "scaling": "strong (1024 chats split over the GPUs)",
+                      "n_gpus": world,
+                      "scaling": f"strong ({args.engine4_chats} chats split over the GPUs)",
                       "per_rank": gather_ranks(rank_summary(rank, r), world)})
             runs[mixed_min] = r
         engine4 = runs[None]
