@@ -104,6 +104,9 @@ def parse():
     ap.add_argument("--sample-one", type=str, default=None, metavar="ROWS,...",
                     help="pkv_sample on [ROWS, 151936] bf16 logits: device time per call "
                          "(CUDA graph of 20 calls) and GB/s of logits read")
+    ap.add_argument("--persistent", action="store_true",
+                    help="with --decode-step --profile-range: profile the persistent "
+                         "all-layers launch")
     ap.add_argument("--profile-range", action="store_true",
                     help="with --decode-step / --prefill-step: one eager step inside "
                          "cudaProfilerStart/Stop "
@@ -339,7 +342,10 @@ def fp8_decode_run(args, device, bf16_ms_per_step):
     peaks, src = measured_peaks()
     peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
     achieved = bytes_decode / (kern_ms * 1e-3) / 1e9
-    del cache, q, k, v, q_rot, out, handles
+    # every view of the pool (the step's handles, the fill loop's slice) goes
+    # before the cache is returned to the driver: the next runs need the memory
+    del cache, q, k, v, q_rot, out, handles, step, body, cos, sin
+    gc.collect()
     torch.cuda.empty_cache()
     return {"metric": "paged decode-attn HBM GB/s on the FP8 (e4m3) pool", "kv_format": "fp8_e4m3",
             "value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
@@ -651,19 +657,22 @@ def call_roofline(calls, nparams):
 
 
 def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_batch,
-               rank=0, world=1, seed=0, mixed_min=None):
+               rank=0, world=1, seed=0, mixed_min=None, mixed_graphs=True):
     """Serve `chats_total` chats through chat.py (uniform random token-id prompts
     in `prompt_range`, `reply`-token replies with EOS and stop sequences off as
     metrics/benchmark_concurrency.py:122,143 does, temperature-1 sampling, one
     prefill per tick).  Rank r serves chats i with i % world == r from one
     seeded prompt set, on its own model replica and `blocks`-block pool.
     mixed_min: chat.MIXED_PREFILL_MIN_TOKENS for this run (None: the
-    reference's scheduling).  Returns this rank's tokens, wall time and a
+    reference's scheduling); its mixed steps replay captured graphs
+    (model.MixedGraphs) unless mixed_graphs is False.  Returns this rank's tokens, wall time and a
     roofline."""
     import chat
     import model as M
     from kv_cache import KVCache
 
+    gc.collect()  # the previous run's pool back to the driver before this one's
+    torch.cuda.empty_cache()
     torch.manual_seed(seed + rank)
     m = M.Qwen2ForCausalLM().to(device, torch.bfloat16).eval()
     random_init_(m, seed + 11)
@@ -678,6 +687,14 @@ def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_b
     prunner = m.enable_prefill_graphs(cache, max_len=hi)
     for b in prunner.buckets:
         prunner._capture(b)
+    mrunner = None
+    if mixed_min is not None and mixed_graphs and mixed_min <= hi:
+        mrunner = m.enable_mixed_graphs(cache, max_len=hi, max_batch=max_batch)
+        t0 = mrunner.buckets(max(mixed_min, 2), 1)[0]
+        for tp in mrunner.t_buckets:
+            for bp in mrunner.b_buckets:
+                if tp >= t0:
+                    mrunner.capture(tp, bp)
     g = torch.Generator().manual_seed(seed + 5)
     prompts = [torch.randint(0, M.VOCAB_SIZE, (int(torch.randint(lo, hi + 1, (1,), generator=g)),),
                              generator=g).tolist() for _ in range(chats_total + 1)]
@@ -714,7 +731,9 @@ def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_b
     chat.MIXED_PREFILL_MIN_TOKENS = None
     m._graphs.clear()  # the graph runners and the model refer to each other
     m._prefill_graphs.clear()
-    del runner, prunner, m, cache, cm
+    m._mixed_graphs.clear()
+    mixed_kind = "CUDA-graph" if mrunner is not None else "eager"
+    del runner, prunner, mrunner, m, cache, cm
     gc.collect()
     torch.cuda.empty_cache()
     return {"tok_s": round(toks / el, 1), "tokens": toks, "wall_s": round(el, 4),
@@ -731,7 +750,8 @@ def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_b
                       f"random-init bf16 Qwen2.5-1.5B (std 0.02), temperature-1 sampling, "
                       f"one prefill per tick (chat.py), CUDA-graph decode and prefill"
                       + (f"; prompts >= {mixed_min} tokens admitted while others decode share "
-                         f"their forward (eager mixed step)" if mixed_min is not None else "")}
+                         f"their forward ({mixed_kind} "
+                         f"mixed step)" if mixed_min is not None else "")}
 
 
 def engine3_run(args, device, seed=0):
@@ -762,6 +782,8 @@ def engine3_run(args, device, seed=0):
     from kv_cache import KVCache
 
     torch.manual_seed(seed)
+    gc.collect()
+    torch.cuda.empty_cache()
     m = M.Qwen2ForCausalLM().to(device, torch.bfloat16).eval()
     random_init_(m, seed + 11)
     block_bytes = L * 2 * 16 * HKV * D * 2
@@ -1137,10 +1159,12 @@ def sample_one(spec, device):
         del graph
 
 
-def decode_step_diag(spec, device, profile_range=False):
+def decode_step_diag(spec, device, profile_range=False, persistent_profile=False):
     """Whole-model decode step (random-init Qwen2.5-1.5B, B rows of CTX
     tokens of history) replayed from a CUDA graph, under the skinny-GEMM
-    policy and with every projection on cuBLAS."""
+    policy, with every projection on cuBLAS and (B <= 32) as the persistent
+    all-layers launch (pkv_decode_layers).  persistent_profile: the profiled
+    eager step uses the persistent launch."""
     import model as M
     from kv_cache import KVCache
 
@@ -1155,9 +1179,13 @@ def decode_step_diag(spec, device, profile_range=False):
     cache.advance(seqs, ctx)
     ids = torch.randint(0, 1000, (B, 1), device=device)
     res = {}
+    import pagedkv
+
+    policies = ("skinny", "cublas") + (("persistent",) if B <= pagedkv.LAYERS_MAX_ROWS else ())
     with torch.no_grad():
-        for policy in ("skinny", "cublas"):
-            m.skinny_linears = policy == "skinny"
+        for policy in policies:
+            m.skinny_linears = policy != "cublas"
+            m.persistent_decode = policy == "persistent"
             m.enable_decode_graphs(cache, max_batch=max(B, 16))
             for _ in range(3):
                 m(ids, cache, seqs)
@@ -1170,7 +1198,9 @@ def decode_step_diag(spec, device, profile_range=False):
             b.synchronize()
             res[policy] = round(a.elapsed_time(b) / 10, 4)
             m._graphs.clear()
+        cache.check_errors()
         m.skinny_linears = True
+        m.persistent_decode = persistent_profile and "persistent" in res
         if profile_range:
             m(ids, cache, seqs)
             torch.cuda.synchronize()
@@ -1180,6 +1210,7 @@ def decode_step_diag(spec, device, profile_range=False):
             torch.cuda.profiler.stop()
     print(json.dumps({"diag": "decode_step", "rows": B, "ctx": ctx,
                       "graph_ms_skinny_policy": res["skinny"], "graph_ms_cublas": res["cublas"],
+                      **({"graph_ms_persistent": res["persistent"]} if "persistent" in res else {}),
                       "skinny_rows": M.Qwen2ForCausalLM.skinny_rows}), flush=True)
 
 
@@ -1309,7 +1340,7 @@ def main():
         if args.linear_sweep:
             linear_sweep([int(r) for r in args.linear_sweep.split(",")], dev)
         if args.decode_step:
-            decode_step_diag(args.decode_step, dev, args.profile_range)
+            decode_step_diag(args.decode_step, dev, args.profile_range, args.persistent)
         if args.prefill_step:
             prefill_step_diag(args.prefill_step, dev, args.profile_range)
         return

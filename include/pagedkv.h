@@ -419,6 +419,64 @@ int pkv_linear_rope_append(const void* x, int64_t ldx, const void* w_qkv, int64_
                            int32_t seq_len_q, int32_t head_dim, void* workspace,
                            size_t workspace_bytes, int32_t* err_flag, void* stream);
 
+/*
+ * All decoder layers of one small decode step in ONE persistent launch.
+ *
+ * Replaces, for a step of 1 <= rows <= PKV_LAYERS_MAX_ROWS rows that each add
+ * one token (T = 1), the per-layer loop of model.py:157-207 over
+ * QwenBlock.forward (model.py:131-138): q/k/v projections + bias, RoPE, the
+ * K/V write into the paged cache (kv_cache.py:86-101), attention over each
+ * row's blocks (kernels/fa2.py:164-214 at T = 1), o_proj, residual add +
+ * RMSNorm, gate/up + SwiGLU, down_proj, residual add and the next layer's
+ * RMSNorm -- the same ops, bf16 rounding points and arithmetic as
+ * pkv_linear_rope_append, pkv_paged_decode, pkv_linear_add_rmsnorm and
+ * pkv_linear_silu_mul applied layer by layer, up to fp32 summation order in
+ * the k-split sums and the RMSNorm sums of squares.  One CTA per SM streams
+ * every layer's weights through a TMA ring that keeps filling across the
+ * layer's phases; the phases meet at grid-wide barriers (every wait bounded:
+ * a timeout sets PKV_DEVERR_TIMEOUT in err_flag and the launch returns).
+ *
+ * Shapes are Qwen2.5-1.5B's: hidden 1536, 12 query and 2 KV heads of 128,
+ * intermediate 8960, num_layers <= PKV_LAYERS_MAX_LAYERS.  Per layer (bf16,
+ * row-major, 16-byte aligned, rows contiguous):
+ *   qkv_w [2048][1536] (q rows, then k, then v), qkv_b [2048],
+ *   o_w [1536][1536], post_norm_w [1536] (post_attention_layernorm),
+ *   gate_up_w [17920][1536] in the PKV_W_GATE_UP_PAIRED layout,
+ *   down_w [1536][8960], in_norm_w [1536] (input_layernorm; layer 0's is
+ *   not read: h0 is already normalised).
+ * h0 [rows][1536]: layer 0's normalised input; xs [rows][1536]: the residual
+ * stream, updated in place; m_out [rows][1536] receives the last layer's MLP
+ * output before its residual add (the caller finishes with the final add +
+ * RMSNorm and the LM head).  kv_pool: the whole cache [num_layers][2]
+ * [num_slots][2][128] bf16 (K then V plane per layer).  Row b writes its new
+ * K/V at position starts[b] (< 0: inactive row, nothing written, its
+ * outputs undefined) through block_tables[seq_rows[b]] and attends to
+ * positions [0, starts[b]].  rope_cos/rope_sin: bf16 [rope_rows][128].
+ * workspace: pkv_decode_layers_workspace_size(rows) bytes, 256-byte aligned,
+ * owned by one stream at a time; its first 4 KiB are reset by the call.
+ */
+#define PKV_LAYERS_MAX_ROWS 32
+#define PKV_LAYERS_MAX_LAYERS 32
+
+typedef struct pkv_layer_weights {
+  const void* qkv_w;
+  const void* qkv_b;
+  const void* o_w;
+  const void* post_norm_w;
+  const void* gate_up_w;
+  const void* down_w;
+  const void* in_norm_w;
+} pkv_layer_weights;
+
+size_t pkv_decode_layers_workspace_size(int32_t rows);
+
+int pkv_decode_layers(const pkv_layer_weights* layers, int32_t num_layers, const void* h0,
+                      void* xs, void* m_out, int32_t rows, void* kv_pool, int64_t num_slots,
+                      const int32_t* block_tables, int64_t table_pitch, const int32_t* seq_rows,
+                      const int32_t* starts, const void* rope_cos, const void* rope_sin,
+                      int64_t rope_rows, float eps, void* workspace, size_t workspace_bytes,
+                      int32_t* err_flag, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -379,10 +379,11 @@ def _process(active):
     seqs = [job.chat.seq for job in continuing]
     if mixed is not None:
         new_job, prefill_ids = mixed
+        # host tensors: a mixed-step graph copies them with its other inputs
         with torch.no_grad():
             logits = model.forward_mixed(
-                torch.tensor([prefill_ids], device=DEVICE), new_job.chat.seq,
-                torch.tensor([[job.next_token] for job in continuing], device=DEVICE), seqs, _kv())
+                _host_ids(prefill_ids), new_job.chat.seq,
+                torch.tensor([job.next_token for job in continuing]).view(-1, 1), seqs, _kv())
         tokens = _sample(logits)
         new_job.next_token = tokens[0]
         for job, token_id in zip(continuing, tokens[1:]):

@@ -813,4 +813,143 @@ int pkv_linear_rope_append(const void* x, int64_t ldx, const void* w_qkv, int64_
   return launch_status(pkv::launch_append(a, s), "append_rope");
 }
 
+// ---------------------------------------------------------------- decode layers
+static int device_sms() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    return 0;
+  return n;
+}
+
+size_t pkv_decode_layers_workspace_size(int32_t rows) {
+  const int sms = device_sms();
+  if (rows <= 0 || rows > PKV_LAYERS_MAX_ROWS || sms <= 0) return 0;
+  return pkv::decode_layers_workspace_bytes(rows, sms);
+}
+
+int pkv_decode_layers(const pkv_layer_weights* layers, int32_t num_layers, const void* h0,
+                      void* xs, void* m_out, int32_t rows, void* kv_pool, int64_t num_slots,
+                      const int32_t* block_tables, int64_t table_pitch, const int32_t* seq_rows,
+                      const int32_t* starts, const void* rope_cos, const void* rope_sin,
+                      int64_t rope_rows, float eps, void* workspace, size_t workspace_bytes,
+                      int32_t* err_flag, void* stream) {
+  if (!layers || num_layers <= 0 || num_layers > PKV_LAYERS_MAX_LAYERS)
+    return fail(PKV_ERR_UNSUPPORTED, "num_layers must be in [1, %d] (got %d)",
+                PKV_LAYERS_MAX_LAYERS, num_layers);
+  if (rows < 0 || rows > PKV_LAYERS_MAX_ROWS)
+    return fail(PKV_ERR_UNSUPPORTED, "rows must be in [0, %d] (got %d)", PKV_LAYERS_MAX_ROWS, rows);
+  if (!h0 || !xs || !m_out || !starts || !rope_cos || !rope_sin)
+    return fail(PKV_ERR_INVALID, "null h0, xs, m_out, starts or rope tables");
+  if (rope_rows <= 0) return fail(PKV_ERR_INVALID, "rope_rows must be positive");
+  int st = check_pool(kv_pool, kv_pool, num_slots, block_tables, table_pitch);
+  if (st) return st;
+  if (!aligned16(h0) || !aligned16(xs) || !aligned16(m_out) || !aligned16(rope_cos) ||
+      !aligned16(rope_sin))
+    return fail(PKV_ERR_ALIGN, "h0, xs, m_out and rope tables must be 16-byte aligned");
+  for (int l = 0; l < num_layers; ++l) {
+    const pkv_layer_weights& w = layers[l];
+    if (!w.qkv_w || !w.qkv_b || !w.o_w || !w.post_norm_w || !w.gate_up_w || !w.down_w ||
+        (l > 0 && !w.in_norm_w))
+      return fail(PKV_ERR_INVALID, "layer %d: null weight", l);
+    if (!aligned16(w.qkv_w) || !aligned16(w.qkv_b) || !aligned16(w.o_w) ||
+        !aligned16(w.post_norm_w) || !aligned16(w.gate_up_w) || !aligned16(w.down_w) ||
+        (l > 0 && !aligned16(w.in_norm_w)))
+      return fail(PKV_ERR_ALIGN, "layer %d: weights must be 16-byte aligned", l);
+  }
+  if (rows == 0) return ok();
+  const int sms = device_sms();
+  if (sms <= 0) return fail(PKV_ERR_DRIVER, "no current CUDA device");
+  const pkv::LayersPlan pl = pkv::plan_decode_layers(rows, sms);
+  if (!pl.valid) return fail(PKV_ERR_UNSUPPORTED, "no decode-layers plan for %d SMs", sms);
+  const size_t need = pkv::decode_layers_workspace_bytes(rows, sms);
+  if (!workspace || workspace_bytes < need)
+    return fail(PKV_ERR_WORKSPACE, "decode_layers needs %zu workspace bytes, got %zu", need,
+                workspace ? workspace_bytes : (size_t)0);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(PKV_ERR_ALIGN, "workspace not 256-byte aligned");
+
+  // Tensor maps: one per weight matrix of every layer and one over the
+  // whole pool; kept for the next call with the same pointers.
+  static std::mutex mu;
+  static pkv::LayersMaps cached;
+  static std::string cached_key;
+  std::string key(reinterpret_cast<const char*>(layers), sizeof(pkv_layer_weights) * num_layers);
+  key.append(reinterpret_cast<const char*>(&kv_pool), sizeof(kv_pool));
+  key.append(reinterpret_cast<const char*>(&num_slots), sizeof(num_slots));
+  key.append(reinterpret_cast<const char*>(&num_layers), sizeof(num_layers));
+  int dev = 0;
+  cudaGetDevice(&dev);
+  key.append(reinterpret_cast<const char*>(&dev), sizeof(dev));
+  pkv::LayersMaps maps;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (key != cached_key) {
+      for (int l = 0; l < num_layers; ++l) {
+        const pkv_layer_weights& w = layers[l];
+        if ((st = encode_rows(&cached.w[l][0], w.qkv_w, 2048, 1536, 1536, 128)) ||
+            (st = encode_rows(&cached.w[l][1], w.o_w, 1536, 1536, 1536, 128)) ||
+            (st = encode_rows(&cached.w[l][2], w.gate_up_w, 17920, 1536, 1536, 128)) ||
+            (st = encode_rows(&cached.w[l][3], w.down_w, 1536, 8960, 8960, 128))) {
+          cached_key.clear();
+          return st;
+        }
+      }
+      EncodeFn fn = encode_fn();
+      if (!fn) {
+        cached_key.clear();
+        return fail(PKV_ERR_DRIVER, "cuTensorMapEncodeTiled entry point unavailable");
+      }
+      cuuint64_t dims[4] = {128, 2, static_cast<cuuint64_t>(num_slots),
+                            static_cast<cuuint64_t>(2 * num_layers)};
+      cuuint64_t strides[3] = {128 * 2, 2 * 128 * 2, static_cast<cuuint64_t>(num_slots) * 2 * 128 * 2};
+      cuuint32_t box[4] = {64, 1, 16, 1};
+      cuuint32_t es[4] = {1, 1, 1, 1};
+      CUresult r = fn(&cached.pool, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, kv_pool, dims, strides,
+                      box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r != CUDA_SUCCESS) {
+        cached_key.clear();
+        return fail(PKV_ERR_DRIVER, "pool tensor map encode failed (%d)", (int)r);
+      }
+      cached_key = key;
+    }
+    maps = cached;
+  }
+
+  pkv::LayersParams p{};
+  p.L = num_layers;
+  p.M = rows;
+  p.G = pl.grid;
+  p.P = pl.partitions;
+  p.min_blocks = pl.min_blocks;
+  p.xslots = pl.xslots;
+  p.nw = pl.nw;
+  for (int l = 0; l < num_layers; ++l) {
+    p.qkv_b[l] = static_cast<const __nv_bfloat16*>(layers[l].qkv_b);
+    p.post_w[l] = static_cast<const __nv_bfloat16*>(layers[l].post_norm_w);
+    p.in_w[l] = static_cast<const __nv_bfloat16*>(layers[l].in_norm_w);
+  }
+  p.h0 = static_cast<const __nv_bfloat16*>(h0);
+  p.xs = static_cast<__nv_bfloat16*>(xs);
+  p.m_out = static_cast<__nv_bfloat16*>(m_out);
+  p.pool = static_cast<__nv_bfloat16*>(kv_pool);
+  p.num_slots = num_slots;
+  p.num_blocks = static_cast<int32_t>(num_slots / 16);
+  p.tables = block_tables;
+  p.pitch = table_pitch;
+  p.rows = seq_rows;
+  p.starts = starts;
+  p.cos = static_cast<const __nv_bfloat16*>(rope_cos);
+  p.sin = static_cast<const __nv_bfloat16*>(rope_sin);
+  p.rope_rows = rope_rows;
+  p.eps = eps;
+  // as pkv_paged_decode computes it from sm_scale = 1 / sqrt(128) (fa2.py:168)
+  p.scale_log2 = static_cast<float>(1.0 / sqrt(128.0)) * 1.4426950408889634f;
+  p.err = err_flag;
+  pkv::carve_decode_layers(p, workspace, rows, sms, pl.partitions);
+  return launch_status(
+      pkv::launch_decode_layers(p, maps, pl, static_cast<cudaStream_t>(stream)), "decode_layers");
+}
+
 }  // extern "C"

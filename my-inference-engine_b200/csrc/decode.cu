@@ -84,6 +84,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? 4 : 2)
     paged_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap) {
   constexpr int kSB = decode_stage_bytes<NST, kFp8>();
+  static_assert(NST <= 32, "the prologue's block ids come from the first 32-id chunk");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -152,14 +153,23 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? 4 : 2)
   __syncwarp();
 
   const uint64_t policy = policy_evict_first();
-  auto issue = [&](int i) {
+  // Block ids of this warp's iterations, 32 at a time: lane k holds the id of
+  // iteration 32c + k (ids_cur) and of 32(c + 1) + k (ids_next, loaded one
+  // chunk ahead).  The id a refill needs is a shuffle away, so the copy
+  // issue never waits on a table load from global memory.
+  auto load_ids = [&](int c) -> int {
+    const int it = c * 32 + lane;
+    return (kPaged && it < my_n) ? __ldg(trow + blk_begin + warp + kDecodeWarps * it) : 0;
+  };
+  int ids_cur = load_ids(0);
+  int ids_next = my_n > 32 ? load_ids(1) : 0;
+  auto issue = [&](int i, int blk) {
     const int j = blk_begin + warp + kDecodeWarps * i;
     const int st = i % NST;
     uint8_t* kst = wstage + st * kSB;
     uint8_t* vst = kst + kHeadBlockBytes;
     mbar_arrive_expect_tx(&wbar[st], kSB);
     if constexpr (kFp8) {
-      int blk = trow[j];
       if (blk < 0 || blk >= p.num_blocks) {
         err.raise(PKV_DEVERR_BLOCK_ID);
         blk = 0;
@@ -167,7 +177,6 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? 4 : 2)
       bulk_load(kst, p.kv8 + (static_cast<int64_t>(blk) * (gridDim.y / p.sub_groups) + kvh) * kSB,
                 kSB, &wbar[st], policy);
     } else if constexpr (kPaged) {
-      int blk = trow[j];
       if (blk < 0 || blk >= p.num_blocks) {
         err.raise(PKV_DEVERR_BLOCK_ID);
         blk = 0;
@@ -185,8 +194,9 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? 4 : 2)
       tma_load_4d(vst + kBoxBytes, &vmap, &wbar[st], 64, tok, kvh, b, policy);
     }
   };
-  if (lane == 0) {
-    for (int i = 0; i < min(NST, my_n); ++i) issue(i);
+  for (int i = 0; i < min(NST, my_n); ++i) {  // NST <= 32: all in chunk 0
+    const int blk = __shfl_sync(0xffffffffu, ids_cur, i);
+    if (lane == 0) issue(i, blk);
   }
 
   // Q^T as the B operand: lane (g, t) holds query head g, dims 2t..2t+1 and
@@ -330,7 +340,15 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? 4 : 2)
       }
     }
     __syncwarp();
-    if (lane == 0 && i + NST < my_n) issue(i + NST);
+    const int nx = i + NST;
+    if (nx < my_n) {  // warp-uniform
+      if ((nx & 31) == 0) {
+        ids_cur = ids_next;
+        ids_next = load_ids((nx >> 5) + 1);
+      }
+      const int blk = __shfl_sync(0xffffffffu, ids_cur, nx & 31);
+      if (lane == 0) issue(nx, blk);
+    }
   }
   if (!ok) {
     // Give loads still in flight a bounded chance to land before the shared

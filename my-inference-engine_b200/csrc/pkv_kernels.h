@@ -213,4 +213,61 @@ struct SampleLaunch {
 int sample_splits(int32_t rows, int32_t vocab);
 cudaError_t launch_sample(const SampleLaunch& a, cudaStream_t stream);
 
+// All decoder layers of a small decode step in one persistent launch
+// (layers.cu).  Shapes are Qwen2.5-1.5B's: hidden 1536, 12 q / 2 KV heads of
+// 128, intermediate 8960.
+constexpr int kLayersMax = 32;
+struct LayersMaps {
+  // per layer: q/k/v [2048][1536], o [1536][1536], gate/up paired
+  // [17920][1536], down [1536][8960]; 2-D maps, box {64, 128}, 128B swizzle
+  CUtensorMap w[kLayersMax][4];
+  // the whole pool [2L][slots][Hkv][128] bf16: 4-D map, box {64, 1, 16, 1}
+  CUtensorMap pool;
+};
+struct LayersParams {
+  int32_t L, M, G;      // layers, rows, grid (one CTA per SM)
+  int32_t P;            // attention partitions per (row, KV head)
+  int32_t min_blocks;   // a row's attention partitions hold at least this many blocks
+  int32_t xslots, nw;   // activation slots, W ring stages
+  const __nv_bfloat16* qkv_b[kLayersMax];
+  const __nv_bfloat16* post_w[kLayersMax];  // post_attention_layernorm
+  const __nv_bfloat16* in_w[kLayersMax];    // input_layernorm (layers >= 1)
+  const __nv_bfloat16* h0;  // [M][1536] layer 0's normalised input
+  __nv_bfloat16* xs;        // [M][1536] residual stream, updated in place
+  __nv_bfloat16* m_out;     // [M][1536] the last layer's MLP output
+  __nv_bfloat16* pool;      // [2L][slots][Hkv][128]
+  int64_t num_slots;
+  int32_t num_blocks;
+  const int32_t* tables;
+  int64_t pitch;
+  const int32_t* rows;    // table row of each batch row (nullable: identity)
+  const int32_t* starts;  // length before this step; < 0 = inactive row
+  const __nv_bfloat16* cos;
+  const __nv_bfloat16* sin;
+  int64_t rope_rows;
+  float eps, scale_log2;
+  // workspace pieces (carve_decode_layers)
+  uint32_t* sync;     // [0] grid barrier arrivals, [2] abort word
+  int32_t* tile_cnt;  // per W tile completion counters
+  int32_t* att_cnt;   // per (row, KV head) attention partition counters
+  float* part;        // [G][2][32][128] fp32 tile-segment partials
+  float* att_o;       // [M * Hkv * P][8][128]
+  float* att_lse;     // [M * Hkv * P][8]
+  float* ss;          // [12][32] per-tile sums of squares of the residual
+  __nv_bfloat16* q_rot;    // [M][12][128]
+  __nv_bfloat16* att_out;  // [M][1536]
+  __nv_bfloat16* act;      // [M][8960]
+  int32_t* err;
+};
+struct LayersPlan {
+  int32_t mpad, grid, partitions, min_blocks, xslots, nw, smem_bytes;
+  bool valid;
+};
+LayersPlan plan_decode_layers(int32_t rows, int32_t sms);
+size_t decode_layers_workspace_bytes(int32_t rows, int32_t sms);
+size_t decode_layers_sync_bytes();
+void carve_decode_layers(LayersParams& p, void* ws, int32_t rows, int32_t sms, int32_t partitions);
+cudaError_t launch_decode_layers(const LayersParams& p, const LayersMaps& maps,
+                                 const LayersPlan& pl, cudaStream_t stream);
+
 }  // namespace pkv

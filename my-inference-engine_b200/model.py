@@ -164,6 +164,7 @@ class Qwen2ForCausalLM(torch.nn.Module):
         self._rope_retired = []  # outgrown tables stay alive: captured graphs may point at them
         self._graphs = {}  # id(cache) -> DecodeGraphs
         self._prefill_graphs = {}  # id(cache) -> PrefillGraphs
+        self._mixed_graphs = {}  # id(cache) -> MixedGraphs
 
     def rope_tables(self, num_positions, dtype, device):
         key = (str(device), dtype)
@@ -257,6 +258,15 @@ class Qwen2ForCausalLM(torch.nn.Module):
         N = xs.shape[0]
         if segs is None:
             segs = [(0, B, T, step, is_causal)]
+        if (self.persistent_decode and len(segs) == 1 and segs[0][2] == 1
+                and 0 < N <= pagedkv.LAYERS_MAX_ROWS and not cache.fp8
+                and segs[0][3].q_lens is None and len(self.layers) <= pagedkv.LAYERS_MAX_LAYERS):
+            # a small decode step: every layer in one persistent launch
+            st = segs[0][3]
+            m = torch.empty_like(xs)
+            return pagedkv.decode_layers(self._layer_table(), h, xs, m, cache.buf,
+                                         cache.block_tables, st.rows, st.starts, cos, sin,
+                                         RMS_NORM_EPS, err=cache.err_flag)
         use = {op: self.skinny_linears and N <= lim for op, lim in self.skinny_rows.items()}
         # the q/k/v GEMM's fused RoPE + append epilogue writes the bf16 pool;
         # an FP8 pool takes the separate quantising append
@@ -317,6 +327,25 @@ class Qwen2ForCausalLM(torch.nn.Module):
                 m = F.linear(act, mlp.down_proj.weight)
         return m
 
+    def forward_mixed_step(self, ids, step_p, step_d, Tp, Bp, cache):
+        """Device-only mixed step (no host synchronisation, capturable): ids
+        [Tp + Bp] int32 = the prompt's Tp (right-padded, step_p.q_lens real)
+        tokens then the Bp decode rows' tokens (rows with start -1 inactive).
+        Returns logits [1 + Bp, vocab]: the prompt's last real token, then
+        each decode row."""
+        import pagedkv
+
+        x = self.embed_tokens(ids.long())
+        cos, sin = self.rope_tables(cache.table_pitch * cache.block_size, x.dtype, x.device)
+        xs = x.view(Tp + Bp, HIDDEN_SIZE)
+        h = pagedkv.add_rmsnorm(xs, None, self.layers[0].input_layernorm.weight, RMS_NORM_EPS)
+        segs = [(0, 1, Tp, step_p, True), (Tp, Bp, 1, step_d, False)]
+        m = self._fused_layers(h, xs, 0, 0, cos, sin, None, None, cache, None, segs=segs)
+        last = torch.cat([step_p.q_lens.long() - 1,
+                          torch.arange(Tp, Tp + Bp, device=x.device)])
+        hl = pagedkv.add_rmsnorm(m[last], xs[last], self.norm.weight, RMS_NORM_EPS)
+        return hl @ self.embed_tokens.weight.T
+
     def forward_mixed(self, prefill_ids, prefill_seq, decode_ids, decode_seqs, cache):
         """One forward over a prompt and a batch of decode rows (a mixed
         prefill + decode step): prefill_ids [1, T] for sequence prefill_seq,
@@ -324,11 +353,14 @@ class Qwen2ForCausalLM(torch.nn.Module):
         run once over all T + B rows (one pass over the weights); RoPE + K/V
         append and attention run per part (the causal prefill kernel for the
         prompt, the decode kernel for the rest).  Returns logits
-        [1 + B, vocab]: the prompt's last token, then each decode row.  Eager
-        (not graph-captured): meant for prompts long enough that the GPU work
-        hides the launches.  Needs the fused weights (fuse_weights_)."""
+        [1 + B, vocab]: the prompt's last token, then each decode row.
+        Replays a captured graph when enable_mixed_graphs covers (T, B), else
+        runs eagerly.  Needs the fused weights (fuse_weights_)."""
         import pagedkv
 
+        runner = self._mixed_graphs.get(id(cache))
+        if runner is not None and runner.covers(prefill_ids.shape[1], len(decode_seqs)):
+            return runner.run(prefill_ids, prefill_seq, decode_ids, decode_seqs)
         self.fuse_weights_()
         dev = cache.device
         T, B = prefill_ids.shape[1], len(decode_seqs)
@@ -364,6 +396,26 @@ class Qwen2ForCausalLM(torch.nn.Module):
     def refresh_packed_weights(self):
         for layer in self.layers:
             layer.mlp.__dict__.pop("_gate_up_paired", None)
+        self.__dict__.pop("_layers_table", None)
+
+    def _layer_table(self):
+        """The per-layer weight table of pagedkv.decode_layers (merged q/k/v,
+        the paired gate/up copy), made on first use and kept."""
+        tab = self.__dict__.get("_layers_table")
+        if tab is None:
+            import pagedkv
+
+            ents = []
+            for layer in self.layers:
+                at, mlp = layer.self_attn, layer.mlp
+                ents.append({"qkv_w": at.qkv_weight, "qkv_b": at.qkv_bias,
+                             "o_w": at.o_proj.weight,
+                             "post_norm_w": layer.post_attention_layernorm.weight,
+                             "gate_up_w": self._paired_gate_up(mlp).data,
+                             "down_w": mlp.down_proj.weight,
+                             "in_norm_w": layer.input_layernorm.weight})
+            tab = self.__dict__["_layers_table"] = pagedkv.LayerTable(ents)
+        return tab
 
     @property
     def fused(self):
@@ -375,6 +427,10 @@ class Qwen2ForCausalLM(torch.nn.Module):
     # B200 (measured per projection, CUDA-graph replay).
     skinny_linears = True
     skinny_rows = {"qkv": 32, "o": 32, "gate_up": 32, "down": 128}
+    # A decode step (one token per row) of at most pagedkv.LAYERS_MAX_ROWS
+    # rows on a bf16 pool runs all layers as one persistent launch
+    # (pkv_decode_layers) instead of the per-op kernels.
+    persistent_decode = False
 
     def fuse_weights_(self):
         """Merge q/k/v (weights + biases) and gate/up weights into single
@@ -413,12 +469,31 @@ class Qwen2ForCausalLM(torch.nn.Module):
         self._graphs[id(cache)] = DecodeGraphs(self, cache, max_batch)
         return self._graphs[id(cache)]
 
+    def enable_mixed_graphs(self, cache, max_len=4096, max_batch=256):
+        """Capture mixed prefill + decode steps (forward_mixed) per (padded
+        prompt length, padded decode batch) bucket, lazily on first use or
+        ahead of time with MixedGraphs.capture."""
+        self.fuse_weights_()
+        self._mixed_graphs[id(cache)] = MixedGraphs(self, cache, max_len, max_batch)
+        return self._mixed_graphs[id(cache)]
+
     def enable_prefill_graphs(self, cache, max_len=4096):
         """Capture one-row prefills (chat.py admits one message per tick) per
         padded length bucket, lazily on first use."""
         self.fuse_weights_()
         self._prefill_graphs[id(cache)] = PrefillGraphs(self, cache, max_len)
         return self._prefill_graphs[id(cache)]
+
+
+def _prefill_buckets(top):
+    """Padded prompt lengths: 64, 128, 256, then every 128 tokens up to top
+    (< 1/3 padding, ~3% on average)."""
+    out, b = [], 64
+    while b < top:
+        out.append(b)
+        b = b * 2 if b < 256 else b + 128
+    out.append(top)
+    return out
 
 
 def _pinned_free(events, key):
@@ -541,13 +616,7 @@ class PrefillGraphs:
     def __init__(self, model, cache, max_len):
         self.model, self.cache = model, cache
         self.capacity = cache.table_pitch * cache.block_size
-        top = min(max_len, self.capacity)
-        self.buckets = []  # 64, 128, 256, then every 128 tokens: < 1/3 padding, ~3% on average
-        b = 64
-        while b < top:
-            self.buckets.append(b)
-            b = b * 2 if b < 256 else b + 128
-        self.buckets.append(top)
+        self.buckets = _prefill_buckets(min(max_len, self.capacity))
         self.graphs = {}
         self.pool = torch.cuda.graph_pool_handle()
         self._copied = {}  # bucket -> event after the last copy out of its pinned inputs
@@ -597,3 +666,96 @@ class PrefillGraphs:
         g.replay()
         self.cache.advance(seqs, T)
         return logits[:, 0]
+
+
+class MixedGraphs:
+    """CUDA graphs of the mixed prefill + decode step (forward_mixed), one per
+    (padded prompt length Tp, padded decode batch Bp) bucket: Tp as
+    PrefillGraphs (the prompt right-padded, its q_len making the append and
+    the prefill kernel skip the padding), Bp in 16, 32, 64, 128, 256 (padded
+    decode rows inactive, start -1).  One pinned host buffer per bucket holds
+    the step's ids and both segments' (row, start, kv_len) and goes over in
+    one copy; the graph then runs the whole step -- ~600 eager launches --
+    as one replay.  Both segments' attention grids are planned for the
+    cache's per-sequence capacity, as the other graph runners do."""
+
+    def __init__(self, model, cache, max_len, max_batch):
+        self.model, self.cache = model, cache
+        self.capacity = cache.table_pitch * cache.block_size
+        self.t_buckets = _prefill_buckets(min(max_len, self.capacity))
+        mb = min(max_batch, cache.max_seqs)
+        self.b_buckets = [b for b in (16, 32, 64, 128, 256) if b < mb] + [mb]
+        self.graphs = {}
+        self.pool = torch.cuda.graph_pool_handle()
+        self._copied = {}
+
+    def covers(self, T, B):
+        return 1 < T <= self.t_buckets[-1] and 0 < B <= self.b_buckets[-1]
+
+    def buckets(self, T, B):
+        return (next(t for t in self.t_buckets if t >= T), next(b for b in self.b_buckets if b >= B))
+
+    def capture(self, Tp, Bp):
+        from kv_cache import PagedStep
+
+        if (Tp, Bp) in self.graphs:
+            return self.graphs[(Tp, Bp)]
+        dev = self.cache.device
+        # one device buffer: [ids (Tp + Bp) | prompt row, start, kv_len, q_len |
+        # decode rows (Bp) | decode starts | decode kv_lens]
+        n = Tp + Bp + 4 + 3 * Bp
+        dev_in = torch.zeros(n, dtype=torch.int32, device=dev)
+        ids = dev_in[:Tp + Bp]
+        mp = dev_in[Tp + Bp:Tp + Bp + 4]
+        md = dev_in[Tp + Bp + 4:].view(3, Bp)
+        mp[1].fill_(-1)  # inactive until a real step is copied in
+        md[1].fill_(-1)
+        step_p = PagedStep(self.cache, Tp, [0], mp[0:1], mp[1:2], mp[2:3], self.capacity,
+                           q_lens=mp[3:4])
+        step_d = PagedStep(self.cache, 1, [0] * Bp, md[0], md[1], md[2], self.capacity)
+        host = torch.zeros(n, dtype=torch.int32, pin_memory=True)
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self.model.forward_mixed_step(ids, step_p, step_d, Tp, Bp, self.cache)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=self.pool):
+            logits = self.model.forward_mixed_step(ids, step_p, step_d, Tp, Bp, self.cache)
+        self.graphs[(Tp, Bp)] = (g, dev_in, host, logits)
+        return self.graphs[(Tp, Bp)]
+
+    def run(self, prefill_ids, prefill_seq, decode_ids, decode_seqs):
+        T, B = prefill_ids.shape[1], len(decode_seqs)
+        Tp, Bp = self.buckets(T, B)
+        g, dev_in, host, logits = self.capture(Tp, Bp)
+        sp, rp = self.cache.step_rows([prefill_seq], T)
+        sd, rd = self.cache.step_rows(decode_seqs, 1)
+        self.cache.flush_tables()
+        _pinned_free(self._copied, (Tp, Bp))
+        h = host.numpy()
+        h[:Tp + Bp] = 0
+        if not prefill_ids.is_cuda:
+            h[:T] = prefill_ids.reshape(-1).numpy()
+        if not decode_ids.is_cuda:
+            h[Tp:Tp + B] = decode_ids.reshape(-1).numpy()
+        o = Tp + Bp
+        h[o:o + 4] = (rp[0], sp[0], sp[0] + T, T)
+        md = h[o + 4:].reshape(3, Bp)
+        md[0, :B] = rd
+        md[1, :B] = sd
+        np.add(md[1, :B], 1, out=md[2, :B])
+        md[0, B:] = 0
+        md[1, B:] = -1
+        md[2, B:] = 0
+        dev_in.copy_(host, non_blocking=True)
+        _pinned_used(self._copied, (Tp, Bp))
+        if prefill_ids.is_cuda:  # device ids: device-side copies, no host sync
+            dev_in[:T].copy_(prefill_ids.reshape(-1))
+        if decode_ids.is_cuda:
+            dev_in[Tp:Tp + B].copy_(decode_ids.reshape(-1))
+        g.replay()
+        self.cache.advance([prefill_seq], T)
+        self.cache.advance(decode_seqs, 1)
+        return logits[:1 + B]

@@ -26,6 +26,8 @@ PKV_DEVERR_TIMEOUT = 4
 HEAD_DIM = 128
 BLOCK_TOKENS = 16
 LINEAR_MAX_ROWS = 256  # PKV_LINEAR_MAX_ROWS
+LAYERS_MAX_ROWS = 32  # PKV_LAYERS_MAX_ROWS
+LAYERS_MAX_LAYERS = 32  # PKV_LAYERS_MAX_LAYERS
 W_ROWMAJOR, W_TILED, W_GATE_UP_PAIRED = 0, 1, 2  # PKV_W_* layouts
 
 _c_i32p = ctypes.POINTER(ctypes.c_int32)
@@ -87,6 +89,10 @@ _SIGNATURES = {
         [_vp, _i64, _vp, _i64, _i32, _vp, _i32, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp,
          _i64, _vp, _i64, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, ctypes.c_size_t, _vp,
          _vp], ctypes.c_int),
+    "pkv_decode_layers_workspace_size": ([_i32], ctypes.c_size_t),
+    "pkv_decode_layers": (
+        [_vp, _i32, _vp, _vp, _vp, _i32, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _i64,
+         ctypes.c_float, _vp, ctypes.c_size_t, _vp, _vp], ctypes.c_int),
     "pkv_dense_attention": (
         [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i32, _i32,
          _i32, _i32, _i32, _i32, _i32, ctypes.c_float, _vp, _i64, _i64, _i64, _vp,
@@ -490,3 +496,69 @@ def linear_rope_append(x: torch.Tensor, w_qkv: torch.Tensor, bias: torch.Tensor 
 def default_scale(d: int = HEAD_DIM) -> float:
     """1/sqrt(d), as kernels/fa2.py:173 computes it."""
     return 1.0 / math.sqrt(d)
+
+
+# ---------------------------------------------------------------- decode layers
+_LAYER_FIELDS = ("qkv_w", "qkv_b", "o_w", "post_norm_w", "gate_up_w", "down_w", "in_norm_w")
+
+
+class _LayerWeightsC(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_void_p) for name in _LAYER_FIELDS]
+
+
+class LayerTable:
+    """The host array of pkv_layer_weights that pkv_decode_layers reads: one
+    entry per decoder layer (tensors keyed by the struct's field names:
+    qkv_w, qkv_b, o_w, post_norm_w, gate_up_w in the PKV_W_GATE_UP_PAIRED
+    layout, down_w, in_norm_w).  Keeps the tensors alive."""
+
+    def __init__(self, layers: list[dict]):
+        if not 0 < len(layers) <= LAYERS_MAX_LAYERS:
+            raise ValueError(f"1..{LAYERS_MAX_LAYERS} layers supported, got {len(layers)}")
+        self.tensors = layers
+        self.arr = (_LayerWeightsC * len(layers))()
+        for i, d in enumerate(layers):
+            for name in _LAYER_FIELDS:
+                t = d.get(name)
+                if t is not None and not t.is_contiguous():
+                    raise ValueError(f"layer {i}: {name} must be contiguous")
+                setattr(self.arr[i], name, None if t is None else t.data_ptr())
+
+    def __len__(self) -> int:
+        return len(self.tensors)
+
+
+_layers_ws: dict[int, torch.Tensor] = {}
+
+
+def decode_layers_workspace(device: torch.device) -> torch.Tensor:
+    """Per-device scratch of pkv_decode_layers, sized for PKV_LAYERS_MAX_ROWS
+    rows so one buffer serves every step (and the graphs that captured it)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _layers_ws.get(idx)
+    if ws is None:
+        need = int(lib().pkv_decode_layers_workspace_size(LAYERS_MAX_ROWS))
+        if need <= 0:
+            raise PagedKVError("pkv_decode_layers_workspace_size: no plan for this device")
+        ws = torch.empty(need, dtype=torch.uint8, device=device)
+        _layers_ws[idx] = ws
+    return ws
+
+
+def decode_layers(table: LayerTable, h0: torch.Tensor, xs: torch.Tensor, m_out: torch.Tensor,
+                  kv_pool: torch.Tensor, tables: torch.Tensor, rows: torch.Tensor | None,
+                  starts: torch.Tensor, rope_cos: torch.Tensor, rope_sin: torch.Tensor,
+                  eps: float, err: torch.Tensor | None = None) -> torch.Tensor:
+    """pkv_decode_layers: every decoder layer of a one-token-per-row step in
+    one launch.  h0, xs, m_out: [rows, 1536] bf16 (xs updated in place, the
+    last layer's MLP output into m_out); kv_pool: the cache's whole
+    [layers, 2, slots, 2, 128] buffer."""
+    n = h0.shape[0]
+    ws = decode_layers_workspace(h0.device)
+    st = lib().pkv_decode_layers(
+        ctypes.cast(table.arr, _vp), len(table), _ptr(h0), _ptr(xs), _ptr(m_out), n,
+        _ptr(kv_pool), kv_pool.shape[2], _ptr(tables), tables.stride(0), _ptr(rows),
+        _ptr(starts), _ptr(rope_cos), _ptr(rope_sin), rope_cos.shape[0], eps, _ptr(ws),
+        ws.numel(), _ptr(err), _stream(h0.device))
+    _check(st, "pkv_decode_layers")
+    return m_out

@@ -22,7 +22,7 @@ INCLUDE = HERE.parent / "include"
 LIB = HERE / "libpagedkv.so"
 BUILD_DIR = HERE / "_build"
 SOURCES = ["capi.cu", "append.cu", "decode.cu", "prefill_tc.cu", "fused.cu", "linear_tc.cu",
-           "sample.cu"]
+           "sample.cu", "layers.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 

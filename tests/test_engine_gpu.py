@@ -101,10 +101,11 @@ def test_graph_inputs_survive_back_to_back_calls(cuda, small_model):
         assert bool((pick >= a.max(-1).values - 0.05).all())
 
 
-@pytest.mark.parametrize("mixed", [None, 1])
-def test_engine_serves_chats_with_eviction(cuda, small_model, mixed):
+@pytest.mark.parametrize("mixed,mixed_graphs", [(None, False), (1, False), (1, True)])
+def test_engine_serves_chats_with_eviction(cuda, small_model, mixed, mixed_graphs):
     """mixed=1: every prompt admitted while others decode joins their step
-    (chat.MIXED_PREFILL_MIN_TOKENS, model.forward_mixed)."""
+    (chat.MIXED_PREFILL_MIN_TOKENS, model.forward_mixed); mixed_graphs: those
+    steps replay captured graphs (model.MixedGraphs)."""
     import chat
     from kv_cache import KVCache
 
@@ -124,6 +125,8 @@ def test_engine_serves_chats_with_eviction(cuda, small_model, mixed):
     cache = KVCache(40, 16, cuda, torch.bfloat16)
     chat.init(kv_cache=cache, start_worker=False)
     m.enable_decode_graphs(cache, max_batch=8)
+    if mixed_graphs:
+        mg = m.enable_mixed_graphs(cache, max_len=256, max_batch=8)
     saved = (chat.MAX_REPLY_TOKENS, chat.STOP_SEQUENCES, chat.MIXED_PREFILL_MIN_TOKENS)
     chat.MAX_REPLY_TOKENS = 24
     chat.STOP_SEQUENCES = []
@@ -146,11 +149,14 @@ def test_engine_serves_chats_with_eviction(cuda, small_model, mixed):
             assert pieces[-1] is None and len(pieces) == 24 + 1  # 24 tokens, then done
         for c in chats:
             assert len(c.messages) == 4
+        if mixed_graphs:
+            assert mg.graphs, "no mixed step replayed a graph"
     finally:
         chat.MAX_REPLY_TOKENS, chat.STOP_SEQUENCES, chat.MIXED_PREFILL_MIN_TOKENS = saved
         chat._mixed.clear()
         chat._kv_cache = None
         m._graphs.clear()
+        m._mixed_graphs.clear()
 
 
 @pytest.mark.parametrize("gemm", ["cublas", "skinny"])
@@ -250,6 +256,63 @@ def test_mixed_forward_matches_separate_calls(cuda, small_model, gemm):
     d = (ca.buf.float() - cb.buf.float()).abs()
     assert float(d.max()) < 0.1 and float(d[live].mean()) < 0.005
     # same block ownership, and blocks no sequence owns stay zero
+    assert ca._block_tables == cb._block_tables
+    used = {x for t in cb._block_tables.values() for x in t}
+    unused = [x for x in range(cb.num_blocks) if x not in used]
+    view = cb.buf.view(cb.buf.shape[0], 2, cb.num_blocks, 16, -1)
+    assert int(view[:, :, unused].count_nonzero()) == 0
+
+
+def test_mixed_graph_matches_eager(cuda, small_model):
+    """Mixed steps replayed from (padded prompt, padded decode batch) graphs
+    give the eager forward_mixed's logits and K/V and advance every sequence
+    the same way.  Two steps of one bucket run back to back with host-side
+    ids and no synchronisation between them (the bucket's pinned input is
+    refilled while the first copy may still be pending); the prompt tails and
+    the padded decode rows must leave the pool untouched.  Both arms run the
+    skinny GEMMs (the padded graph has more rows, which could otherwise pick
+    another GEMM)."""
+    from kv_cache import KVCache
+
+    m = small_model.fuse_weights_()
+    saved = m.skinny_linears, m.skinny_rows
+    m.skinny_linears = True
+    m.skinny_rows = {op: 256 for op in saved[1]}
+    g = torch.Generator().manual_seed(6)
+    hist = [torch.randint(0, 151936, (n,), generator=g).tolist() for n in (33, 7, 130)]
+    prompts = [torch.randint(0, 151936, (1, n), generator=g) for n in (90, 101)]
+    decs = [torch.tensor([[5], [6], [7]]), torch.tensor([[8], [9], [10]])]
+    res = []
+    try:
+        for use_graph in (False, True):
+            c = KVCache(64, 16, cuda, torch.bfloat16)
+            if use_graph:
+                mg = m.enable_mixed_graphs(c, max_len=256, max_batch=16)
+            seqs = [c.alloc() for _ in hist]
+            with torch.no_grad():
+                for s, p in zip(seqs, hist):
+                    m(torch.tensor([p], device=cuda), c, [s])
+                new = [c.alloc() for _ in prompts]
+                lg = [m.forward_mixed(p, n, d, seqs, c).float().clone()
+                      for p, n, d in zip(prompts, new, decs)]
+            torch.cuda.synchronize()
+            c.check_errors()
+            if use_graph:
+                assert set(mg.graphs) == {(128, 16)}
+            res.append((lg, c, [c.length(s) for s in seqs + new]))
+    finally:
+        m.skinny_linears, m.skinny_rows = saved
+        m._mixed_graphs.clear()
+    (la, ca, na), (lb, cb, nb) = res
+    assert na == nb == [35, 9, 132, 90, 101]
+    for a, b in zip(la, lb):
+        assert b.shape == (4, 151936)
+        d = (a - b).abs()
+        assert float(d.max()) < 0.1 and float(d.mean()) < 0.01
+        assert torch.equal(a.argmax(-1), b.argmax(-1))
+    live = (ca.buf != 0) | (cb.buf != 0)
+    d = (ca.buf.float() - cb.buf.float()).abs()
+    assert float(d.max()) < 0.1 and float(d[live].mean()) < 0.005
     assert ca._block_tables == cb._block_tables
     used = {x for t in cb._block_tables.values() for x in t}
     unused = [x for x in range(cb.num_blocks) if x not in used]
