@@ -71,9 +71,10 @@ def parse():
     ap.add_argument("--engine4-prompt", type=int, nargs=2, default=[32, 4096])
     ap.add_argument("--engine4-reply", type=int, default=128)
     ap.add_argument("--engine4-pool-gb", type=float, default=120.0)
-    ap.add_argument("--engine4-mixed", type=int, default=None, metavar="MIN_TOKENS",
+    ap.add_argument("--engine4-mixed", type=int, default=1024, metavar="MIN_TOKENS",
                     help="also serve config 4 with chat.MIXED_PREFILL_MIN_TOKENS=MIN_TOKENS "
-                         "(prompts of at least MIN_TOKENS share the tick's decode forward)")
+                         "(prompts of at least MIN_TOKENS share the tick's decode forward, "
+                         "replayed from CUDA graphs); 0 = skip")
     ap.add_argument("--no-fp8", action="store_true", help="skip the FP8-pool decode line")
     ap.add_argument("--no-engine3", action="store_true")
     ap.add_argument("--engine3-chats", type=int, default=256)
@@ -1449,7 +1450,8 @@ def main():
         need = per_gpu * -(-(args.engine4_prompt[1] + args.engine4_reply + 1) // 16) + 64
         blocks = int(min(need, args.engine4_pool_gb * 1e9 // block_bytes))
         runs = {}
-        for mixed_min in [None] + ([args.engine4_mixed] if args.engine4_mixed is not None else []):
+        mixed_on = args.engine4_mixed is not None and args.engine4_mixed > 0
+        for mixed_min in [None] + ([args.engine4_mixed] if mixed_on else []):
             r = engine_run(dev, label="config4", chats_total=args.engine4_chats,
                            prompt_range=args.engine4_prompt, reply=args.engine4_reply,
                            blocks=blocks, max_batch=256, rank=rank, world=world,
@@ -1465,7 +1467,7 @@ def main():
                       "per_rank": gather_ranks(rank_summary(rank, r), world)})
             runs[mixed_min] = r
         engine4 = runs[None]
-        engine4_mixed = runs.get(args.engine4_mixed) if args.engine4_mixed is not None else None
+        engine4_mixed = runs.get(args.engine4_mixed) if mixed_on else None
         if engine is not None and rank == 0 and world == 1 and not args.no_engine_cpu:
             torch.set_num_threads(os.cpu_count() or 1)
             engine["cpu_baseline"] = engine_cpu_sample()

@@ -7,6 +7,7 @@
 #include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 
 #include <mutex>
 #include <string>
@@ -925,6 +926,8 @@ int pkv_decode_layers(const pkv_layer_weights* layers, int32_t num_layers, const
   p.min_blocks = pl.min_blocks;
   p.xslots = pl.xslots;
   p.nw = pl.nw;
+
+
   for (int l = 0; l < num_layers; ++l) {
     p.qkv_b[l] = static_cast<const __nv_bfloat16*>(layers[l].qkv_b);
     p.post_w[l] = static_cast<const __nv_bfloat16*>(layers[l].post_norm_w);
