@@ -103,8 +103,9 @@ int pkv_append_rope(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
                     int32_t* err_flag, void* stream);
 
 /*
- * Bytes of fp32 scratch pkv_paged_decode needs for these sizes (split-K
- * partials + per-(row, kv_head) counters).  0 when one pass suffices.
+ * Bytes of fp32 scratch pkv_paged_decode (and pkv_paged_decode_fp8) needs
+ * for these sizes (split-K partials + per-(row, kv_head) counters).  0 when
+ * one pass suffices.
  */
 size_t pkv_decode_workspace_size(int32_t batch, int32_t num_q_heads,
                                  int32_t num_kv_heads, int32_t max_kv_len);
@@ -113,7 +114,9 @@ size_t pkv_decode_workspace_size(int32_t batch, int32_t num_q_heads,
  * The split-K plan pkv_paged_decode takes for these sizes, written to
  * plan[0..3] = {blocks_per_part, min_blocks_per_part, max_parts (grid.x),
  * sub_groups}.  Host-only arithmetic (no GPU, no launch); lets a caller or a
- * test see which partition sizing a launch of this shape uses.  Diagnostic,
+ * test see which partition sizing a launch of this shape uses (the FP8
+ * kernel, with twice the CTAs resident per SM, plans for twice the CTAs and
+ * so may split rows more finely).  Diagnostic,
  * no counterpart in the reference (its kernel has no split-K,
  * kernels/fa2.py:192-207).  Returns PKV_ERR_INVALID for invalid sizes.
  */

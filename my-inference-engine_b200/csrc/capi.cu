@@ -369,7 +369,10 @@ int pkv_fp8_dequant(const void* kv8_pool, int64_t num_blocks, const int32_t* blo
 size_t pkv_decode_workspace_size(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
                                  int32_t max_kv_len) {
   if (batch <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0) return 0;
-  return pkv::plan_decode(batch, num_q_heads, num_kv_heads, max_kv_len).workspace_bytes;
+  // enough for either pool format's plan
+  const size_t a = pkv::plan_decode(batch, num_q_heads, num_kv_heads, max_kv_len).workspace_bytes;
+  const size_t b = pkv::plan_decode(batch, num_q_heads, num_kv_heads, max_kv_len, true).workspace_bytes;
+  return a > b ? a : b;
 }
 
 int pkv_decode_plan(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t max_kv_len,
@@ -386,7 +389,8 @@ int pkv_decode_plan(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, in
 }
 
 static int decode_common(const pkv::DecodeLaunch& a, const pkv::KVSource& src, cudaStream_t stream) {
-  const pkv::DecodePlan plan = pkv::plan_decode(a.batch, a.num_q_heads, a.num_kv_heads, a.max_kv_len);
+  const pkv::DecodePlan plan =
+      pkv::plan_decode(a.batch, a.num_q_heads, a.num_kv_heads, a.max_kv_len, a.kv8 != nullptr);
   if (static_cast<int64_t>(a.batch) * a.num_kv_heads * plan.sub_groups > pkv::decode_max_units())
     return fail(PKV_ERR_UNSUPPORTED, "batch * kv_heads too large for one decode launch (max %lld)",
                 (long long)pkv::decode_max_units());

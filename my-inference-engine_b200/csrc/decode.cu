@@ -519,14 +519,17 @@ cudaError_t launch_decode_t(const DecodeParams& prm, const KVSource& src, dim3 g
 }  // namespace
 
 DecodePlan plan_decode(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
-                       int32_t max_kv_len) {
+                       int32_t max_kv_len, bool fp8) {
   DecodePlan pl{};
   const int group = num_q_heads / num_kv_heads;
   pl.sub_groups = (group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta;
   const int64_t units = static_cast<int64_t>(batch) * num_kv_heads * pl.sub_groups;
   const int nblk = max(1, (max_kv_len + kBlockTokens - 1) / kBlockTokens);
   const int64_t units1 = units > 0 ? units : 1;
-  const int64_t want = (kTargetCtas + units1 - 1) / units1;
+  // the FP8 kernel keeps twice the CTAs resident per SM (4 vs 2): the same
+  // number of waves takes twice the CTAs
+  const int64_t target = fp8 ? 2 * static_cast<int64_t>(kTargetCtas) : kTargetCtas;
+  const int64_t want = (target + units1 - 1) / units1;
   const int64_t parts = want < kMaxParts ? want : kMaxParts;
   int min_bpp = kMinBlocksPerPartSmall;
   if (units * (nblk / kMinBlocksPerPart) >= kBusyCtas)

@@ -64,8 +64,9 @@ struct DecodePlan {
 size_t decode_counter_bytes();
 int64_t decode_max_units();  // rows * kv_heads * sub_groups per launch
 
+// fp8: the plan of the FP8-pool kernel (twice the resident CTAs per SM)
 DecodePlan plan_decode(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
-                       int32_t max_kv_len);
+                       int32_t max_kv_len, bool fp8 = false);
 cudaError_t launch_decode(const DecodeLaunch& a, const KVSource& src, const DecodePlan& plan,
                           cudaStream_t stream);
 // Same launch with the split-K scratch taken from the library's static device
