@@ -71,6 +71,9 @@ def parse():
     ap.add_argument("--engine4-prompt", type=int, nargs=2, default=[32, 4096])
     ap.add_argument("--engine4-reply", type=int, default=128)
     ap.add_argument("--engine4-pool-gb", type=float, default=120.0)
+    ap.add_argument("--engine-mixed", type=int, default=32, metavar="MIN_TOKENS",
+                    help="also serve config 2 with chat.MIXED_PREFILL_MIN_TOKENS=MIN_TOKENS "
+                         "(graph-replayed mixed prefill + decode steps); 0 = skip")
     ap.add_argument("--engine4-mixed", type=int, default=1024, metavar="MIN_TOKENS",
                     help="also serve config 4 with chat.MIXED_PREFILL_MIN_TOKENS=MIN_TOKENS "
                          "(prompts of at least MIN_TOKENS share the tick's decode forward, "
@@ -1431,18 +1434,25 @@ def main():
                     "tokens_per_s": round(args.seqs * world / (f_ms * 1e-3), 1), "n_gpus": world})
     prefill = None if args.no_prefill else prefill_run(args, dev, seed=args.seed)
     engine = engine4 = engine4_mixed = None
+    engine_mixed = None
     if not args.no_engine:
-        # config 2 on every GPU (weak scaling: 16 chats per GPU)
-        engine = engine_run(dev, label="config2", chats_total=args.engine_chats,
-                            prompt_range=args.engine_prompt, reply=args.engine_reply,
-                            blocks=args.engine_blocks, max_batch=max(args.engine_chats, 1),
-                            seed=args.seed + rank)
-        wall_max, tok_rate = replica_rate(engine["tokens"], engine["wall_s"] * 1e3, dev, world)
-        engine["tok_s_all_gpus"] = round(tok_rate, 1)
-        engine["wall_s_max_over_gpus"] = round(wall_max / 1e3, 4)
-        engine["n_gpus"] = world
-        engine["scaling"] = "weak (each GPU serves its own chats)"
-        engine["per_rank"] = gather_ranks(rank_summary(rank, engine), world)
+        # config 2 on every GPU (weak scaling: 16 chats per GPU), with the
+        # reference's schedule and (--engine-mixed) with mixed ticks
+        c2 = {}
+        for mixed_min in [None] + ([args.engine_mixed] if args.engine_mixed > 0 else []):
+            r = engine_run(dev, label="config2", chats_total=args.engine_chats,
+                           prompt_range=args.engine_prompt, reply=args.engine_reply,
+                           blocks=args.engine_blocks, max_batch=max(args.engine_chats, 1),
+                           seed=args.seed + rank, mixed_min=mixed_min)
+            wall_max, tok_rate = replica_rate(r["tokens"], r["wall_s"] * 1e3, dev, world)
+            r["tok_s_all_gpus"] = round(tok_rate, 1)
+            r["wall_s_max_over_gpus"] = round(wall_max / 1e3, 4)
+            r["n_gpus"] = world
+            r["scaling"] = "weak (each GPU serves its own chats)"
+            r["per_rank"] = gather_ranks(rank_summary(rank, r), world)
+            c2[mixed_min] = r
+        engine = c2[None]
+        engine_mixed = c2.get(args.engine_mixed) if args.engine_mixed > 0 else None
     if not args.no_engine4:
         # config 4: 1024 chats split round-robin over the GPUs (strong scaling)
         block_bytes = L * 2 * 16 * HKV * D * 2
@@ -1521,7 +1531,8 @@ def main():
                 "kv_bytes_per_step": step_bytes, "prefill": prefill, "engine": engine, "engine_config4": engine4,
                 **({"engine_config3": engine3} if engine3 is not None else {}),
                 **({"fp8_decode": fp8} if fp8 is not None else {}),
-                **({"engine_config4_mixed": engine4_mixed} if engine4_mixed is not None else {})}
+                **({"engine_config4_mixed": engine4_mixed} if engine4_mixed is not None else {}),
+                **({"engine_mixed": engine_mixed} if engine_mixed is not None else {})}
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
