@@ -41,11 +41,13 @@ __global__ void __launch_bounds__(32 * kNormRowsPerCta)
   const int row = blockIdx.x * kNormRowsPerCta + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
-  uint4 av[kChunks], rv[kChunks];
+  uint4 av[kChunks], rv[kChunks], wv[kChunks];
 #pragma unroll
   for (int c = 0; c < kChunks; ++c) {
     av[c] = *reinterpret_cast<const uint4*>(a + row * a_stride + (c * 32 + lane) * 8);
     if (resid) rv[c] = *reinterpret_cast<const uint4*>(resid + row * r_stride + (c * 32 + lane) * 8);
+    // the norm weight with the row: its load overlaps the sum of squares
+    wv[c] = __ldg(reinterpret_cast<const uint4*>(weight + (c * 32 + lane) * 8));
   }
   float h[kChunks][8];
   float ss = 0.f;
@@ -75,8 +77,7 @@ __global__ void __launch_bounds__(32 * kNormRowsPerCta)
 #pragma unroll
   for (int c = 0; c < kChunks; ++c) {
     const int col = (c * 32 + lane) * 8;
-    const uint4 wv = *reinterpret_cast<const uint4*>(weight + col);
-    const __nv_bfloat16* wp = reinterpret_cast<const __nv_bfloat16*>(&wv);
+    const __nv_bfloat16* wp = reinterpret_cast<const __nv_bfloat16*>(&wv[c]);
     uint4 ov;
     __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(&ov);
 #pragma unroll
