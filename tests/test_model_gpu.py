@@ -109,7 +109,8 @@ def _agreement(ref_logits, flat_ids, margin):
 
 
 @pytest.mark.parametrize("path", ["reference_ops", "fused_cublas", "fused_skinny", "graphs",
-                                  "mixed", "mixed_graphs", "persistent", "fp8_pool"])
+                                  "mixed", "mixed_graphs", "persistent", "fp8_pool",
+                                  "fp8_graphs", "fp8_mixed_graphs"])
 def test_greedy_ids_match_oracle_and_reference(cuda, models, path):
     """fused_*: merged q/k/v and gate/up GEMMs + fused add/RMSNorm/SwiGLU
     kernels (the engine's path), with the projections on cuBLAS or on the
@@ -123,7 +124,10 @@ def test_greedy_ids_match_oracle_and_reference(cuda, models, path):
     (64-token prompt, 16-row decode) bucket, 15 padded rows inactive.
     persistent: the decode steps as one persistent launch over all layers
     (pkv_decode_layers).  fp8_pool: the engine on an FP8 (e4m3) cache,
-    against oracles whose caches apply the same e4m3 round trip."""
+    against oracles whose caches apply the same e4m3 round trip;
+    fp8_graphs: the same with the prefill and decode steps replayed from
+    CUDA graphs (padded buckets, as `graphs`); fp8_mixed_graphs: with the
+    mixed step replayed as in `mixed_graphs`."""
     import copy
 
     from kv_cache import KVCache
@@ -134,24 +138,24 @@ def test_greedy_ids_match_oracle_and_reference(cuda, models, path):
         ours.skinny_linears = path != "fused_cublas"
         ours.persistent_decode = path == "persistent"
     prompts, steps = fx["prompts"], fx["steps"]
-    fp8 = path == "fp8_pool"
+    fp8 = path in ("fp8_pool", "fp8_graphs", "fp8_mixed_graphs")
     c1 = KVCache(64, 16, cuda, torch.bfloat16, kv_format="fp8_e4m3" if fp8 else "bf16")
     s1 = [c1.alloc(), c1.alloc()]
-    if path == "mixed_graphs":  # the mixed step replayed from a (64, 16) bucket graph
+    if path in ("mixed_graphs", "fp8_mixed_graphs"):  # the mixed step from a (64, 16) bucket graph
         mg = ours.enable_mixed_graphs(c1, max_len=256, max_batch=16)
-    if path == "graphs":
+    if path in ("graphs", "fp8_graphs"):
         dg = ours.enable_decode_graphs(c1, max_batch=8)
         dg.buckets = [4, 8]  # the 2-row step runs in a 4-row graph: 2 padded, inactive rows
         pg = ours.enable_prefill_graphs(c1, max_len=256)
         assert all(len(p) < pg.buckets[0] for p in prompts)  # both prompts right-padded
     got, got_logits = _greedy(ours, c1, s1, prompts, steps, cuda,
-                              mixed=path in ("mixed", "mixed_graphs"))
+                              mixed=path in ("mixed", "mixed_graphs", "fp8_mixed_graphs"))
     torch.cuda.synchronize()
     c1.check_errors()
-    if path == "mixed_graphs":
+    if path in ("mixed_graphs", "fp8_mixed_graphs"):
         assert set(mg.graphs) == {(64, 16)}, "mixed graph not replayed"
         ours._mixed_graphs.clear()
-    if path == "graphs":
+    if path in ("graphs", "fp8_graphs"):
         assert set(dg.graphs) == {4} and set(pg.graphs) == {pg.buckets[0]}, "graphs not replayed"
         ours._graphs.clear()
         ours._prefill_graphs.clear()
