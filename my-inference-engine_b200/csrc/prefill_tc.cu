@@ -9,12 +9,13 @@
 //
 //   grid  = (Hq, B, ceil(T/128)): one CTA per 128 query rows of one head,
 //           heaviest (last) q-tiles first
-//   block = 6 warps
-//     warp 0    TMA producer (one thread): Q tile once, then 128-key K and V
-//               tiles (eight 16-token blocks each, through the block table)
-//               into separate 2-deep rings, K one tile ahead of V: a K stage
-//               is refilled as soon as its Q.K^T retired, so the next K tile
-//               loads during the current softmax; block ids read one tile ahead
+//   block = 7 warps
+//     warp 0    TMA producer (one thread): Q tile once, then 128-key K tiles
+//               (eight 16-token blocks each, through the block table) into a
+//               2-deep ring, one tile ahead: a K stage is refilled as soon as
+//               its Q.K^T retired, so the next K tile loads during the current
+//               softmax; block ids read one tile ahead
+//     warp 6    TMA producer of the V tiles (their own 2-deep ring)
 //     warp 1    owns TMEM (512 columns: S0, S1, O) and issues tcgen05.mma:
 //               S[b] = Q.K^T (M=128, N=128, K=128 in 8 steps), then
 //               O += P.V (K = 16 keys per step, only the loaded blocks)
@@ -44,7 +45,10 @@ constexpr int kTileBlocks = kKeys / kBlockTokens;  // 8
 constexpr int kRegion = kRows * 128;               // 16 KiB: 128 rows x 64 bf16
 constexpr int kOperand = 2 * kRegion;              // 32 KiB: dims (or keys) 0-63 | 64-127
 constexpr int kStages = 2;
-constexpr int kThreads = 192;
+// warp 6 issues the V tiles while warp 0 issues Q and the K tiles: a tile's
+// 32 TMA boxes otherwise take one thread most of a tile period to issue
+constexpr bool kSplitProducer = true;
+constexpr int kThreads = kSplitProducer ? 224 : 192;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -290,8 +294,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             fetch(j + 1, idk);
             if (!issue(j + 1, idk, false)) break;
           }
-          if (!issue(j, idv, true)) break;
+          if (!kSplitProducer && !issue(j, idv, true)) break;
         }
+      }
+    }
+  } else if (kSplitProducer && warp == 6) {
+    // ------------------------------------------------------------ V producer
+    if (lane == 0) {
+      for (int j = 0; j < ntiles; ++j) {
+        fetch(j, idv);
+        if (!issue(j, idv, true)) break;
       }
     }
   } else if (warp == 1) {
