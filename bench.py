@@ -92,7 +92,7 @@ def parse():
     ap.add_argument("--linear-sweep", type=str, default=None, metavar="ROWS",
                     help="comma-separated row counts: per-projection GEMM + fused-op times, "
                          "skinny tensor-core GEMMs vs cuBLAS, CUDA-graph replay")
-    ap.add_argument("--decode-step", type=str, default=None, metavar="B:CTX",
+    ap.add_argument("--decode-step", type=str, default=None, metavar="B:CTX[:PITCH]",
                     help="whole-model decode step time (CUDA graph) at B rows of CTX tokens, "
                          "skinny-GEMM policy vs cuBLAS")
     ap.add_argument("--prefill-step", type=int, default=None, metavar="T",
@@ -1172,11 +1172,14 @@ def decode_step_diag(spec, device, profile_range=False, persistent_profile=False
     import model as M
     from kv_cache import KVCache
 
-    B, ctx = (int(v) for v in spec.split(":"))
+    parts = [int(v) for v in spec.split(":")]
+    B, ctx = parts[0], parts[1]
+    pitch = parts[2] if len(parts) > 2 else None  # table pitch in blocks (None: the default)
     m = M.Qwen2ForCausalLM().to(device, torch.bfloat16).eval()
     random_init_(m, 11)
     m.fuse_weights_()
-    cache = KVCache(B * (ctx // 16 + 8) + 16, 16, device, torch.bfloat16, max_seqs=max(B, 16))
+    cache = KVCache(B * (ctx // 16 + 8) + 16, 16, device, torch.bfloat16, max_seqs=max(B, 16),
+                    max_blocks_per_seq=pitch)
     seqs = [cache.alloc() for _ in range(B)]
     for s_ in seqs:  # a history of ctx tokens per row (pool contents irrelevant to timing)
         cache.ensure_capacity(s_, ctx)
@@ -1212,7 +1215,7 @@ def decode_step_diag(spec, device, profile_range=False, persistent_profile=False
             m(ids, cache, seqs)
             torch.cuda.synchronize()
             torch.cuda.profiler.stop()
-    print(json.dumps({"diag": "decode_step", "rows": B, "ctx": ctx,
+    print(json.dumps({"diag": "decode_step", "rows": B, "ctx": ctx, "table_pitch": cache.table_pitch,
                       "graph_ms_skinny_policy": res["skinny"], "graph_ms_cublas": res["cublas"],
                       **({"graph_ms_persistent": res["persistent"]} if "persistent" in res else {}),
                       "skinny_rows": M.Qwen2ForCausalLM.skinny_rows}), flush=True)
