@@ -498,15 +498,30 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------- head pairs
 // Two query heads of one KV group per CTA (GQA groups of even size): the K/V
 // tiles are loaded once for both, halving the L2 -> SM traffic per head-tile
-// that sets the tile period of the one-head kernel.  10 warps: warp 0 TMA,
-// warp 1 MMA, warps 2-5 softmax of head A, warps 6-9 softmax of head B (each
-// warpgroup covers the four TMEM lane quarters).  TMEM: S_A, S_B, O_A, O_B.
+// that sets the tile period of the one-head kernel.  Warp 0 TMA, warp 1 MMA,
+// warps 4-7 softmax of head A, warps 8-11 softmax of head B (each warpgroup
+// covers the four TMEM lane quarters).  TMEM: S_A, S_B, O_A, O_B.
 // One shared P buffer is filled in a fixed order (P_A(j), then P_B(j) once
 // P.V_A(j) retired, then P_A(j+1) once P.V_B(j) retired), so shared memory
 // holds both Q tiles, two K and two V stages and P (224 KiB); Q.K^T of the
 // next tile is issued before the current tile's two P.V products, so the
 // exponentials of tile j+1 overlap the P.V chain of tile j.
-constexpr int kPairThreads = 320;
+// 12 warps in three warpgroups, registers split with setmaxnreg: warpgroup
+// 0 (warp 0 TMA, warp 1 MMA, warps 2-3 idle) drops to kPairRegsLow, the
+// softmax warpgroups (warps 4-7 head A, 8-11 head B) rise to kPairRegsHigh.
+// Launched at kPairRegsLaunch per thread: 384 x 168 = 64512 >= 128 x 80 +
+// 256 x 208 = 63488 (the producer and MMA code spills below 80); the host
+// launches the kernel only when
+// the compiled kernel has exactly kPairRegsLaunch registers, so the split
+// always fits what the block was given.  (10 warps without the split put
+// three warps on one SM sub-partition, capping every thread at ~170
+// registers, where the softmax spilled.)
+constexpr int kPairThreads = 384;
+constexpr int kPairRegsLaunch = 168;
+constexpr int kPairRegsLow = 80;
+constexpr int kPairRegsHigh = 208;
+static_assert(128 * kPairRegsLow + 256 * kPairRegsHigh <= kPairThreads * kPairRegsLaunch,
+              "register split exceeds the launch allocation");
 constexpr uint32_t kPColSA = 0, kPColSB = 128, kPColOA = 256, kPColOB = 384;
 constexpr int kPOffQ = 0;                          // Q_A, Q_B: 2 x 32 KiB
 constexpr int kPOffK = kPOffQ + 2 * kOperand;      // K stage s at +s*32 KiB
@@ -664,6 +679,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t sP = smem_u32(smem + kPOffP);
 
+  // Each role's code sits inside the branch that set its register limit, so
+  // the compiler allocates that role's registers under that limit.
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPairRegsLow));
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -730,9 +749,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       umma_commit(mma_done);
       mbar_wait(mma_done, 0, err);  // every MMA retired before TMEM is freed
     }
+  }  // warps 2-3: register donors only
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kPairRegsHigh));
     // ------------------------------------------------------------ softmax
-    const int h = warp >= 6 ? 1 : 0;  // warps 2-5: head A, 6-9: head B
+    const int h = warp >= 8 ? 1 : 0;  // warps 4-7: head A, 8-11: head B
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // query row within the tile == TMEM lane
     const int qi = q0 + r;
@@ -890,6 +911,21 @@ cudaError_t launch_tc_t(const TcParams& prm, const CUtensorMap& qmap, const KVSo
                   stream, prm, qmap, src.kmap, src.vmap);
 }
 
+// The head-pair kernel's register split assumes the block was launched with
+// exactly kPairRegsLaunch registers per thread (setmaxnreg.inc draws on that
+// allocation); a build where the compiler chose another count must not run it.
+bool pair_kernel_usable() {
+  static int ok = -1;
+  if (ok < 0) {
+    cudaFuncAttributes a0{}, a1{};
+    ok = cudaFuncGetAttributes(&a0, prefill_tc_pair_kernel<false>) == cudaSuccess &&
+         cudaFuncGetAttributes(&a1, prefill_tc_pair_kernel<true>) == cudaSuccess &&
+         a0.numRegs == kPairRegsLaunch && a1.numRegs == kPairRegsLaunch;
+    if (!ok) cudaGetLastError();
+  }
+  return ok == 1;
+}
+
 template <TcKernel kKind>
 cudaError_t launch_tc_kind(const TcParams& prm, const CUtensorMap& qmap, const KVSource& src,
                            dim3 grid, cudaStream_t stream) {
@@ -939,6 +975,7 @@ cudaError_t launch_prefill_tc(const PrefillLaunch& a, const CUtensorMap& qmap, c
     if (!strcmp(force, "one")) kind = TcKernel::kOneHead;
     if (!strcmp(force, "pair") && prm.group % 2 == 0) kind = TcKernel::kHeadPair;
   }
+  if (kind == TcKernel::kHeadPair && !pair_kernel_usable()) kind = TcKernel::kOneHead;
   if (kind == TcKernel::kHeadPair)
     return launch_tc_kind<TcKernel::kHeadPair>(prm, qmap, src,
                                                dim3(a.num_q_heads / 2, a.batch, qtiles), stream);
