@@ -594,6 +594,7 @@ class _CountingModel:
 
     def __init__(self, model, cache):
         self.model, self.cache, self.calls = model, cache, []
+        self.last_mixed = None
 
     @property
     def _graphs(self):
@@ -623,6 +624,8 @@ class _CountingModel:
         out = self.model.forward_mixed(prefill_ids, prefill_seq, decode_ids, decode_seqs, cache)
         e1.record()
         self.calls.append(("mixed", T + B, kv, e0, e1, pairs))
+        self.last_mixed = {"T": T, "B": B, "prompt_start": s0,
+                           "max_decode_len": max(cache.length(s) for s in decode_seqs)}
         return out
 
 
@@ -725,7 +728,13 @@ def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_b
     one_round([chats_total], 4)  # warm-up: sampling, one graph of each kind
     cm.calls.clear()
     mine = [i for i in range(chats_total) if i % world == rank]
-    el, toks = one_round(mine, reply)
+    try:
+        el, toks = one_round(mine, reply)
+    except RuntimeError as e:
+        # name the failing step: the device error word and the last mixed step
+        bits = int(cache.err_flag.item())
+        raise RuntimeError(f"{label} run failed: {e}; device error bits {bits:#x}; "
+                           f"{len(cm.calls)} model calls; last mixed step {cm.last_mixed}") from e
     torch.cuda.synchronize()
     nparams = sum(p.numel() for p in m.parameters())
     cr = call_roofline(cm.calls, nparams)
@@ -958,6 +967,43 @@ def engine_cpu_sample(seconds_budget=60.0):
 
 
 # ---------------------------------------------------------------- ranks
+def reset_chat_scheduler():
+    """Drop chat.py's scheduler state after a run that raised mid-tick (its
+    jobs, deferred and resident chats, queued messages, cache), so the next
+    engine run starts clean."""
+    import chat
+
+    chat.active.clear()
+    chat._deferred.clear()
+    chat._mixed.clear()
+    for c in chat._resident:
+        c.seq = None
+    chat._resident.clear()
+    while not chat._job_queue.empty():
+        chat._job_queue.get_nowait()
+    chat._kv_cache = None
+    chat.MIXED_PREFILL_MIN_TOKENS = None
+
+
+def opt_in_run(fn, device, world):
+    """Run one opt-in engine leg (a mixed-step mode): returns (result, None),
+    or (None, error text) on every rank if it raised on any rank, so that a
+    failure there is reported in the JSON line instead of losing the line,
+    and every rank still takes the same collectives."""
+    err = None
+    try:
+        r = fn()
+    except RuntimeError as e:
+        r, err = None, f"{type(e).__name__}: {e}"[:600]
+        reset_chat_scheduler()
+        gc.collect()
+        torch.cuda.empty_cache()
+    if cross_rank(1.0 if err else 0.0, torch.distributed.ReduceOp.MAX if world > 1 else None,
+                  device, world) > 0:
+        return None, err or "failed on another rank"
+    return r, None
+
+
 def cross_rank(value, op, device, world):
     """all_reduce of one float over the ranks (MAX or SUM); identity at N=1."""
     if world == 1:
@@ -1443,10 +1489,18 @@ def main():
         # reference's schedule and (--engine-mixed) with mixed ticks
         c2 = {}
         for mixed_min in [None] + ([args.engine_mixed] if args.engine_mixed > 0 else []):
-            r = engine_run(dev, label="config2", chats_total=args.engine_chats,
-                           prompt_range=args.engine_prompt, reply=args.engine_reply,
-                           blocks=args.engine_blocks, max_batch=max(args.engine_chats, 1),
-                           seed=args.seed + rank, mixed_min=mixed_min)
+            def leg(mixed_min=mixed_min):
+                return engine_run(dev, label="config2", chats_total=args.engine_chats,
+                                  prompt_range=args.engine_prompt, reply=args.engine_reply,
+                                  blocks=args.engine_blocks, max_batch=max(args.engine_chats, 1),
+                                  seed=args.seed + rank, mixed_min=mixed_min)
+            if mixed_min is None:
+                r = leg()
+            else:
+                r, err = opt_in_run(leg, dev, world)
+                if err is not None:
+                    c2[mixed_min] = {"error": err, "mixed_min_tokens": mixed_min}
+                    continue
             wall_max, tok_rate = replica_rate(r["tokens"], r["wall_s"] * 1e3, dev, world)
             r["tok_s_all_gpus"] = round(tok_rate, 1)
             r["wall_s_max_over_gpus"] = round(wall_max / 1e3, 4)
@@ -1465,10 +1519,18 @@ def main():
         runs = {}
         mixed_on = args.engine4_mixed is not None and args.engine4_mixed > 0
         for mixed_min in [None] + ([args.engine4_mixed] if mixed_on else []):
-            r = engine_run(dev, label="config4", chats_total=args.engine4_chats,
-                           prompt_range=args.engine4_prompt, reply=args.engine4_reply,
-                           blocks=blocks, max_batch=256, rank=rank, world=world,
-                           seed=args.seed, mixed_min=mixed_min)
+            def leg(mixed_min=mixed_min):
+                return engine_run(dev, label="config4", chats_total=args.engine4_chats,
+                                  prompt_range=args.engine4_prompt, reply=args.engine4_reply,
+                                  blocks=blocks, max_batch=256, rank=rank, world=world,
+                                  seed=args.seed, mixed_min=mixed_min)
+            if mixed_min is None:
+                r = leg()
+            else:
+                r, err = opt_in_run(leg, dev, world)
+                if err is not None:
+                    runs[mixed_min] = {"error": err, "mixed_min_tokens": mixed_min}
+                    continue
             toks_all = cross_rank(r["tokens"], torch.distributed.ReduceOp.SUM if world > 1 else None,
                                   dev, world)
             wall_max = cross_rank(r["wall_s"], torch.distributed.ReduceOp.MAX if world > 1 else None,

@@ -33,7 +33,15 @@ def _rank(rank, world, port, q):
     ms_max, rate = bench.replica_rate(1e9, ms_local, dev, world)
     total = bench.cross_rank(rank + 1, torch.distributed.ReduceOp.SUM, dev, world)
     per = bench.gather_ranks({"rank": rank, "tok_s": 100.0 * (rank + 1)}, world)
-    q.put((rank, ms_max, rate, total, per))
+
+    def leg_fails_on_rank_1():
+        if rank == 1:
+            raise RuntimeError("planted")
+        return {"rank": rank}
+
+    failed = bench.opt_in_run(leg_fails_on_rank_1, dev, world)
+    ok = bench.opt_in_run(lambda: {"rank": rank}, dev, world)
+    q.put((rank, ms_max, rate, total, per, failed, ok))
     torch.distributed.destroy_process_group()
 
 
@@ -48,7 +56,11 @@ def test_replica_rate_two_gloo_ranks():
         p.join(120)
         assert p.exitcode == 0
     got = sorted(q.get(timeout=10) for _ in range(2))
-    for rank, ms_max, rate, total, per in got:
+    for rank, ms_max, rate, total, per, failed, ok in got:
+        # an opt-in leg that raised on one rank is reported as failed on both,
+        # after the same collectives; one that ran everywhere returns its result
+        assert failed == (None, "RuntimeError: planted" if rank == 1 else "failed on another rank")
+        assert ok == ({"rank": rank}, None)
         assert ms_max == pytest.approx(15.0)           # the slowest rank
         assert rate == pytest.approx(2e9 / 15e-3)      # both ranks' units / job time
         assert total == pytest.approx(3.0)
