@@ -34,6 +34,9 @@ constexpr int kDecodeWarps = 4;
 constexpr int kDecodeStages = 3;  // per warp
 constexpr int kStageBytes = 2 * kHeadBlockBytes;  // K + V, one head, one block
 constexpr int kMaxHeadsPerCta = 8;
+// Lazy softmax rescaling threshold (log2 units of the scaled scores): a
+// probability is at most 2^kLazyLog2 before its row sum divides it out.
+constexpr float kLazyLog2 = 8.f;
 // split-K completion counters: one int32 per (row, kv head, head sub-group)
 constexpr int64_t kDecodeMaxUnits = 1 << 16;
 constexpr size_t kDecodeCounterBytes = kDecodeMaxUnits * sizeof(int32_t);
@@ -294,23 +297,32 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? 4 : 2)
       mb0 = fmaxf(mb0, __shfl_xor_sync(0xffffffffu, mb0, off));
       mb1 = fmaxf(mb1, __shfl_xor_sync(0xffffffffu, mb1, off));
     }
-    const float mn0 = fmaxf(m0, mb0), mn1 = fmaxf(m1, mb1);
-    const float base0 = mn0 == -INFINITY ? 0.f : mn0;
-    const float base1 = mn1 == -INFINITY ? 0.f : mn1;
-    const float al0 = ex2(m0 - base0), al1 = ex2(m1 - base1);
+    // Lazy rescaling: the running base moves (and O and l are rescaled)
+    // only when some lane's block maximum exceeds its base by more than
+    // 2^kLazyLog2; otherwise probabilities are taken against the old base
+    // and stay <= 2^kLazyLog2.  The decision is warp-uniform.
+    if (__any_sync(0xffffffffu, mb0 > m0 + kLazyLog2 || mb1 > m1 + kLazyLog2)) {
+      const float mn0 = fmaxf(m0, mb0), mn1 = fmaxf(m1, mb1);
+      const float al0 = ex2(m0 - (mn0 == -INFINITY ? 0.f : mn0));
+      const float al1 = ex2(m1 - (mn1 == -INFINITY ? 0.f : mn1));
+      l0 *= al0;
+      l1 *= al1;
+      m0 = mn0;
+      m1 = mn1;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        o[mt][0] *= al0;
+        o[mt][1] *= al1;
+        o[mt][2] *= al0;
+        o[mt][3] *= al1;
+      }
+    }
+    const float base0 = m0 == -INFINITY ? 0.f : m0;
+    const float base1 = m1 == -INFINITY ? 0.f : m1;
     const float p0 = ex2(x0 - base0), p2 = ex2(x2 - base0);
     const float p1 = ex2(x1 - base1), p3 = ex2(x3 - base1);
-    l0 = l0 * al0 + p0 + p2;
-    l1 = l1 * al1 + p1 + p3;
-    m0 = mn0;
-    m1 = mn1;
-#pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-      o[mt][0] *= al0;
-      o[mt][1] *= al1;
-      o[mt][2] *= al0;
-      o[mt][3] *= al1;
-    }
+    l0 += p0 + p2;
+    l1 += p1 + p3;
     if constexpr (kFp8) {
       const uint32_t pb0 = movm_t(pack_f16(p0 * vs0, p1 * vs0));
       const uint32_t pb1 = movm_t(pack_f16(p2 * vs1, p3 * vs1));
