@@ -22,6 +22,7 @@
 // index so the result does not depend on which CTA finished last.
 #include <math.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "pkv_device.cuh"
@@ -37,6 +38,39 @@ constexpr int kMaxHeadsPerCta = 8;
 // Lazy softmax rescaling threshold (log2 units of the scaled scores): a
 // probability is at most 2^kLazyLog2 before its row sum divides it out.
 constexpr float kLazyLog2 = 8.f;
+// Partition plan.  Every (row, KV head) unit gets up to kMaxParts
+// partitions, enough for kTargetCtas CTAs in total (several waves of 2
+// resident CTAs per SM).  A partition holds at least kMinBlocksPerPart blocks
+// (8 per warp) when the launch has work for kBusyCtas CTAs of that size, so
+// per-CTA set-up and the split-K merge stay amortised; smaller launches (few
+// rows, short contexts: latency-bound) go down to 16 or 4 blocks.
+#ifndef PKV_DECODE_TARGET_CTAS
+#define PKV_DECODE_TARGET_CTAS (148 * 2 * 6)
+#endif
+#ifndef PKV_DECODE_MIN_BLOCKS_PER_PART
+#define PKV_DECODE_MIN_BLOCKS_PER_PART 32
+#endif
+constexpr int kTargetCtas = PKV_DECODE_TARGET_CTAS;
+constexpr int kMinBlocksPerPart = PKV_DECODE_MIN_BLOCKS_PER_PART;
+constexpr int kMaxParts = 16;
+constexpr int64_t kBusyCtas = 600;
+constexpr int kMinBlocksPerPartSmall = kDecodeWarps;
+constexpr int64_t kWaveCtas = 148 * 2;  // resident bf16 CTAs (the FP8 kernel fits twice as many)
+constexpr int64_t kFillUnits = 128;     // units that, one CTA each, occupy most of the 148 SMs
+
+// The per-partition minimum for `units` (row, KV head) units of `nblk`
+// blocks each.  The host plans the grid with it for the launch's longest row
+// (or a CUDA graph's capacity); the kernel applies it again to each row's
+// own length (through block thresholds the host derives for the launch), so
+// rows far shorter than planned -- a graph captured for the cache's capacity
+// replaying short histories -- are split as an eager launch of their real
+// length would split them.
+inline int min_blocks_per_part_for(int64_t units, int nblk) {
+  if (units * (nblk / kMinBlocksPerPart) >= kBusyCtas) return kMinBlocksPerPart;
+  if (units * (nblk / 16) >= kBusyCtas) return 16;
+  return kMinBlocksPerPartSmall;
+}
+
 // split-K completion counters: one int32 per (row, kv head, head sub-group)
 constexpr int64_t kDecodeMaxUnits = 1 << 16;
 constexpr size_t kDecodeCounterBytes = kDecodeMaxUnits * sizeof(int32_t);
@@ -55,6 +89,10 @@ struct DecodeParams {
   int32_t sub_groups;  // CTAs per KV head (group > 8)
   int32_t max_parts;   // grid.x: partitions available to every row
   int32_t min_blocks_per_part;
+  // min_blocks_per_part_for(units, nblk) of this launch's units as block
+  // thresholds (nblk >= busy32: 32, >= busy16: 16, else the small minimum),
+  // and the partitions per row of about one wave of resident CTAs
+  int32_t busy32, busy16, wave_parts;
   float scale_log2;
   float* part_o;
   float* part_lse;
@@ -130,10 +168,23 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? 4 : 2)
     return;
   }
   // Every row splits into up to gridDim.x equal partitions of at least
-  // min_blocks_per_part blocks (rounded to the warp count), sized from its own
-  // length: the grid is planned for the longest row (or a captured capacity),
-  // shorter rows use fewer partitions instead of tiny ones.
-  const int np = min(p.max_parts, max(1, nblk / p.min_blocks_per_part));
+  // min_bpp blocks (rounded to the warp count), sized from its own length:
+  // the grid is planned for the longest row (or a captured capacity), shorter
+  // rows use fewer partitions instead of tiny ones, and the minimum itself is
+  // the one a launch of rows of this length would take (never above the
+  // plan's).
+  // No partition holds fewer than kMinBlocksPerPartSmall blocks: a CTA past
+  // that many partitions of its row has no work and leaves at once (a grid
+  // planned for a graph's capacity has many such CTAs).
+  if (part * kMinBlocksPerPartSmall >= nblk) return;
+  const int row_min =
+      nblk >= p.busy32 ? kMinBlocksPerPart : (nblk >= p.busy16 ? 16 : kMinBlocksPerPartSmall);
+  const int min_bpp = min(p.min_blocks_per_part, row_min);
+  int np = min(p.max_parts, max(1, nblk / min_bpp));
+  // a latency-bound launch (rows like this one would not keep kBusyCtas CTAs
+  // busy) takes at most about one wave of CTAs: more partitions only add
+  // waves of set-up and merge
+  if (row_min < kMinBlocksPerPart) np = min(np, p.wave_parts);
   const int per = (nblk + np - 1) / np;
   const int bpp = max(kDecodeWarps, (per + kDecodeWarps - 1) / kDecodeWarps * kDecodeWarps);
   const int nparts = (nblk + bpp - 1) / bpp;
@@ -491,23 +542,6 @@ int64_t decode_max_units() { return kDecodeMaxUnits; }
 
 namespace {
 
-// Partition plan.  Every (row, KV head) unit gets up to kMaxParts
-// partitions, enough for kTargetCtas CTAs in total (several waves of 2
-// resident CTAs per SM).  A partition holds at least kMinBlocksPerPart blocks
-// (8 per warp) when the launch has work for kBusyCtas CTAs of that size, so
-// per-CTA set-up and the split-K merge stay amortised; smaller launches (few
-// rows, short contexts: latency-bound) go down to 16 or 4 blocks.
-#ifndef PKV_DECODE_TARGET_CTAS
-#define PKV_DECODE_TARGET_CTAS (148 * 2 * 6)
-#endif
-#ifndef PKV_DECODE_MIN_BLOCKS_PER_PART
-#define PKV_DECODE_MIN_BLOCKS_PER_PART 32
-#endif
-constexpr int kTargetCtas = PKV_DECODE_TARGET_CTAS;
-constexpr int kMinBlocksPerPart = PKV_DECODE_MIN_BLOCKS_PER_PART;
-constexpr int kMaxParts = 16;
-constexpr int64_t kBusyCtas = 600;
-constexpr int kMinBlocksPerPartSmall = kDecodeWarps;
 
 template <bool kPaged, bool kFp8 = false>
 cudaError_t launch_decode_t(const DecodeParams& prm, const KVSource& src, dim3 grid,
@@ -543,11 +577,7 @@ DecodePlan plan_decode(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
   const int64_t target = fp8 ? 2 * static_cast<int64_t>(kTargetCtas) : kTargetCtas;
   const int64_t want = (target + units1 - 1) / units1;
   const int64_t parts = want < kMaxParts ? want : kMaxParts;
-  int min_bpp = kMinBlocksPerPartSmall;
-  if (units * (nblk / kMinBlocksPerPart) >= kBusyCtas)
-    min_bpp = kMinBlocksPerPart;
-  else if (units * (nblk / 16) >= kBusyCtas)
-    min_bpp = 16;
+  const int min_bpp = min_blocks_per_part_for(units, nblk);
   int bpp = static_cast<int>((nblk + parts - 1) / parts);
   bpp = max(bpp, min_bpp);
   bpp = (bpp + kDecodeWarps - 1) / kDecodeWarps * kDecodeWarps;
@@ -582,6 +612,17 @@ cudaError_t launch_decode(const DecodeLaunch& a, const KVSource& src, const Deco
   prm.sub_groups = plan.sub_groups;
   prm.max_parts = plan.max_parts;
   prm.min_blocks_per_part = plan.min_blocks_per_part;
+  {
+    const int64_t units = static_cast<int64_t>(a.batch) * a.num_kv_heads * plan.sub_groups;
+    const int64_t need = (kBusyCtas + units - 1) / units;  // units * (nblk / m) >= kBusyCtas
+    prm.busy32 = static_cast<int32_t>(std::min<int64_t>(need * kMinBlocksPerPart, 1 << 30));
+    prm.busy16 = static_cast<int32_t>(std::min<int64_t>(need * 16, 1 << 30));
+    // when one partition per row already puts a CTA on most SMs, splitting
+    // further only doubles the CTAs per SM and adds a merge (64 rows x 512
+    // tokens: 12.8 us unsplit vs 15.0 us in two)
+    const int64_t wave = (a.kv8 ? 2 : 1) * (units >= kFillUnits ? kWaveCtas / 2 : kWaveCtas);
+    prm.wave_parts = static_cast<int32_t>(std::max<int64_t>(1, wave / units));
+  }
   prm.scale_log2 = a.sm_scale * 1.4426950408889634f;
   prm.err = a.err;
   prm.kv8 = a.kv8;
