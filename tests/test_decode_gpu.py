@@ -57,9 +57,11 @@ def test_config0_paged_decode_matches_reference(cuda, golden):
     assert max_err(out, want) < TOL
 
 
-def _paged_case(cuda, lens, seed, Hq=12, num_blocks=None, poison=True):
+def _paged_case(cuda, lens, seed, Hq=12, num_blocks=None, poison=True, plan_len=None):
     """Random paged decode case through the raw binding; unused pool slots are
-    poisoned with PAD_VALUE so a masking leak shows as a large error."""
+    poisoned with PAD_VALUE so a masking leak shows as a large error.
+    plan_len: the max_kv_len the launch is planned for (default: the rows'
+    real maximum)."""
     import pagedkv
 
     g = torch.Generator().manual_seed(seed)
@@ -81,8 +83,8 @@ def _paged_case(cuda, lens, seed, Hq=12, num_blocks=None, poison=True):
     cache.write(0, step, kn.to(cuda), vn.to(cuda))
     out = torch.empty(B, 12, 128, dtype=torch.bfloat16, device=cuda)
     pagedkv.paged_decode(q[:, :, 0].to(cuda), cache.buf[0, 0], cache.buf[0, 1], cache.block_tables,
-                         step.rows, step.kv_lens, step.max_kv_len, out, 1 / math.sqrt(128), 2,
-                         cache.err_flag)
+                         step.rows, step.kv_lens, plan_len or step.max_kv_len, out,
+                         1 / math.sqrt(128), 2, cache.err_flag)
     torch.cuda.synchronize()
     cache.check_errors()
     kd = [torch.cat([a, b[i:i + 1]], 2) for i, (a, b) in enumerate(zip(hk, [kn] * B))]
@@ -103,6 +105,22 @@ def _paged_case(cuda, lens, seed, Hq=12, num_blocks=None, poison=True):
 def test_paged_decode_random_vs_oracle(cuda, lens):
     err, _ = _paged_case(cuda, lens, seed=sum(lens))
     assert err < TOL
+
+
+@pytest.mark.parametrize("B,lo,hi", [(8, 300, 520), (16, 480, 1000), (64, 400, 520),
+                                     (130, 60, 130), (40, 1500, 2100)])
+def test_capacity_planned_decode_vs_oracle(cuda, B, lo, hi):
+    """A grid planned for a 16k-token capacity (as a captured decode graph
+    plans it) over rows far shorter: each row takes the partition minimum of
+    its own length and a latency-bound launch about one wave of CTAs.  The
+    output matches the oracle and, up to rounding, the launch planned for
+    the rows' real maximum."""
+    g = torch.Generator().manual_seed(B * 1000 + hi)
+    lens = torch.randint(lo, hi + 1, (B,), generator=g).tolist()
+    err_cap, out_cap = _paged_case(cuda, lens, seed=B + hi, plan_len=16384)
+    err, out = _paged_case(cuda, lens, seed=B + hi)
+    assert err_cap < TOL and err < TOL, (err_cap, err)
+    assert max_err(out_cap, out.float()) < TOL
 
 
 def test_paged_decode_is_deterministic(cuda):

@@ -104,9 +104,13 @@ def test_fp8_append_bytes_bit_exact(cuda, hist, T):
     assert bad.size == 0, f"{len(bad)} FP8 pool bytes differ, first at {bad[:4].tolist()}"
 
 
-def _decode_case(cuda, lens, seed):
+def _decode_case(cuda, lens, seed, plan_len=None):
     """FP8 and bf16 caches with the same history (random, written through
-    the appends), then one decode step: appended token + attention."""
+    the appends), then one decode step: appended token + attention.
+    plan_len: the max_kv_len the launches are planned for (default: the
+    rows' real maximum; a captured graph plans for the cache's capacity)."""
+    import dataclasses
+
     from kernels.fa2 import flash_attention
 
     g = torch.Generator().manual_seed(seed)
@@ -125,6 +129,8 @@ def _decode_case(cuda, lens, seed):
     q16, q8, _, _, (st16, st8) = _append_both(cuda, (c16, c8), (s16, s8), 1, g)
     outs = []
     for c, st, q in ((c16, st16, q16), (c8, st8, q8)):
+        if plan_len:
+            st = dataclasses.replace(st, max_kv_len=plan_len)
         kh, vh = c.read(0, st)
         o = torch.full_like(q, float("nan"))
         flash_attention(q, kh, vh, False, st.kv_lens, out=o)
@@ -138,7 +144,21 @@ def _decode_case(cuda, lens, seed):
 @pytest.mark.parametrize("lens", [[1], [15, 16, 17], [1000, 37, 512, 1], [4096, 100],
                                   [8192, 8191, 3]])
 def test_fp8_decode_vs_oracle(cuda, lens):
-    c16, c8, s16, s8, q, (o16, o8) = _decode_case(cuda, lens, seed=sum(lens) + 1)
+    _check_fp8_decode(lens, _decode_case(cuda, lens, seed=sum(lens) + 1))
+
+
+@pytest.mark.parametrize("B,lo,hi", [(16, 480, 1000), (70, 60, 130)])
+def test_fp8_capacity_planned_decode_vs_oracle(cuda, B, lo, hi):
+    """FP8 decode planned for a 16k-token capacity over short rows (the
+    per-row partition minimum and the one-wave cap, at the FP8 kernel's
+    four CTAs per SM)."""
+    g = torch.Generator().manual_seed(B * 1000 + hi)
+    lens = torch.randint(lo, hi + 1, (B,), generator=g).tolist()
+    _check_fp8_decode(lens, _decode_case(cuda, lens, seed=B + hi, plan_len=16384))
+
+
+def _check_fp8_decode(lens, case):
+    c16, c8, s16, s8, q, (o16, o8) = case
     pool = c8.pool8[0].cpu().numpy()
     worst_acc = 0.0
     for b, n in enumerate(lens):
