@@ -234,7 +234,10 @@ int pkv_append_rope_fp8(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
  * kv8_pool/num_blocks in place of the two bf16 planes).  Each block is one
  * bulk copy per KV head; K and V are widened to f16 in registers (exactly),
  * the products are f16 tensor-core MMAs accumulating in fp32, and the
- * per-token scales are applied to the scores and the probabilities.
+ * per-token scales are applied to the scores and the probabilities.  A
+ * probability (at most 2^8 before the row sum divides it out) times its
+ * token's V scale (amax / 448) is an f16 operand, so V rows must stay below
+ * about 1.1e5 in magnitude.
  * Replaces KVCache.read + fa2_forward at T = 1 (kv_cache.py:117-121,
  * kernels/fa2.py:23-162) for a cache in FP8 mode.
  */
