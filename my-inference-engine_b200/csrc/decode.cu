@@ -342,17 +342,19 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kFp8 ? 4 : 2)
     if (tok0 >= kv_len) x0 = x1 = -INFINITY;
     if (tok0 + 8 >= kv_len) x2 = x3 = -INFINITY;
 
-    float mb0 = fmaxf(x0, x2), mb1 = fmaxf(x1, x3);
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-      mb0 = fmaxf(mb0, __shfl_xor_sync(0xffffffffu, mb0, off));
-      mb1 = fmaxf(mb1, __shfl_xor_sync(0xffffffffu, mb1, off));
-    }
     // Lazy rescaling: the running base moves (and O and l are rescaled)
-    // only when some lane's block maximum exceeds its base by more than
+    // only when some score of the block exceeds its head's base by more than
     // 2^kLazyLog2; otherwise probabilities are taken against the old base
-    // and stay <= 2^kLazyLog2.  The decision is warp-uniform.
+    // and stay <= 2^kLazyLog2.  Each lane tests its own scores and one vote
+    // makes the decision warp-uniform, so the block maximum (three shuffle
+    // rounds across the token lanes) is only reduced when the base moves.
+    float mb0 = fmaxf(x0, x2), mb1 = fmaxf(x1, x3);
     if (__any_sync(0xffffffffu, mb0 > m0 + kLazyLog2 || mb1 > m1 + kLazyLog2)) {
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        mb0 = fmaxf(mb0, __shfl_xor_sync(0xffffffffu, mb0, off));
+        mb1 = fmaxf(mb1, __shfl_xor_sync(0xffffffffu, mb1, off));
+      }
       const float mn0 = fmaxf(m0, mb0), mn1 = fmaxf(m1, mb1);
       const float al0 = ex2(m0 - (mn0 == -INFINITY ? 0.f : mn0));
       const float al1 = ex2(m1 - (mn1 == -INFINITY ? 0.f : mn1));
