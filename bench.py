@@ -78,6 +78,9 @@ def parse():
                     help="also serve config 4 with chat.MIXED_PREFILL_MIN_TOKENS=MIN_TOKENS "
                          "(prompts of at least MIN_TOKENS share the tick's decode forward, "
                          "replayed from CUDA graphs); 0 = skip")
+    ap.add_argument("--engine4-chunk", type=int, default=0, metavar="TOKENS",
+                    help="also serve config 4 with mixed steps (--engine4-mixed threshold) and "
+                         "chat.MIXED_PREFILL_CHUNK=TOKENS (chunked prefill); 0 = skip")
     ap.add_argument("--no-fp8", action="store_true", help="skip the FP8-pool decode line")
     ap.add_argument("--no-engine3", action="store_true")
     ap.add_argument("--engine3-chats", type=int, default=256)
@@ -664,7 +667,7 @@ def call_roofline(calls, nparams):
 
 
 def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_batch,
-               rank=0, world=1, seed=0, mixed_min=None, mixed_graphs=True):
+               rank=0, world=1, seed=0, mixed_min=None, mixed_graphs=True, mixed_chunk=None):
     """Serve `chats_total` chats through chat.py (uniform random token-id prompts
     in `prompt_range`, `reply`-token replies with EOS and stop sequences off as
     metrics/benchmark_concurrency.py:122,143 does, temperature-1 sampling, one
@@ -672,7 +675,8 @@ def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_b
     seeded prompt set, on its own model replica and `blocks`-block pool.
     mixed_min: chat.MIXED_PREFILL_MIN_TOKENS for this run (None: the
     reference's scheduling); its mixed steps replay captured graphs
-    (model.MixedGraphs) unless mixed_graphs is False.  Returns this rank's tokens, wall time and a
+    (model.MixedGraphs) unless mixed_graphs is False; mixed_chunk:
+    chat.MIXED_PREFILL_CHUNK (chunked prefill).  Returns this rank's tokens, wall time and a
     roofline."""
     import chat
     import model as M
@@ -687,6 +691,7 @@ def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_b
     chat.init(kv_cache=cache, start_worker=False)
     chat.STOP_SEQUENCES = []
     chat.MIXED_PREFILL_MIN_TOKENS = mixed_min
+    chat.MIXED_PREFILL_CHUNK = mixed_chunk
     lo, hi = prompt_range
     runner = m.enable_decode_graphs(cache, max_batch=max_batch)
     for b in runner.buckets:  # capture outside the timed region
@@ -697,7 +702,9 @@ def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_b
     mrunner = None
     if mixed_min is not None and mixed_graphs and mixed_min <= hi:
         mrunner = m.enable_mixed_graphs(cache, max_len=hi, max_batch=max_batch)
-        t0 = mrunner.buckets(max(mixed_min, 2), 1)[0]
+        # chunks of a prompt above mixed_chunk tokens are longer than half of it
+        shortest = min(mixed_min, mixed_chunk // 2 + 1) if mixed_chunk else mixed_min
+        t0 = mrunner.buckets(max(shortest, 2), 1)[0]
         for tp in mrunner.t_buckets:
             for bp in mrunner.b_buckets:
                 if tp >= t0:
@@ -742,6 +749,7 @@ def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_b
     gpu_decode, gpu_prefill, gpu_mixed = cr["decode_ms"], cr["prefill_ms"], cr["mixed_ms"]
     chat._kv_cache = None
     chat.MIXED_PREFILL_MIN_TOKENS = None
+    chat.MIXED_PREFILL_CHUNK = None
     m._graphs.clear()  # the graph runners and the model refer to each other
     m._prefill_graphs.clear()
     m._mixed_graphs.clear()
@@ -764,7 +772,9 @@ def engine_run(device, *, label, chats_total, prompt_range, reply, blocks, max_b
                       f"one prefill per tick (chat.py), CUDA-graph decode and prefill"
                       + (f"; prompts >= {mixed_min} tokens admitted while others decode share "
                          f"their forward ({mixed_kind} "
-                         f"mixed step)" if mixed_min is not None else "")}
+                         f"mixed step)" if mixed_min is not None else "")
+                      + (f", in chunks of at most {mixed_chunk} tokens, one per tick"
+                         if mixed_min is not None and mixed_chunk else "")}
 
 
 def engine3_run(args, device, seed=0):
@@ -1482,7 +1492,7 @@ def main():
         fp8.update({"value": round(f_rate / 1e9, 2), "ms_per_step": round(f_ms, 4),
                     "tokens_per_s": round(args.seqs * world / (f_ms * 1e-3), 1), "n_gpus": world})
     prefill = None if args.no_prefill else prefill_run(args, dev, seed=args.seed)
-    engine = engine4 = engine4_mixed = None
+    engine = engine4 = engine4_mixed = engine4_chunked = None
     engine_mixed = None
     if not args.no_engine:
         # config 2 on every GPU (weak scaling: 16 chats per GPU), with the
@@ -1518,19 +1528,25 @@ def main():
         blocks = int(min(need, args.engine4_pool_gb * 1e9 // block_bytes))
         runs = {}
         mixed_on = args.engine4_mixed is not None and args.engine4_mixed > 0
-        for mixed_min in [None] + ([args.engine4_mixed] if mixed_on else []):
-            def leg(mixed_min=mixed_min):
+        legs = [(None, None)] + ([(args.engine4_mixed, None)] if mixed_on else [])
+        if mixed_on and args.engine4_chunk > 0:
+            legs.append((args.engine4_mixed, args.engine4_chunk))
+        for mixed_min, chunk in legs:
+            def leg(mixed_min=mixed_min, chunk=chunk):
                 return engine_run(dev, label="config4", chats_total=args.engine4_chats,
                                   prompt_range=args.engine4_prompt, reply=args.engine4_reply,
                                   blocks=blocks, max_batch=256, rank=rank, world=world,
-                                  seed=args.seed, mixed_min=mixed_min)
+                                  seed=args.seed, mixed_min=mixed_min, mixed_chunk=chunk)
             if mixed_min is None:
                 r = leg()
             else:
                 r, err = opt_in_run(leg, dev, world)
                 if err is not None:
-                    runs[mixed_min] = {"error": err, "mixed_min_tokens": mixed_min}
+                    runs[(mixed_min, chunk)] = {"error": err, "mixed_min_tokens": mixed_min,
+                                                **({"chunk_tokens": chunk} if chunk else {})}
                     continue
+            if chunk:
+                r["chunk_tokens"] = chunk
             toks_all = cross_rank(r["tokens"], torch.distributed.ReduceOp.SUM if world > 1 else None,
                                   dev, world)
             wall_max = cross_rank(r["wall_s"], torch.distributed.ReduceOp.MAX if world > 1 else None,
@@ -1540,9 +1556,11 @@ def main():
                       "n_gpus": world,
                       "scaling": f"strong ({args.engine4_chats} chats split over the GPUs)",
                       "per_rank": gather_ranks(rank_summary(rank, r), world)})
-            runs[mixed_min] = r
-        engine4 = runs[None]
-        engine4_mixed = runs.get(args.engine4_mixed) if mixed_on else None
+            runs[(mixed_min, chunk)] = r
+        engine4 = runs[(None, None)]
+        engine4_mixed = runs.get((args.engine4_mixed, None)) if mixed_on else None
+        engine4_chunked = (runs.get((args.engine4_mixed, args.engine4_chunk))
+                           if mixed_on and args.engine4_chunk > 0 else None)
         if engine is not None and rank == 0 and world == 1 and not args.no_engine_cpu:
             torch.set_num_threads(os.cpu_count() or 1)
             engine["cpu_baseline"] = engine_cpu_sample()
@@ -1597,6 +1615,8 @@ def main():
                 **({"engine_config3": engine3} if engine3 is not None else {}),
                 **({"fp8_decode": fp8} if fp8 is not None else {}),
                 **({"engine_config4_mixed": engine4_mixed} if engine4_mixed is not None else {}),
+                **({"engine_config4_chunked": engine4_chunked}
+                   if engine4_chunked is not None else {}),
                 **({"engine_mixed": engine_mixed} if engine_mixed is not None else {})}
         print(json.dumps(line), flush=True)
     if world > 1:

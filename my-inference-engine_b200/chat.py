@@ -34,7 +34,12 @@ of at least that many tokens while other jobs are decoding runs the prompt
 and their decode rows as ONE forward (model.forward_mixed: one pass over the
 weights, one sampling sync).  The admitted job then takes its first decode
 step in the next tick instead of this one; every other decision (admission,
-eviction, deferral, trimming, FIFO order) is unchanged.
+eviction, deferral, trimming, FIFO order) is unchanged.  With
+MIXED_PREFILL_CHUNK also set, such a prompt longer than the chunk runs as
+ceil(len / chunk) near-equal chunks on consecutive ticks, each sharing that
+tick's decode forward (chunked prefill: every chunk attends to the ones
+before it through the cache); the job joins the decode batch after its
+last chunk, whose last-token logits give its first token.
 """
 from __future__ import annotations
 
@@ -59,6 +64,9 @@ MAX_SEQ_LEN = 2048
 
 # opt-in mixed prefill + decode ticks (see the module docstring); None = off
 MIXED_PREFILL_MIN_TOKENS = None
+# with mixed ticks on: a mixed prompt longer than this many tokens is split
+# into near-equal chunks, one per tick (chunked prefill); None = whole prompt
+MIXED_PREFILL_CHUNK = None
 
 DEVICE = torch.device("cuda")
 DTYPE = torch.bfloat16
@@ -337,6 +345,16 @@ def _ensure_worker():
             _worker_thread.start()
 
 
+def _chunk_len(n):
+    """Tokens of an n-token mixed prompt remainder to run this tick: all of
+    it, or with MIXED_PREFILL_CHUNK = c the first of ceil(n / c) near-equal
+    chunks (no short tail chunk)."""
+    c = MIXED_PREFILL_CHUNK
+    if not c or n <= c:
+        return n
+    return -(-n // -(-n // c))
+
+
 def _process(active):
     """One decode step for every job currently active, in FIFO order."""
     continuing = []
@@ -379,15 +397,19 @@ def _process(active):
     seqs = [job.chat.seq for job in continuing]
     if mixed is not None:
         new_job, prefill_ids = mixed
+        chunk = _chunk_len(len(prefill_ids))
         # host tensors: a mixed-step graph copies them with its other inputs
         with torch.no_grad():
             logits = model.forward_mixed(
-                _host_ids(prefill_ids), new_job.chat.seq,
+                _host_ids(prefill_ids[:chunk]), new_job.chat.seq,
                 torch.tensor([job.next_token for job in continuing]).view(-1, 1), seqs, _kv())
         tokens = _sample(logits)
-        new_job.next_token = tokens[0]
         for job, token_id in zip(continuing, tokens[1:]):
             job.next_token = token_id
+        if chunk < len(prefill_ids):  # more of the prompt next tick
+            _mixed.append((new_job, prefill_ids[chunk:]))
+            return
+        new_job.next_token = tokens[0]
         active.append(new_job)
         return
 

@@ -40,12 +40,15 @@ def models(cuda, golden):
     return ours, ref32, ref16, fx
 
 
-def _greedy(m, cache, seqs, prompts, steps, device, mixed=False):
+def _greedy(m, cache, seqs, prompts, steps, device, mixed=False, chunks=1):
     """Greedy ids and the logits that chose them, per row.  Default schedule:
     each prompt prefilled alone, then `steps` batched decode steps.  mixed:
     prompt 1 is prefilled in ONE forward with row 0's first decode step
     (model.forward_mixed, the mixed prefill + decode tick), then the batched
-    decode steps; row 0 therefore ends one token ahead."""
+    decode steps; row 0 therefore ends one token ahead.  chunks > 1: prompt 1
+    is split into that many near-equal chunks (chunked prefill), each in one
+    mixed forward with one of row 0's decode steps; its first token comes
+    from the last chunk."""
     ids = [[] for _ in prompts]
     logits = [[] for _ in prompts]
 
@@ -56,11 +59,15 @@ def _greedy(m, cache, seqs, prompts, steps, device, mixed=False):
     with torch.no_grad():
         if mixed:
             take(0, m(torch.tensor([prompts[0]], device=device), cache, [seqs[0]])[0, -1].float())
-            lg = m.forward_mixed(torch.tensor([prompts[1]], device=device), seqs[1],
-                                 torch.tensor([[ids[0][-1]]], device=device), [seqs[0]],
-                                 cache).float()
+            p1, pos = prompts[1], 0
+            for k in range(chunks):
+                n = -(-(len(p1) - pos) // (chunks - k))
+                lg = m.forward_mixed(torch.tensor([p1[pos:pos + n]], device=device), seqs[1],
+                                     torch.tensor([[ids[0][-1]]], device=device), [seqs[0]],
+                                     cache).float()
+                take(0, lg[1])
+                pos += n
             take(1, lg[0])
-            take(0, lg[1])
             n_dec = steps - 1
         else:
             for r, p in enumerate(prompts):
@@ -109,8 +116,8 @@ def _agreement(ref_logits, flat_ids, margin):
 
 
 @pytest.mark.parametrize("path", ["reference_ops", "fused_cublas", "fused_skinny", "graphs",
-                                  "mixed", "mixed_graphs", "persistent", "fp8_pool",
-                                  "fp8_graphs", "fp8_mixed_graphs"])
+                                  "mixed", "mixed_graphs", "chunked", "chunked_graphs",
+                                  "persistent", "fp8_pool", "fp8_graphs", "fp8_mixed_graphs"])
 def test_greedy_ids_match_oracle_and_reference(cuda, models, path):
     """fused_*: merged q/k/v and gate/up GEMMs + fused add/RMSNorm/SwiGLU
     kernels (the engine's path), with the projections on cuBLAS or on the
@@ -122,6 +129,9 @@ def test_greedy_ids_match_oracle_and_reference(cuda, models, path):
     inactive.  mixed: prompt 1 shares one forward with row 0's decode step
     (model.forward_mixed); mixed_graphs: that step replayed from a captured
     (64-token prompt, 16-row decode) bucket, 15 padded rows inactive.
+    chunked / chunked_graphs: the same with prompt 1 prefilled in three
+    chunks (chunked prefill: each chunk attends to the cache rows the
+    earlier chunks appended), eager / from the (64, 16) bucket graph.
     persistent: the decode steps as one persistent launch over all layers
     (pkv_decode_layers).  fp8_pool: the engine on an FP8 (e4m3) cache,
     against oracles whose caches apply the same e4m3 round trip;
@@ -141,7 +151,8 @@ def test_greedy_ids_match_oracle_and_reference(cuda, models, path):
     fp8 = path in ("fp8_pool", "fp8_graphs", "fp8_mixed_graphs")
     c1 = KVCache(64, 16, cuda, torch.bfloat16, kv_format="fp8_e4m3" if fp8 else "bf16")
     s1 = [c1.alloc(), c1.alloc()]
-    if path in ("mixed_graphs", "fp8_mixed_graphs"):  # the mixed step from a (64, 16) bucket graph
+    mixed_graphs = path in ("mixed_graphs", "chunked_graphs", "fp8_mixed_graphs")
+    if mixed_graphs:  # the mixed step from a (64, 16) bucket graph
         mg = ours.enable_mixed_graphs(c1, max_len=256, max_batch=16)
     if path in ("graphs", "fp8_graphs"):
         dg = ours.enable_decode_graphs(c1, max_batch=8)
@@ -149,10 +160,11 @@ def test_greedy_ids_match_oracle_and_reference(cuda, models, path):
         pg = ours.enable_prefill_graphs(c1, max_len=256)
         assert all(len(p) < pg.buckets[0] for p in prompts)  # both prompts right-padded
     got, got_logits = _greedy(ours, c1, s1, prompts, steps, cuda,
-                              mixed=path in ("mixed", "mixed_graphs", "fp8_mixed_graphs"))
+                              mixed=mixed_graphs or path in ("mixed", "chunked"),
+                              chunks=3 if path.startswith("chunked") else 1)
     torch.cuda.synchronize()
     c1.check_errors()
-    if path in ("mixed_graphs", "fp8_mixed_graphs"):
+    if mixed_graphs:
         assert set(mg.graphs) == {(64, 16)}, "mixed graph not replayed"
         ours._mixed_graphs.clear()
     if path in ("graphs", "fp8_graphs"):
