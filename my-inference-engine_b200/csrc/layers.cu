@@ -556,9 +556,10 @@ __device__ __noinline__ void w_epilogue(const LayersParams& __restrict__ p, int 
   if (ok) {
     tc_fence_after();
     const uint32_t ta = tmem + (static_cast<uint32_t>(q4 * 32) << 16) + static_cast<uint32_t>(buf * MPAD);
-    tmem_ld16(ta, *reinterpret_cast<float(*)[16]>(&v[0]));
-    if constexpr (MPAD == 32) tmem_ld16(ta + 16, *reinterpret_cast<float(*)[16]>(&v[16]));
-    tmem_wait_ld();
+    if constexpr (MPAD == 32)
+      tmem_ld16x2_sync(ta, *reinterpret_cast<float(*)[32]>(&v[0]));
+    else
+      tmem_ld16_sync(ta, *reinterpret_cast<float(*)[16]>(&v[0]));
   }
   tc_fence_before();
   __syncwarp();

@@ -236,8 +236,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
       float* red = reinterpret_cast<float*>(smem);
       for (int c = 0; c < p.mpad; c += 16) {
         float v[16];
-        tmem_ld16(taddr + c, v);
-        tmem_wait_ld();
+        tmem_ld16_sync(taddr + c, v);
 #pragma unroll
         for (int e = 0; e < 16; ++e) red[(c + e) * kTileN + nl] = v[e];
       }

@@ -367,14 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       float s[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(lane_addr + (sb ? kColS1 : kColS0) + c * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = v[i];
-      }
-      tmem_wait_ld();
+      tmem_ld32x4_sync(lane_addr + (sb ? kColS1 : kColS0), s);
 
       const int key0 = j * kKeys;
       // Row max of the raw scores (scale_log2 > 0 commutes with max), as 8
@@ -426,8 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           float v[32];
-          tmem_ld32(lane_addr + kColO + c * 32, v);
-          tmem_wait_ld();
+          tmem_ld32_sync(lane_addr + kColO + c * 32, v);
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] *= alpha;
           tmem_st32(lane_addr + kColO + c * 32, v);
@@ -459,9 +451,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const float inv = 1.f / l;  // 0/0 -> NaN for a row with no visible key
       float v[4][32];  // all of O's row, one wait
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + kColO + c * 32, v[c]);
-      tmem_wait_ld();
+      tmem_ld32x4_sync(lane_addr + kColO, *reinterpret_cast<float(*)[128]>(&v[0][0]));
       // direct row stores: staging through shared memory (store_o_rows, as
       // the head-pair kernel does) cost this kernel two registers and ~5%
       // of its main-loop speed on every measured shape
@@ -769,14 +759,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       }
       tc_fence_after();
       float s[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(lane_addr + colS + c * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = v[i];
-      }
-      tmem_wait_ld();
+      tmem_ld32x4_sync(lane_addr + colS, s);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[h]);
@@ -846,8 +829,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           float v[32];
-          tmem_ld32(lane_addr + colO + c * 32, v);
-          tmem_wait_ld();
+          tmem_ld32_sync(lane_addr + colO + c * 32, v);
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] *= alpha;
           tmem_st32(lane_addr + colO + c * 32, v);
@@ -867,9 +849,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       tc_fence_after();
       const float inv = 1.f / l;  // 0/0 -> NaN for a row with no visible key
       float v[4][32];  // all of O's row, one wait
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + colO + c * 32, v[c]);
-      tmem_wait_ld();
+      tmem_ld32x4_sync(lane_addr + colO, *reinterpret_cast<float(*)[128]>(&v[0][0]));
       // Q_h is free: pv_done[h] of the last tile retired every earlier MMA,
       // this head's Q.K^T products included
       const int w0 = q0 + quarter * 32;
