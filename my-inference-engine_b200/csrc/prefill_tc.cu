@@ -57,7 +57,7 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 constexpr int kOffQ = 0;
 constexpr int kOffKV = kOffQ + kOperand;  // stage s: K at +s*64K, V at +32K
 constexpr int kOffBar = kOffKV + kStages * 2 * kOperand;
-constexpr int kNumBars = 1 + 4 * kStages + 2 + 1 + 1 + 1;
+constexpr int kNumBars = 1 + 4 * kStages + 2 + 2 + 1 + 1;
 constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
 
 // instruction descriptors (kind::f16): fp32 accumulate, bf16 A/B, M=128, N=128
@@ -143,8 +143,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   // S[b] is rewritten by Q.K^T(j+2) only after P.V(j) (issue order), which
   // waited for P(j): that also means the softmax has read S(j)
   uint64_t* s_full = v_empty + kStages;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* pv_done = p_full + 1;
+  // P(j) ready (one arrival per softmax warp), per parity of j like S: a
+  // warp that skipped its P.V wait can be a whole tile ahead of the slowest
+  // warp, and with one barrier its arrival for tile j+1 would complete tile
+  // j's phase before the slow warp's P(j) was written.  Two barriers also
+  // keep the MMA issuer from missing a phase: tile j+2's arrivals need
+  // S(j+2), which is issued only after P.V(j+1), i.e. after the issuer saw
+  // tile j's phase.
+  uint64_t* p_full = s_full + 2;  // [tile & 1]
+  uint64_t* pv_done = p_full + 2;
   uint64_t* mma_done = pv_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
 
@@ -257,7 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_empty[s], 1);  // tcgen05.commit after the tile's P.V
     }
     for (int s = 0; s < 2; ++s) mbar_init(&s_full[s], 1);  // tcgen05.commit after Q.K^T
-    mbar_init(p_full, 4);
+    for (int s = 0; s < 2; ++s) mbar_init(&p_full[s], 4);
     mbar_init(pv_done, 1);
     mbar_init(mma_done, 1);
     fence_mbar_init();
@@ -311,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       bool dead = !mbar_wait(q_full, 0, err);
       auto issue_pv = [&](int i) -> bool {
-        if (!mbar_wait(p_full, i & 1, err)) return false;
+        if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1, err)) return false;
         const int st = i % kStages;
         if (!mbar_wait(&v_full[st], (i / kStages) & 1, err)) return false;
         tc_fence_after();
@@ -436,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[sb]);
     }
     // ------------------------------------------------------------ epilogue
     // tcgen05.ld is warp-collective: every lane loads, only rows < T store
