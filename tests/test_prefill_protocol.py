@@ -17,7 +17,10 @@ each softmax warp reads S(j) of its own tile and, when it rescales O,
 finds every P.V up to j-1 in it; each P.V reads P(i) written by all four
 warps and the V tile i; the epilogue finds all P.V products in O; no actor
 waits forever.  The softmax warps' lazy-rescale choice (wait for the last
-P.V only when some row's maximum moved) is random per warp and tile."""
+P.V only when some row's maximum moved) is random per warp and tile.
+
+The P-ready barrier is one per parity of the tile, as in the kernel
+(p_full[j & 1]); the last test shows why ONE barrier is not enough."""
 import random
 
 import pytest
@@ -67,6 +70,7 @@ def run(ntiles, seed, paired_p_full=True):
 
     def pf(j):  # (barrier, parity) that tile j's P arrivals complete
         return (f"p_full{j & 1}", (j >> 1) & 1) if paired_p_full else ("p_full0", j & 1)
+
     for s in range(STAGES):
         for n in ("k_full", "k_empty", "v_full", "v_empty"):
             B[f"{n}{s}"] = Barrier(1)
@@ -81,7 +85,6 @@ def run(ntiles, seed, paired_p_full=True):
     tmem = {"S0": [None] * 4, "S1": [None] * 4, "O": set()}
     tma = []    # pending loads: (region, tile, barrier)
     pipe = []   # issued tensor ops in order
-    log = []
 
     def load(region, tile, bar):
         B[bar].expect_tx(1)
