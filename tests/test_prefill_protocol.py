@@ -20,7 +20,8 @@ waits forever.  The softmax warps' lazy-rescale choice (wait for the last
 P.V only when some row's maximum moved) is random per warp and tile.
 
 The P-ready barrier is one per parity of the tile, as in the kernel
-(p_full[j & 1]); the last test shows why ONE barrier is not enough."""
+(p_full[j & 1]); a test shows why ONE barrier is not enough.  The
+head-pair kernel (prefill_tc_pair_kernel) is modelled the same way."""
 import random
 
 import pytest
@@ -236,3 +237,166 @@ def test_one_p_full_barrier_lets_a_fast_warp_complete_the_phase_early():
         except Race as e:
             caught.append(str(e))
     assert any("P.V(" in c and "read P lanes" in c for c in caught), caught[:3]
+
+
+def run_pair(ntiles, seed, cross_wait=True):
+    """The head-pair kernel (prefill_tc_pair_kernel): two heads over shared
+    K/V tiles, one S buffer per head (s_full / s_free), ONE shared-memory P
+    buffer filled in the order P_A(j), P_B(j), P_A(j+1) -- head A waits for
+    P.V_B(j-1), head B for P.V_A(j), before writing it -- O per head, and the
+    epilogue staging each head's output rows through that head's Q tile.
+    cross_wait=False drops head B's wait for P.V_A(j) (to show the model
+    notices when the shared P buffer is overwritten early)."""
+    rng = random.Random(seed)
+    B = {"q_full": Barrier(1), "mma_done": Barrier(1)}
+    for s in range(STAGES):
+        for n in ("k_full", "k_empty", "v_full", "v_empty"):
+            B[f"{n}{s}"] = Barrier(1)
+    for h in range(2):
+        B[f"s_full{h}"] = Barrier(1)
+        B[f"s_free{h}"] = Barrier(4)
+        B[f"p_full{h}"] = Barrier(4)
+        B[f"pv_done{h}"] = Barrier(1)
+    smem = {"Q0": None, "Q1": None, "P": [None] * 4}
+    for s in range(STAGES):
+        smem[f"K{s}"] = smem[f"V{s}"] = None
+    tmem = {"S0": [None] * 4, "S1": [None] * 4, "O0": set(), "O1": set()}
+    tma, pipe = [], []
+
+    def load(region, tile, bar):
+        B[bar].expect_tx(1)
+        tma.append((region, tile, bar))
+
+    def producer():
+        B["q_full"].expect_tx(2)  # one arrival expecting both Q tiles' bytes
+        tma.append(("Q0", 0, "q_full"))
+        tma.append(("Q1", 0, "q_full"))
+        load("K0", 0, "k_full0")
+        yield None
+        for j in range(ntiles):
+            if j + 1 < ntiles:
+                t, st = j + 1, (j + 1) % STAGES
+                if t >= STAGES:
+                    yield lambda st=st, t=t: B[f"k_empty{st}"].test(((t // STAGES) - 1) & 1)
+                load(f"K{st}", t, f"k_full{st}")
+            st = j % STAGES
+            if j >= STAGES:
+                yield lambda st=st, j=j: B[f"v_empty{st}"].test(((j // STAGES) - 1) & 1)
+            load(f"V{st}", j, f"v_full{st}")
+            yield None
+
+    def issue_qk(j):
+        st = j % STAGES
+        yield lambda: B[f"k_full{st}"].test((j // STAGES) & 1)
+        for h in range(2):
+            if j >= 1:
+                yield lambda h=h: B[f"s_free{h}"].test((j - 1) & 1)
+            pipe.append(("QK", h, j, st))
+            pipe.append(("commit", f"s_full{h}"))
+        pipe.append(("commit", f"k_empty{st}"))
+
+    def issue_pv(j, h):
+        yield lambda: B[f"p_full{h}"].test(j & 1)
+        st = j % STAGES
+        if h == 0:
+            yield lambda: B[f"v_full{st}"].test((j // STAGES) & 1)
+        pipe.append(("PV", h, j, st))
+        pipe.append(("commit", f"pv_done{h}"))
+        if h == 1:
+            pipe.append(("commit", f"v_empty{st}"))
+
+    def mma():
+        yield None
+        yield lambda: B["q_full"].test(0)
+        yield from issue_qk(0)
+        for j in range(ntiles):
+            if j + 1 < ntiles:
+                yield from issue_qk(j + 1)
+            yield from issue_pv(j, 0)
+            yield from issue_pv(j, 1)
+        pipe.append(("commit", "mma_done"))
+        yield lambda: B["mma_done"].test(0)
+
+    def softmax(h, w):
+        yield None
+        for j in range(ntiles):
+            yield lambda j=j: B[f"s_full{h}"].test(j & 1)
+            if tmem[f"S{h}"][w] != ("S", j):
+                raise Race(f"softmax {h}/{w} tile {j} read S lanes holding {tmem[f'S{h}'][w]}")
+            B[f"s_free{h}"].arrive()
+            yield None
+            if h == 0 and j >= 1:
+                yield lambda j=j: B["pv_done1"].test((j - 1) & 1)
+            elif h == 1 and cross_wait:
+                yield lambda j=j: B["pv_done0"].test(j & 1)
+            smem["P"][w] = (h, j)
+            if j >= 1 and rng.random() < 0.3 and set(range(j)) - tmem[f"O{h}"]:
+                raise Race(f"softmax {h}/{w} rescaled O before P.V {sorted(set(range(j)) - tmem[f'O{h}'])}")
+            B[f"p_full{h}"].arrive()
+            yield None
+        yield lambda: B[f"pv_done{h}"].test((ntiles - 1) & 1)
+        if tmem[f"O{h}"] != set(range(ntiles)):
+            raise Race(f"epilogue {h}/{w} read O with {sorted(tmem[f'O{h}'])}")
+        smem[f"Q{h}"] = "staging"  # the epilogue stages output rows in Q_h
+
+    actors = [producer(), mma()] + [softmax(h, w) for h in range(2) for w in range(4)]
+    waiting = [None] * len(actors)
+    done = [False] * len(actors)
+
+    def step_pipe():
+        op = pipe.pop(0)
+        if op[0] == "QK":
+            _, h, j, st = op
+            if smem[f"Q{h}"] != 0 or smem[f"K{st}"] != j:
+                raise Race(f"Q.K^T_{h}({j}) read Q={smem[f'Q{h}']} K{st}={smem[f'K{st}']}")
+            tmem[f"S{h}"] = [("S", j)] * 4
+        elif op[0] == "PV":
+            _, h, j, st = op
+            if smem["P"] != [(h, j)] * 4:
+                raise Race(f"P.V_{h}({j}) read P holding {smem['P']}")
+            if smem[f"V{st}"] != j:
+                raise Race(f"P.V_{h}({j}) read V{st}={smem[f'V{st}']}")
+            tmem[f"O{h}"].add(j)
+        else:
+            B[op[1]].arrive()
+
+    for _ in range(400000):
+        choices = [("actor", a) for a in range(len(actors))
+                   if not done[a] and (waiting[a] is None or waiting[a]())]
+        if pipe:
+            choices.append(("pipe", None))
+        if tma:
+            choices.append(("tma", None))
+        if not choices:
+            if all(done):
+                return
+            raise Race(f"deadlock: waiting actors {[a for a in range(len(actors)) if not done[a]]}")
+        kind, a = rng.choice(choices)
+        if kind == "pipe":
+            step_pipe()
+        elif kind == "tma":
+            region, tile, bar = tma.pop(rng.randrange(len(tma)))
+            smem[region] = tile
+            B[bar].complete_tx(1)
+        else:
+            try:
+                waiting[a] = next(actors[a])
+            except StopIteration:
+                done[a] = True
+    raise Race("no termination")
+
+
+@pytest.mark.parametrize("ntiles", [1, 2, 3, 5, 8])
+def test_pair_kernel_protocol_under_random_timing(ntiles):
+    for seed in range(300):
+        run_pair(ntiles, seed * 1000 + ntiles)
+
+
+def test_pair_model_notices_an_early_p_overwrite():
+    caught = []
+    for seed in range(200):
+        try:
+            run_pair(4, seed, cross_wait=False)
+        except Race as e:
+            caught.append(str(e))
+    assert any("read P holding" in c for c in caught), caught[:3]
