@@ -1,6 +1,7 @@
-"""Host-side pieces of the mixed-step graphs and the persistent decode-layers
-entry point (no GPU): bucket choice, argument checks before any device
-call, and the work split the kernel's plan relies on."""
+"""Host-side pieces of the mixed-step graphs, the persistent decode-layers
+entry point and the paged decode kernel's partitioning (no GPU): bucket
+choice, argument checks before any device call, and the work splits the
+kernels' plans rely on."""
 import ctypes
 
 import pytest
@@ -82,3 +83,85 @@ def test_decode_layers_work_split(sms):
             assert cs == list(range(cs[0], cs[-1] + 1))  # consecutive CTAs
             if ph == "gu" and T <= sms:
                 assert cs == [t]
+
+
+def _decode_rule(units, nblk):
+    """min_blocks_per_part_for (csrc/decode.cu): 32 when rows of nblk blocks
+    would keep 600 CTAs of 32 blocks busy, 16 likewise, else 4."""
+    if units * (nblk // 32) >= 600:
+        return 32
+    if units * (nblk // 16) >= 600:
+        return 16
+    return 4
+
+
+def _decode_host_plan(batch, hkv, max_kv_len, fp8):
+    """plan_decode + the per-launch thresholds of launch_decode (decode.cu)."""
+    units = batch * hkv
+    nblk = max(1, -(-max_kv_len // 16))
+    target = (2 if fp8 else 1) * 148 * 2 * 6
+    parts = min(-(-target // units), 16)
+    mb = _decode_rule(units, nblk)
+    bpp = max(-(-nblk // parts), mb)
+    bpp = -(-bpp // 4) * 4
+    max_parts = -(-nblk // bpp)
+    need = -(-600 // units)
+    wave = (2 if fp8 else 1) * (148 if units >= 128 else 296)
+    return {"units": units, "min_bpp": mb, "max_parts": max_parts, "busy32": need * 32,
+            "busy16": need * 16, "wave_parts": max(1, wave // units)}
+
+
+def _decode_row_parts(plan, kv_len):
+    """The kernel's partitioning of one row (paged_decode_kernel): returns the
+    (first block, block count) of every non-empty partition."""
+    nblk = -(-kv_len // 16)
+    row_min = 32 if nblk >= plan["busy32"] else 16 if nblk >= plan["busy16"] else 4
+    min_bpp = min(plan["min_bpp"], row_min)
+    np_ = min(plan["max_parts"], max(1, nblk // min_bpp))
+    if row_min < 32:
+        np_ = min(np_, plan["wave_parts"])
+    per = -(-nblk // np_)
+    bpp = max(4, -(-per // 4) * 4)
+    nparts = -(-nblk // bpp)
+    out = []
+    for part in range(plan["max_parts"]):
+        if part * 4 >= nblk or part >= nparts:  # the kernel's early exits
+            continue
+        b0 = part * bpp
+        out.append((b0, min(nblk, b0 + bpp) - b0))
+    return out
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_decode_partitions_cover_every_block_once(fp8):
+    """Per-row partition minimum and the one-wave cap (decode.cu): for plans
+    made for the rows' maximum or for a 16k-token graph capacity, every row's
+    partitions cover its blocks exactly once, never exceed the grid's
+    partitions, and a row below the busy threshold gets at most the
+    one-wave share of partitions (so a launch of such rows stays within
+    about one wave of resident CTAs)."""
+    import random
+
+    rng = random.Random(5)
+    for _ in range(400):
+        batch = rng.choice([1, 2, 8, 16, 32, 64, 128, 256])
+        lens = [rng.randint(1, 9000) for _ in range(batch)]
+        for plan_len in (max(lens), 16384):
+            plan = _decode_host_plan(batch, 2, plan_len, fp8)
+            for n in lens:
+                parts = _decode_row_parts(plan, n)
+                nblk = -(-n // 16)
+                covered = [b for b0, cnt in parts for b in range(b0, b0 + cnt)]
+                assert covered == list(range(nblk)), (batch, n, plan_len)
+                assert 1 <= len(parts) <= plan["max_parts"]
+                if nblk < plan["busy32"]:
+                    assert len(parts) <= plan["wave_parts"], (batch, n, plan_len)
+
+
+def test_decode_thresholds_restate_the_rule():
+    """The host's block thresholds give the rule's answer for every length."""
+    for units in (2, 16, 32, 64, 128, 256, 512, 1024):
+        plan = _decode_host_plan(units // 2, 2, 8192, False)
+        for nblk in range(0, 700):
+            row = 32 if nblk >= plan["busy32"] else 16 if nblk >= plan["busy16"] else 4
+            assert row == _decode_rule(units, nblk)
